@@ -1,0 +1,166 @@
+/*
+ * sa3b200.h - C ABI of the B200 (sm_100a) Stable Audio 3 DiT denoiser path.
+ *
+ * Every entry point takes plain device pointers owned by the caller, sizes
+ * and strides in ELEMENTS, and a CUDA stream (cudaStream_t passed as void*).
+ * None of them allocates device memory, synchronises the host, or keeps
+ * mutable state between calls except the device error word read by
+ * sa3_get_device_error(). All launches are asynchronous on `stream` and can
+ * be captured into CUDA graphs.
+ *
+ * Return value: SA3_OK (0) or a negative sa3_status. Argument errors are
+ * detected on the host before anything is launched.
+ *
+ * Layout convention ("token rows"): activations are row-major 2-D views
+ * [rows, features]; a row is one token, features hold all heads
+ * (head h occupies columns [h*head_dim, (h+1)*head_dim)). This is the layout
+ * nn.Linear produces, so projections feed attention without transposes.
+ */
+#ifndef SA3B200_H
+#define SA3B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SA3_OK = 0,
+  SA3_ERR_ARG = -1,         /* bad size / null pointer / inconsistent arguments */
+  SA3_ERR_ALIGN = -2,       /* pointer or stride violates the 16-byte rule */
+  SA3_ERR_DTYPE = -3,       /* dtype combination not supported */
+  SA3_ERR_LAUNCH = -4,      /* CUDA launch or driver call failed */
+  SA3_ERR_UNSUPPORTED = -5, /* shape outside what the kernels implement */
+} sa3_status;
+
+/* device error word codes (low byte) */
+#define SA3_DEVERR_TIMEOUT 1
+
+/* element types */
+#define SA3_DT_BF16 0
+#define SA3_DT_F16 1
+#define SA3_DT_E4M3 2
+#define SA3_DT_F32 3
+
+/* ------------------------------------------------------------------ misc */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int sa3_version(void);
+
+/* Reads and clears the device error word of the current device (0 = no
+ * kernel reported a timed-out wait). Synchronises the device. */
+int sa3_get_device_error(int* err);
+
+/* ------------------------------------------------------------- GEMM (a3, a4)
+ *
+ * C[M, N] = epilogue( (A[M, K] . B[N, K]^T) * a_scale * b_scale[n] + bias[n] )
+ *
+ * Replaces the nn.Linear calls of the DiT trunk:
+ *   Attention.to_qkv / to_q / to_kv / to_out  (stable_audio_3/models/transformer.py:547-560)
+ *   GLU.proj + SiLU gate                        (transformer.py:421-444)
+ *   FeedForward linear_out                      (transformer.py:485)
+ * with the adaLN gate + residual of TransformerBlock.forward
+ * (transformer.py:1027-1029, 1047-1049) fused into the epilogue.
+ *
+ * A and B are K-major (B is the nn.Linear weight [out, in]). ab_dtype is
+ * SA3_DT_BF16 (tcgen05 kind::f16) or SA3_DT_E4M3 (kind::f8f6f4).
+ * a_scale: device fp32 scalar or NULL (1). b_scale: device fp32 [N] or NULL.
+ * bias: device fp32 [N] or NULL. lda/ldb/ldc in elements; A, B rows must be
+ * 16-byte aligned (lda*elt and ldb*elt multiples of 16).
+ */
+#define SA3_EPI_STORE 0          /* C = acc (bf16) */
+#define SA3_EPI_SILU 1           /* C = silu(acc) */
+#define SA3_EPI_SWIGLU 2         /* B rows interleaved in blocks of 128 [x|gate]; C[:, N/2] = x*silu(gate) */
+#define SA3_EPI_GATED_RESIDUAL 3 /* C = residual + acc * sigmoid(1 - gate[batch(row), n]) */
+#define SA3_EPI_RESIDUAL 4       /* C = residual + acc */
+
+typedef struct {
+  int kind;                 /* SA3_EPI_* */
+  const float* bias;        /* [N] fp32 or NULL */
+  const void* residual;     /* bf16, row stride ld_residual; may alias C */
+  long long ld_residual;
+  const float* gate;        /* fp32 gate rows: batch b reads gate + b*ld_gate */
+  long long ld_gate;
+  int rows_per_batch;       /* batch(row) = row / rows_per_batch when row_batch is NULL */
+  const int* row_batch;     /* optional int32 [M]: batch index of each row */
+  float* amax_out;          /* optional: atomic max of |stored value| (non-negative, caller zeroes) */
+  int seg_in;               /* output row remap: if > 0, out_row = (m / seg_in) * seg_out + seg_offset + m % seg_in */
+  int seg_out;
+  int seg_offset;
+} sa3_epilogue;
+
+int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+             long long ldc, int ab_dtype, const float* a_scale, const float* b_scale, const sa3_epilogue* epi,
+             void* stream);
+
+/* ---------------------------------------------- glue: norms / modulation (a7, a9)
+ *
+ * y[r, :] = RMSNorm(x[r, :]) * gamma * (1 + scale[b, :]) + shift[b, :]
+ *   RMSNorm  : stable_audio_3/models/transformer.py:392-410 (F.rms_norm)
+ *   modulate : transformer.py:1020-1026, 1043-1045 (x * (1 + scale) + shift)
+ * b = batch(r) as in sa3_epilogue. `mod` is NULL for a plain RMSNorm
+ * (cross_attend_norm, transformer.py:1033); otherwise scale of batch b is
+ * mod + b*ld_mod + scale_off and shift is mod + b*ld_mod + shift_off (fp32).
+ * gamma: fp32 [D] or NULL.
+ * mode SA3_NORM_WRITE writes y as out_dtype (BF16 or E4M3; E4M3 divides by
+ *   s = max(*quant_amax, 1e-12) / 448 first and saturates, and, if scale_out
+ *   is non-NULL, stores s there for the consuming GEMM's a_scale).
+ * mode SA3_NORM_AMAX writes nothing and atomically maxes |y| into *amax_out.
+ * x is bf16 [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
+ */
+#define SA3_NORM_WRITE 0
+#define SA3_NORM_AMAX 1
+int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, long long ldx, long long ldo, const float* gamma,
+                         float eps, const float* mod, long long ld_mod, int scale_off, int shift_off,
+                         int rows_per_batch, const int* row_batch, int mode, int out_dtype,
+                         const float* quant_amax, float* scale_out, float* amax_out, void* stream);
+
+/* Per-tensor dynamic FP8 quantisation: out = e4m3(x / s), s = max(*amax,1e-12)/448,
+ * s also stored to *scale_out when non-NULL. If amax_out is non-NULL, the
+ * kernel only computes max|x| into it (no write). x is bf16. */
+int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, long long ldx, long long ldo,
+                      const float* amax, float* scale_out, float* amax_out, void* stream);
+
+/* ---------------------------------------------- glue: qk-norm + partial RoPE (a5, a6)
+ *
+ * In place on up to 4 head groups of a token-row buffer (e.g. q, k, q_diff,
+ * k_diff inside the fused to_qkv output). For every row r and head h of
+ * group g (columns col_off[g] + h*64 .. +63):
+ *   t = RMSNorm_64(t) * gamma_g            (Attention.apply_qk_layernorm, transformer.py:589-595, eps 1e-6)
+ *   if rope[g]: t[0:32] = t*cos + rotate_half(t)*sin at position pos(r)
+ *                         (apply_rotary_pos_emb / rotate_half, transformer.py:296-322; fp32)
+ * pos(r) = row_pos[r] if row_pos else r % rows_per_batch.
+ * cos_sin: fp32 table [max_pos, 32]: cols 0..15 cos(pos*inv_freq[i]),
+ *          cols 16..31 sin(pos*inv_freq[i])  (RotaryEmbedding, transformer.py:239-294).
+ * head_dim must be 64, rot_dim 32.
+ */
+int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, int ngroups, const int* col_off,
+                     const float* const* gamma, const int* rope, float eps, const float* cos_sin, int max_pos,
+                     int rows_per_batch, const int* row_pos, void* stream);
+
+/* ---------------------------------------------- attention (a1, a2, a11)
+ *
+ * out = softmax(q k^T * scale + band) v           (differential: minus the same with q2, k2)
+ * Replaces flash_attn_func / flash_attn_varlen_func(..., window_size=(wl, wr))
+ * as called from Attention.apply_attn (stable_audio_3/models/transformer.py:641-666),
+ * the differential combine out - out_diff (transformer.py:790-795) and the
+ * non-windowed cross-attention (transformer.py:1031-1035).
+ *
+ * Band (flash-attn convention, bottom-right aligned): key j of a sequence is
+ * visible to query i iff  i + (Lk - Lq) - wl <= j <= i + (Lk - Lq) + wr;
+ * a negative wl / wr means unbounded on that side.
+ * Sequences: if cu_seqlens_q is NULL, sequence b has rows [b*Lq, (b+1)*Lq)
+ * (same for k with Lk); otherwise rows [cu[b], cu[b+1]) (int32, device).
+ * q, k, v, q2, k2, out are token-row buffers with the given row strides;
+ * head h sits at columns h*64 of each. q2/k2 NULL = not differential.
+ * dtype: SA3_DT_BF16 (or SA3_DT_F16). head_dim must be 64.
+ */
+int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2, void* out,
+                  const int* cu_seqlens_q, const int* cu_seqlens_k, int batch, int max_seqlen_q, int max_seqlen_k,
+                  int total_q, int total_k, int heads, int head_dim, long long ldq, long long ldk, long long ldv,
+                  long long ldo, int window_left, int window_right, float softmax_scale, int dtype,
+                  float* amax_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SA3B200_H */

@@ -1,0 +1,350 @@
+// tcgen05 GEMM for the DiT linears: C = epilogue(A . B^T * a_scale * b_scale[n] + bias[n]).
+//
+// Replaces the nn.Linear projections of stable_audio_3/models/transformer.py
+// (Attention.to_qkv/to_q/to_kv/to_out :547-560, GLU.proj :432, FeedForward
+// linear_out :485, TransformerBlock.to_local_embed :944-957) with FP8 e4m3 or
+// bf16 operands, and fuses the adaLN gate + residual of TransformerBlock.forward
+// (:1027-1029, :1047-1049), the SwiGLU of GLU.forward (:443-444) and the
+// local-conditioning left-pad add (_left_pad_to_match :77-88) into the epilogue.
+//
+// Structure (one 128 x 256 output tile per CTA, 128 threads):
+//   warp 0 / lane 0 : TMA producer, STAGES-deep ring of (A 128x128B, B 256x128B)
+//                     tiles with the 128-byte swizzle, one mbarrier per stage.
+//   warp 1 / lane 0 : tcgen05.mma issuer (M=128, N=256, K=16 bf16 or K=32 fp8
+//                     per instruction), accumulator in 256 TMEM columns.
+//   all 4 warps     : epilogue; warp w owns TMEM lanes / tile rows 32w..32w+31.
+#include "common.cuh"
+#include "host_util.h"
+
+namespace sa3 {
+SA3_DEFINE_ERROR_READER(read_error_gemm)
+int read_error_glue(int* out);
+int read_error_attention(int* out);
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BN = 256;
+constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_A_BYTES = GEMM_BM * 128;
+constexpr int GEMM_B_BYTES = GEMM_BN * 128;
+constexpr int GEMM_STAGE_BYTES = GEMM_A_BYTES + GEMM_B_BYTES;
+constexpr int GEMM_SMEM = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int GEMM_TMEM_COLS = 256;
+
+struct GemmParams {
+  int M, N, K;
+  long long ldc;
+  void* C;
+  const float* a_scale;
+  const float* b_scale;
+  sa3_epilogue epi;
+};
+
+__device__ __forceinline__ int out_row_of(const sa3_epilogue& e, int m) {
+  return e.seg_in > 0 ? (m / e.seg_in) * e.seg_out + e.seg_offset + (m % e.seg_in) : m;
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = q[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[i * 8 + 2 * j] = f.x;
+      v[i * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&v)[32]) {
+  uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u;
+    u.x = pack_bf16x2(v[i * 8 + 0], v[i * 8 + 1]);
+    u.y = pack_bf16x2(v[i * 8 + 2], v[i * 8 + 3]);
+    u.z = pack_bf16x2(v[i * 8 + 4], v[i * 8 + 5]);
+    u.w = pack_bf16x2(v[i * 8 + 6], v[i * 8 + 7]);
+    q[i] = u;
+  }
+}
+
+// Scale + bias of one 32-column chunk starting at weight row n (bounds-checked).
+__device__ __forceinline__ void apply_scale_bias(float (&v)[32], int n, int N, float sa, const float* b_scale,
+                                                 const float* bias) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int c = n + i;
+    float s = sa;
+    float b = 0.f;
+    if (c < N) {
+      if (b_scale) s *= __ldg(b_scale + c);
+      if (bias) b = __ldg(bias + c);
+    }
+    v[i] = v[i] * s + b;
+  }
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(128, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
+  uint64_t* empty = full + GEMM_STAGES;
+  uint64_t* accf = empty + GEMM_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * GEMM_BN;
+  const int m0 = blockIdx.y * GEMM_BM;
+  constexpr int BK = FP8 ? 128 : 64;  // elements per 128-byte row
+  const int nkb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GEMM_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, GEMM_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    int issued = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % GEMM_STAGES;
+      if (kb >= GEMM_STAGES) {
+        if (!mbar_wait(&empty[s], ((kb / GEMM_STAGES) - 1) & 1, abort_flag, 1)) break;
+      }
+      uint8_t* st = smem + s * GEMM_STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], GEMM_STAGE_BYTES);
+      tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
+      tma_load_2d(st + GEMM_A_BYTES, &tmB, &full[s], kb * BK, n0);
+      issued = kb + 1;
+    }
+    if (*abort_flag) {
+      // Drain the loads still in flight before the CTA may exit.
+      for (int kb = (issued > GEMM_STAGES ? issued - GEMM_STAGES : 0); kb < issued; ++kb) {
+        volatile int never = 0;
+        mbar_wait(&full[kb % GEMM_STAGES], (kb / GEMM_STAGES) & 1, &never, 4);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = make_idesc(GEMM_BM, GEMM_BN, FP8 ? 0 : 1, FP8 ? 0 : 1, 0, 0);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % GEMM_STAGES;
+      if (!mbar_wait(&full[s], (kb / GEMM_STAGES) & 1, abort_flag, 2)) break;
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(smem + s * GEMM_STAGE_BYTES);
+      const uint64_t ad = sdesc_kmajor_sw128(a_addr);
+      const uint64_t bd = sdesc_kmajor_sw128(a_addr + GEMM_A_BYTES);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        // Each K step consumes 32 bytes of the 128-byte swizzled row: +2 in the
+        // (address >> 4) field of both descriptors.
+        if (FP8)
+          mma_f8_ss(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        else
+          mma_f16_ss(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+      }
+      tc_commit(&empty[s]);
+    }
+    tc_commit(accf);
+  }
+  __syncwarp();
+
+  // ---------------- epilogue
+  const bool ok = mbar_wait(accf, 0, abort_flag, 3);
+  tc_fence_after();
+  if (ok && !*abort_flag) {
+    const sa3_epilogue& e = p.epi;
+    const int m = m0 + warp * 32 + lane;
+    const bool row_ok = m < p.M;
+    const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
+    const int orow = out_row_of(e, m);
+    float amax = 0.f;
+    int batch = 0;
+    if (e.kind == SA3_EPI_GATED_RESIDUAL && row_ok)
+      batch = e.row_batch ? __ldg(e.row_batch + m) : (e.rows_per_batch > 0 ? m / e.rows_per_batch : 0);
+
+    if (e.kind == SA3_EPI_SWIGLU) {
+      // Tile columns [0,128) hold x rows, [128,256) the matching gate rows.
+      const int Nout = p.N / 2;
+      const int nout0 = n0 / 2;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32], g[32];
+        tmem_ld32(trow + c * 32, x);
+        tmem_ld32(trow + 128 + c * 32, g);
+        apply_scale_bias(x, n0 + c * 32, p.N, sa, p.b_scale, e.bias);
+        apply_scale_bias(g, n0 + 128 + c * 32, p.N, sa, p.b_scale, e.bias);
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) y[i] = x[i] * siluf_(g[i]);
+        const int nc = nout0 + c * 32;
+        if (row_ok && nc < Nout) {
+          __nv_bfloat16* dst = C + (long long)orow * p.ldc + nc;
+          if (nc + 32 <= Nout && (p.ldc & 7) == 0) {
+            store_bf16x32(dst, y);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < Nout) dst[i] = __float2bfloat16(y[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16(y[i]))));
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < GEMM_BN / 32; ++c) {
+        const int nc = n0 + c * 32;
+        if (nc >= p.N) break;  // uniform across the CTA
+        float v[32];
+        tmem_ld32(trow + c * 32, v);
+        apply_scale_bias(v, nc, p.N, sa, p.b_scale, e.bias);
+        const bool full_chunk = (nc + 32 <= p.N) && ((p.ldc & 7) == 0) && ((e.ld_residual & 7) == 0);
+        if (e.kind == SA3_EPI_SILU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = siluf_(v[i]);
+        } else if (e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL) {
+          if (row_ok) {
+            const __nv_bfloat16* res =
+                reinterpret_cast<const __nv_bfloat16*>(e.residual) + (long long)orow * e.ld_residual + nc;
+            float r[32];
+            if (full_chunk) {
+              load_bf16x32(res, r);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = (nc + i < p.N) ? __bfloat162float(res[i]) : 0.f;
+            }
+            if (e.kind == SA3_EPI_GATED_RESIDUAL) {
+              const float* gt = e.gate + (long long)batch * e.ld_gate + nc;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float gv = (nc + i < p.N) ? __ldg(gt + i) : 0.f;
+                v[i] = r[i] + v[i] * sigmoidf_(1.f - gv);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = r[i] + v[i];
+            }
+          }
+        }
+        if (row_ok) {
+          __nv_bfloat16* dst = C + (long long)orow * p.ldc + nc;
+          if (full_chunk) {
+            store_bf16x32(dst, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < p.N) dst[i] = __float2bfloat16(v[i]);
+          }
+          if (e.amax_out) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < p.N) amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16(v[i]))));
+          }
+        }
+      }
+    }
+    if (e.amax_out) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) atomic_max_nonneg(e.amax_out, amax);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, GEMM_TMEM_COLS);
+}
+
+}  // namespace sa3
+
+using namespace sa3;
+
+extern "C" int sa3_version(void) { return 100; }
+
+extern "C" int sa3_get_device_error(int* err) {
+  if (!err) return SA3_ERR_ARG;
+  if (cudaDeviceSynchronize() != cudaSuccess) return SA3_ERR_LAUNCH;
+  int a = 0, b = 0, c = 0, rc;
+  if ((rc = read_error_gemm(&a)) || (rc = read_error_glue(&b)) || (rc = read_error_attention(&c))) return rc;
+  *err = a ? a : (b ? b : c);
+  return SA3_OK;
+}
+
+extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
+                        long long ldc, int ab_dtype, const float* a_scale, const float* b_scale,
+                        const sa3_epilogue* epi, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return SA3_ERR_ARG;
+  if (ab_dtype != SA3_DT_BF16 && ab_dtype != SA3_DT_E4M3) return SA3_ERR_DTYPE;
+  const bool fp8 = ab_dtype == SA3_DT_E4M3;
+  const int esz = fp8 ? 1 : 2;
+  if (lda < K || ldb < K) return SA3_ERR_ARG;
+  if (!aligned16(A) || !aligned16(B) || ((lda * esz) % 16) || ((ldb * esz) % 16)) return SA3_ERR_ALIGN;
+  sa3_epilogue e{};
+  if (epi) e = *epi;
+  if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_RESIDUAL) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_SWIGLU) {
+    if (N % GEMM_BN != 0) return SA3_ERR_UNSUPPORTED;
+    if (ldc < N / 2) return SA3_ERR_ARG;
+  } else if (ldc < N) {
+    return SA3_ERR_ARG;
+  }
+  if ((e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL) && !e.residual) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_GATED_RESIDUAL && !e.gate) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_GATED_RESIDUAL && !e.row_batch && e.rows_per_batch <= 0) return SA3_ERR_ARG;
+  if (e.seg_in < 0 || (e.seg_in > 0 && e.seg_out <= 0)) return SA3_ERR_ARG;
+
+  CUtensorMap tmA, tmB;
+  const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t bk = fp8 ? 128 : 64;
+  int rc = make_tmap_2d(&tmA, A, dt, esz, (uint64_t)K, (uint64_t)M, (uint64_t)lda, bk, GEMM_BM);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tmB, B, dt, esz, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, bk, GEMM_BN);
+  if (rc) return rc;
+
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.C = C;
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.epi = e;
+
+  dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);
+  if (grid.y > 65535) return SA3_ERR_UNSUPPORTED;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (fp8) {
+    if ((rc = ensure_smem(gemm_tc_kernel<true>, GEMM_SMEM))) return rc;
+    gemm_tc_kernel<true><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
+  } else {
+    if ((rc = ensure_smem(gemm_tc_kernel<false>, GEMM_SMEM))) return rc;
+    gemm_tc_kernel<false><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
+  }
+  return launch_status();
+}

@@ -1,0 +1,372 @@
+// Fused elementwise glue of the DiT block (HBM-bound; 128-bit vector access).
+//
+//   rmsnorm_modulate : RMSNorm (stable_audio_3/models/transformer.py:392-410)
+//                      + adaLN modulate x*(1+scale)+shift (transformer.py:1018-1026,
+//                      1043-1045), optionally writing e4m3 with the per-tensor
+//                      dynamic activation scale, or only reducing max|y|.
+//   quantize_e4m3    : per-tensor dynamic FP8 quantisation of a bf16 tensor.
+//   qk_norm_rope     : per-head RMSNorm of q/k (Attention.apply_qk_layernorm,
+//                      transformer.py:589-595) + partial rotary embedding on the
+//                      first 32 of 64 dims, fp32 math (apply_rotary_pos_emb /
+//                      rotate_half, transformer.py:296-322; use at :755-781).
+#include "common.cuh"
+#include "host_util.h"
+
+namespace sa3 {
+SA3_DEFINE_ERROR_READER(read_error_glue)
+
+constexpr float kE4M3Max = 448.f;
+
+__device__ __forceinline__ float quant_scale(const float* amax) { return fmaxf(__ldg(amax), 1e-12f) / kE4M3Max; }
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  return u;
+}
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float inv_s_div, float s) {
+  // q = e4m3(v / s): division (not a reciprocal multiply) to match the oracle.
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) lo |= (uint32_t)f32_to_e4m3(v[j] / s) << (8 * j);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) hi |= (uint32_t)f32_to_e4m3(v[4 + j] / s) << (8 * j);
+  (void)inv_s_div;
+  return make_uint2(lo, hi);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-level max then one atomic per block.
+__device__ __forceinline__ void block_amax_commit(float v, float* amax_out) {
+  __shared__ float red[32];
+  v = warp_max(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+    w = warp_max(w);
+    if (lane == 0) atomic_max_nonneg(amax_out, w);
+  }
+}
+
+struct NormParams {
+  const __nv_bfloat16* x;
+  void* out;
+  int rows, D;
+  long long ldx, ldo;
+  const float* gamma;
+  float eps;
+  const float* mod;
+  long long ld_mod;
+  int scale_off, shift_off;
+  int rows_per_batch;
+  const int* row_batch;
+  int mode, out_dtype;
+  const float* quant_amax;
+  float* scale_out;
+  float* amax_out;
+};
+
+// One warp per row; each lane owns chunks of 8 columns at lane*8 + i*256.
+template <int MAXC>
+__global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunk = p.D / 8;
+  float s = 1.f;
+  if (p.mode == SA3_NORM_WRITE && p.out_dtype == SA3_DT_E4M3) {
+    s = quant_scale(p.quant_amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
+  }
+  float amax = 0.f;
+  for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < p.rows; row += gridDim.x * (blockDim.x >> 5)) {
+    const __nv_bfloat16* xr = p.x + (long long)row * p.ldx;
+    float v[MAXC][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) {
+        unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)p.D + p.eps);
+    const float* msc = nullptr;
+    const float* msh = nullptr;
+    if (p.mod) {
+      const int b = p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch;
+      msc = p.mod + (long long)b * p.ld_mod + p.scale_off;
+      msh = p.mod + (long long)b * p.ld_mod + p.shift_off;
+    }
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) {
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = c * 8 + j;
+          float t = v[i][j] * r;
+          if (p.gamma) t *= __ldg(p.gamma + col);
+          if (msc) t = t * (1.f + __ldg(msc + col)) + __ldg(msh + col);
+          y[j] = t;
+        }
+        if (p.mode == SA3_NORM_AMAX) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+        } else if (p.out_dtype == SA3_DT_E4M3) {
+          uint8_t* o = reinterpret_cast<uint8_t*>(p.out) + (long long)row * p.ldo + c * 8;
+          *reinterpret_cast<uint2*>(o) = pack8_e4m3(y, 0.f, s);
+        } else {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + c * 8;
+          *reinterpret_cast<uint4*>(o) = pack8(y);
+        }
+      }
+    }
+  }
+  if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
+}
+
+struct QuantParams {
+  const __nv_bfloat16* x;
+  uint8_t* out;
+  int rows, cols;
+  long long ldx, ldo;
+  const float* amax;
+  float* scale_out;
+  float* amax_out;
+};
+
+__global__ void __launch_bounds__(256) quantize_e4m3_kernel(QuantParams p) {
+  const int cpr = p.cols / 8;  // 8-element chunks per row
+  const long long total = (long long)p.rows * cpr;
+  float s = 1.f;
+  if (!p.amax_out) {
+    s = quant_scale(p.amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
+  }
+  float amax = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    float v[8];
+    unpack8(*reinterpret_cast<const uint4*>(p.x + r * p.ldx + c * 8), v);
+    if (p.amax_out) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    } else {
+      *reinterpret_cast<uint2*>(p.out + r * p.ldo + c * 8) = pack8_e4m3(v, 0.f, s);
+    }
+  }
+  if (p.amax_out) block_amax_commit(amax, p.amax_out);
+}
+
+struct QkParams {
+  __nv_bfloat16* buf;
+  int rows;
+  long long ld;
+  int heads, ngroups;
+  int col_off[4];
+  const float* gamma[4];
+  int rope[4];
+  float eps;
+  const float* cos_sin;
+  int max_pos;
+  int rows_per_batch;
+  const int* row_pos;
+};
+
+// Eight lanes per 64-wide head, 8 elements per lane; a warp handles 4 heads.
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & 7;
+  const int per_row = p.ngroups * p.heads;
+  const long long total = (long long)p.rows * per_row;
+  const long long warps_total = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long long base = gw * 4; base < total; base += warps_total * 4) {
+    const long long item = base + (lane >> 3);
+    const bool active = item < total;
+    const long long row = active ? item / per_row : 0;
+    const int gh = active ? (int)(item - row * per_row) : 0;
+    const int g = gh / p.heads;
+    const int h = gh - g * p.heads;
+    __nv_bfloat16* ptr = p.buf + row * p.ld + p.col_off[g] + h * 64 + sub * 8;
+    float v[8];
+    if (active) unpack8(*reinterpret_cast<const uint4*>(ptr), v);
+    else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    const float r = rsqrtf(ss * (1.f / 64.f) + p.eps);
+    const float* gm = p.gamma[g];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = v[j] * r * (gm ? __ldg(gm + sub * 8 + j) : 1.f);
+    // rotate_half pairs dim d with d +- 16: lanes sub and sub^2 within the first 32 dims.
+    float partner[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 2);
+    if (active && p.rope[g] && sub < 4) {
+      int pos = p.row_pos ? __ldg(p.row_pos + row) : (int)(row % p.rows_per_batch);
+      if (pos >= p.max_pos) {
+        record_error(2, 10);
+        pos = p.max_pos - 1;
+      }
+      const float* cs = p.cos_sin + (long long)pos * 32;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = sub * 8 + j;   // 0..31
+        const int f = d & 15;
+        const float c = __ldg(cs + f), sn = __ldg(cs + 16 + f);
+        const float rh = (d < 16) ? -partner[j] : partner[j];
+        v[j] = v[j] * c + rh * sn;
+      }
+    }
+    if (active) *reinterpret_cast<uint4*>(ptr) = pack8(v);
+  }
+}
+
+inline int grid_for(long long work_items, int per_block) {
+  long long g = (work_items + per_block - 1) / per_block;
+  const long long cap = 148LL * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+}  // namespace sa3
+
+using namespace sa3;
+
+extern "C" int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, long long ldx, long long ldo,
+                                    const float* gamma, float eps, const float* mod, long long ld_mod, int scale_off,
+                                    int shift_off, int rows_per_batch, const int* row_batch, int mode, int out_dtype,
+                                    const float* quant_amax, float* scale_out, float* amax_out, void* stream) {
+  if (!x || rows <= 0 || D <= 0 || (D % 8) || ldx < D) return SA3_ERR_ARG;
+  if (!aligned16(x) || (ldx % 8)) return SA3_ERR_ALIGN;
+  if (mode == SA3_NORM_AMAX) {
+    if (!amax_out) return SA3_ERR_ARG;
+  } else if (mode == SA3_NORM_WRITE) {
+    if (!out || ldo < D) return SA3_ERR_ARG;
+    if (out_dtype == SA3_DT_E4M3) {
+      if (!quant_amax) return SA3_ERR_ARG;
+      if ((reinterpret_cast<uintptr_t>(out) & 7) || (ldo % 8)) return SA3_ERR_ALIGN;
+    } else if (out_dtype == SA3_DT_BF16) {
+      if (!aligned16(out) || (ldo % 8)) return SA3_ERR_ALIGN;
+    } else {
+      return SA3_ERR_DTYPE;
+    }
+  } else {
+    return SA3_ERR_ARG;
+  }
+  if (mod && !row_batch && rows_per_batch <= 0) return SA3_ERR_ARG;
+  NormParams p;
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.out = out;
+  p.rows = rows;
+  p.D = D;
+  p.ldx = ldx;
+  p.ldo = ldo;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.mod = mod;
+  p.ld_mod = ld_mod;
+  p.scale_off = scale_off;
+  p.shift_off = shift_off;
+  p.rows_per_batch = rows_per_batch;
+  p.row_batch = row_batch;
+  p.mode = mode;
+  p.out_dtype = out_dtype;
+  p.quant_amax = quant_amax;
+  p.scale_out = scale_out;
+  p.amax_out = amax_out;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = grid_for(rows, 8);
+  const int nchunk = D / 8;
+  if (nchunk <= 32 * 4)
+    rmsnorm_modulate_kernel<4><<<grid, 256, 0, st>>>(p);
+  else if (nchunk <= 32 * 8)
+    rmsnorm_modulate_kernel<8><<<grid, 256, 0, st>>>(p);
+  else if (nchunk <= 32 * 16)
+    rmsnorm_modulate_kernel<16><<<grid, 256, 0, st>>>(p);
+  else
+    return SA3_ERR_UNSUPPORTED;
+  return launch_status();
+}
+
+extern "C" int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, long long ldx, long long ldo,
+                                 const float* amax, float* scale_out, float* amax_out, void* stream) {
+  if (!x || rows <= 0 || cols <= 0 || (cols % 8) || ldx < cols) return SA3_ERR_ARG;
+  if (!aligned16(x) || (ldx % 8)) return SA3_ERR_ALIGN;
+  if (!amax_out) {
+    if (!out || !amax || ldo < cols) return SA3_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(out) & 7) || (ldo % 8)) return SA3_ERR_ALIGN;
+  }
+  QuantParams p{reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<uint8_t*>(out), rows, cols, ldx, ldo,
+                amax, scale_out, amax_out};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  quantize_e4m3_kernel<<<grid_for((long long)rows * (cols / 8), 256), 256, 0, st>>>(p);
+  return launch_status();
+}
+
+extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, int ngroups, const int* col_off,
+                                const float* const* gamma, const int* rope, float eps, const float* cos_sin,
+                                int max_pos, int rows_per_batch, const int* row_pos, void* stream) {
+  if (!buf || rows <= 0 || heads <= 0 || ngroups < 1 || ngroups > 4 || !col_off) return SA3_ERR_ARG;
+  if (!aligned16(buf) || (ld % 8)) return SA3_ERR_ALIGN;
+  QkParams p{};
+  p.buf = reinterpret_cast<__nv_bfloat16*>(buf);
+  p.rows = rows;
+  p.ld = ld;
+  p.heads = heads;
+  p.ngroups = ngroups;
+  bool any_rope = false;
+  for (int g = 0; g < ngroups; ++g) {
+    if (col_off[g] < 0 || (col_off[g] % 8) || col_off[g] + heads * 64 > ld) return SA3_ERR_ARG;
+    p.col_off[g] = col_off[g];
+    p.gamma[g] = gamma ? gamma[g] : nullptr;
+    p.rope[g] = rope ? rope[g] : 0;
+    any_rope |= p.rope[g] != 0;
+  }
+  if (any_rope && (!cos_sin || max_pos <= 0 || (!row_pos && rows_per_batch <= 0))) return SA3_ERR_ARG;
+  p.eps = eps;
+  p.cos_sin = cos_sin;
+  p.max_pos = max_pos;
+  p.rows_per_batch = rows_per_batch;
+  p.row_pos = row_pos;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long items = (long long)rows * ngroups * heads;
+  qk_norm_rope_kernel<<<grid_for(items, 32), 256, 0, st>>>(p);
+  return launch_status();
+}

@@ -1,0 +1,64 @@
+// Host-side helpers shared by the C-ABI entry points: tensor-map encoding
+// through the driver entry point (no -lcuda link), argument checks and the
+// once-per-device shared-memory attribute setup.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/sa3b200.h"
+
+namespace sa3 {
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D tiled tensor map over a row-major [rows, cols] view with the 128-byte
+// swizzle. box_cols * elem_bytes must be <= 128. Out-of-range elements of a
+// box read as zero.
+inline int make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                        uint64_t rows, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
+                        CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  auto fn = encode_fn();
+  if (!fn) return SA3_ERR_LAUNCH;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return SA3_ERR_ALIGN;
+  if ((row_stride_elems * elem_bytes) % 16 != 0) return SA3_ERR_ALIGN;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SA3_OK : SA3_ERR_LAUNCH;
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SA3_OK : SA3_ERR_LAUNCH;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Raise the dynamic shared-memory limit of `func` (a host-side attribute of
+// the function on the current device; cheap and legal during stream capture).
+template <typename F>
+inline int ensure_smem(F func, int bytes) {
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return SA3_ERR_LAUNCH;
+  return SA3_OK;
+}
+
+}  // namespace sa3

@@ -1,0 +1,249 @@
+"""Kernel parity on a B200: each CUDA op through the C ABI vs the CPU oracle on seeded inputs.
+
+Tolerances (from the path's parity contract):
+  * bf16 attention: max|out - ref| / max|ref| <= 1e-2 vs the fp32 oracle.
+  * FP8 / bf16 GEMM: relative Frobenius error <= 2e-2 vs the oracle's quantized definition
+    (we assert the much tighter 5e-3 where only bf16 output rounding separates them).
+  * FP8 activation quantisation: bit-exact bytes vs the oracle's e4m3 rounding.
+  * glue (norm / modulation / RoPE): bf16 output rounding only, max-abs-rel <= 1e-2.
+"""
+import math
+
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle import ref as orf
+
+pytestmark = pytest.mark.gpu
+
+
+def _gen(seed):
+    g = torch.Generator().manual_seed(seed)
+    return g
+
+
+def rel_fro(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def max_rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+# ----------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 320), (1000, 640, 1024), (2, 1536, 1536)])
+def test_gemm_bf16(cuda, M, N, K):
+    from sa3_b200 import ops
+
+    g = _gen(M + N + K)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g)
+    ref = a.bfloat16().float() @ b.bfloat16().float().T + bias
+    out = ops.gemm(a.bfloat16().to(cuda), b.bfloat16().to(cuda), bias=bias.to(cuda))
+    torch.cuda.synchronize()
+    assert rel_fro(out, ref) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (777, 768, 1536), (130, 256, 6144)])
+def test_gemm_fp8_matches_quantized_definition(cuda, M, N, K):
+    from sa3_b200 import ops
+
+    g = _gen(7 * M + N)
+    x = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.02
+    wq, sw = oq.quantize_weight_e4m3(w)
+    xb = x.bfloat16()
+    ref = oq.fp8_linear(xb.float(), wq, sw)
+
+    xd = xb.to(cuda)
+    amax = torch.zeros(1, device=cuda)
+    ops.absmax(xd, amax)
+    s = torch.zeros(1, device=cuda)
+    xq = ops.quantize_e4m3(xd, amax, scale_out=s)
+    out = ops.gemm(xq, wq.to(cuda), a_scale=s, b_scale=sw.to(cuda))
+    torch.cuda.synchronize()
+    # activation quantisation is bit-exact with the oracle's definition
+    s_ref = oq.act_scale(xb.float())
+    assert torch.equal(s.cpu(), s_ref.reshape(1))
+    xq_ref = (xb.float() / s_ref).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(xq.cpu().view(torch.uint8), xq_ref.view(torch.uint8))
+    assert rel_fro(out, ref) < 5e-3
+
+
+def test_gemm_epilogues(cuda):
+    from sa3_b200 import ops, _lib
+
+    g = _gen(11)
+    B, T, D, K = 2, 200, 512, 256
+    M = B * T
+    a = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(D, K, generator=g) * 0.05).bfloat16()
+    res = torch.randn(M, D, generator=g).bfloat16()
+    gate = torch.randn(B, D, generator=g)
+    h = a.float() @ w.float().T
+    ad, wd = a.to(cuda), w.to(cuda)
+
+    # gated residual: res + h * sigmoid(1 - gate[b])
+    out = res.clone().to(cuda)
+    ops.gemm(ad, wd, out, kind=_lib.EPI_GATED_RESIDUAL, residual=out, gate=gate.to(cuda), rows_per_batch=T)
+    ref = orf.gate_residual(h.view(B, T, D), gate[:, None, :], res.float().view(B, T, D)).view(M, D)
+    assert max_rel(out, ref) < 1e-2
+
+    # plain residual and silu
+    out = ops.gemm(ad, wd, res.clone().to(cuda), kind=_lib.EPI_RESIDUAL, residual=res.to(cuda))
+    assert max_rel(out, h + res.float()) < 1e-2
+    out = ops.gemm(ad, wd, kind=_lib.EPI_SILU)
+    assert max_rel(out, orf.silu(h)) < 1e-2
+
+    # swiglu with the interleaved [x | gate] blocks of 128 rows
+    inner = 256
+    w1 = (torch.randn(2 * inner, K, generator=g) * 0.05).bfloat16()
+    b1 = torch.randn(2 * inner, generator=g)
+    from sa3_b200.quant import interleave_swiglu_rows
+    w1i, b1i = interleave_swiglu_rows(w1, b1)
+    amax = torch.zeros(1, device=cuda)
+    out = ops.gemm(ad, w1i.to(cuda), bias=b1i.to(cuda), kind=_lib.EPI_SWIGLU, amax_out=amax)
+    ref = orf.swiglu(a.float() @ w1.float().T + b1)
+    assert max_rel(out, ref) < 1e-2
+    torch.cuda.synchronize()
+    assert abs(amax.item() - out.float().abs().max().item()) == 0.0
+
+    # left-pad row remap (local conditioning add): x[b, 64 + t] += y[b, t]
+    Tin, Nout = 150, 214
+    xin = torch.randn(B * Tin, K, generator=g).bfloat16()
+    big = torch.randn(B * Nout, D, generator=g).bfloat16()
+    outd = big.clone().to(cuda)
+    ops.gemm(xin.to(cuda), wd, outd, kind=_lib.EPI_RESIDUAL, residual=outd, seg=(Tin, Nout, 64))
+    ref = big.float().clone().view(B, Nout, D)
+    ref[:, 64:, :] += (xin.float() @ w.float().T).view(B, Tin, D)
+    assert max_rel(outd, ref.view(-1, D)) < 1e-2
+
+
+# ----------------------------------------------------------------------------- glue
+def test_rmsnorm_modulate(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(3)
+    B, T, D = 2, 333, 1536
+    x = torch.randn(B * T, D, generator=g).bfloat16()
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    mod = torch.randn(B, 6 * D, generator=g) * 0.3
+    ref = orf.modulate(orf.rms_norm(x.float().view(B, T, D), gamma, 1e-5), mod[:, None, 0:D], mod[:, None, D:2 * D])
+    ref = ref.reshape(B * T, D)
+    out = ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5, mod=mod.to(cuda), scale_off=0, shift_off=D,
+                               rows_per_batch=T)
+    assert max_rel(out, ref) < 1e-2
+    amax = torch.zeros(1, device=cuda)
+    ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5, mod=mod.to(cuda), scale_off=0, shift_off=D,
+                         rows_per_batch=T, amax_only=amax)
+    torch.cuda.synchronize()
+    assert abs(amax.item() - ref.abs().max().item()) / ref.abs().max().item() < 1e-5
+    s = torch.zeros(1, device=cuda)
+    q = ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5, mod=mod.to(cuda), scale_off=0, shift_off=D,
+                             rows_per_batch=T, out_dtype=torch.float8_e4m3fn, quant_amax=amax, scale_out=s)
+    deq = q.float().cpu() * s.cpu()
+    assert rel_fro(deq, oq.fake_quant_act(ref)) < 2e-2
+    # plain RMSNorm (no modulation)
+    out = ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5)
+    assert max_rel(out, orf.rms_norm(x.float(), gamma, 1e-5)) < 1e-2
+
+
+def test_qk_norm_rope(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(5)
+    B, T, H = 2, 300, 4
+    D = H * 64
+    buf = torch.randn(B * T, 5 * D, generator=g).bfloat16()
+    gq = 1 + 0.1 * torch.randn(64, generator=g)
+    gk = 1 + 0.1 * torch.randn(64, generator=g)
+    table = ops.rope_table(T, device=cuda)
+    out = buf.clone().to(cuda)
+    ops.qk_norm_rope(out, H, [0, D, 3 * D, 4 * D], [gq.to(cuda), gk.to(cuda), gq.to(cuda), gk.to(cuda)],
+                     [True] * 4, 1e-6, table, rows_per_batch=T)
+    freqs = orf.rotary_freqs(T, 32)
+    x = buf.float().view(B, T, 5, H, 64)
+    ref = x.clone()
+    for part, gm in ((0, gq), (1, gk), (3, gq), (4, gk)):
+        t = x[:, :, part].permute(0, 2, 1, 3)  # [B, H, T, 64]
+        t = orf.apply_rotary(orf.rms_norm(t, gm, 1e-6), freqs)
+        ref[:, :, part] = t.permute(0, 2, 1, 3)
+    assert max_rel(out.view(B, T, 5, H, 64)[:, :, [0, 1, 3, 4]], ref[:, :, [0, 1, 3, 4]]) < 1e-2
+    # v untouched
+    assert torch.equal(out.view(B, T, 5, H, 64)[:, :, 2].cpu(), buf.view(B, T, 5, H, 64)[:, :, 2])
+
+
+# ----------------------------------------------------------------------------- attention
+def _heads(x, B, N, H):
+    return x.float().cpu().view(B, N, H, 64).permute(0, 2, 1, 3)
+
+
+@pytest.mark.parametrize("B,N,H,w", [(1, 646, 16, 256), (2, 300, 4, 17), (1, 130, 2, 0), (1, 1000, 2, -1)])
+def test_attention_window(cuda, B, N, H, w):
+    from sa3_b200 import ops
+
+    g = _gen(N + H)
+    D = H * 64
+    qkv = torch.randn(B * N, 3 * D, generator=g).bfloat16().to(cuda)
+    q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+    out = ops.attention(q, k, v, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w))
+    ref = orf.attention(_heads(q, B, N, H), _heads(k, B, N, H), _heads(v, B, N, H), w, w)
+    assert max_rel(_heads(out, B, N, H), ref) < 1e-2
+
+
+def test_attention_differential(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(9)
+    B, N, H, w = 2, 700, 3, 256
+    D = H * 64
+    qkv = torch.randn(B * N, 5 * D, generator=g).bfloat16().to(cuda)
+    q, k, v, q2, k2 = (qkv[:, i * D:(i + 1) * D] for i in range(5))
+    out = ops.attention(q, k, v, q2=q2, k2=k2, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w))
+    hh = lambda t: _heads(t, B, N, H)  # noqa: E731
+    ref = orf.differential_attention(hh(q), hh(k), hh(v), hh(q2), hh(k2), w, w)
+    assert max_rel(hh(out), ref) < 1e-2
+
+
+def test_attention_cross_full(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(13)
+    B, Nq, Nk, H = 2, 333, 128, 4
+    D = H * 64
+    q = torch.randn(B * Nq, D, generator=g).bfloat16().to(cuda)
+    kv = torch.randn(B * Nk, 2 * D, generator=g).bfloat16().to(cuda)
+    k, v = kv[:, :D], kv[:, D:]
+    out = ops.attention(q, k, v, heads=H, batch=B, max_seqlen_q=Nq, max_seqlen_k=Nk)
+    ref = orf.attention(_heads(q, B, Nq, H), _heads(k, B, Nk, H), _heads(v, B, Nk, H))
+    assert max_rel(_heads(out, B, Nq, H), ref) < 1e-2
+
+
+def test_attention_varlen(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(17)
+    lens = [100, 300, 77, 513]
+    H, w = 2, 64
+    D = H * 64
+    tot = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    qkv = torch.randn(tot, 3 * D, generator=g).bfloat16().to(cuda)
+    q, k, v = qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:]
+    out = ops.attention(q, k, v, heads=H, cu_seqlens_q=cu.to(cuda), cu_seqlens_k=cu.to(cuda),
+                        max_seqlen_q=max(lens), max_seqlen_k=max(lens), window=(w, w))
+    for i, L in enumerate(lens):
+        s, e = int(cu[i]), int(cu[i + 1])
+        hh = lambda t: _heads(t[s:e], 1, L, H)  # noqa: E731
+        ref = orf.attention(hh(q), hh(k), hh(v), w, w)
+        assert max_rel(hh(out), ref) < 1e-2, f"sequence {i}"
+
+
+def test_no_device_error_recorded(cuda):
+    from sa3_b200 import _lib
+
+    assert _lib.device_error() == 0
