@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Benchmark: Stable Audio 3 medium DiT denoiser step (FP8 linears) on B200.
+
+One step = one DiffusionTransformer.forward of the rf_denoiser with CFG
+(cond + uncond halves batched) at the medium shape: dim 1536, 24 blocks,
+24 heads x 64, differential attention, window (256, 256), L = 8183 latent
+tokens (+64 memory tokens), 128 context tokens, FP8 e4m3 linears with
+per-output-channel weight scales and per-tensor dynamic activation scales,
+random-init weights (no checkpoints offline), synthetic N(0,1) latents.
+
+Metric: latent tokens/s = (sum over sequences in the step, both CFG halves, of
+L) / step time; the per-step latency is reported as ms_per_step. Every
+rank of a torchrun launch runs its own prompt (data-parallel, weak scaling,
+no collective in the step); value = all ranks' tokens / max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "stable-audio-3_b200"))
+
+import torch  # noqa: E402
+
+WORKLOADS = {
+    # the headline configuration: medium DiT, FP8 linears, L = 8183, one prompt = one CFG pair per GPU
+    "medium_fp8": dict(model="medium", mode="fp8", L=8183, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
+    # small DiT in bf16 (24 blocks, dim 1024, L = 2584, CFG pair)
+    "small_bf16": dict(model="small", mode="bf16", L=2584, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
+}
+METRIC = "Medium DiT step latency (ms) + latent tokens/s at 1/2/4/8 B200, FP8/GPTQ"
+UNIT = "latent tokens/s"
+
+
+def _peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) != self.idx:
+                continue
+            rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def model_cfg(name):
+    from sa3_b200.modules import MEDIUM, SMALL
+    return {"medium": MEDIUM, "small": SMALL}[name]
+
+
+def make_inputs(wl, cfg, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    P, L = wl["prompts"], wl["L"]
+    x = torch.randn(P, cfg.io_channels, L, generator=g)
+    t = torch.full((P,), 0.5)
+    cond = torch.randn(P, wl["Tc"], cfg.cond_token_dim, generator=g)
+    gemb = torch.randn(P, cfg.global_cond_dim, generator=g)
+    loc = torch.zeros(P, cfg.local_add_cond_dim, L)
+    return [a.to(device) if device is not None else a for a in (x, t, cond, gemb, loc)]
+
+
+# ----------------------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_block_sample(wl, threads: int, tokens: int = 0):
+    """Time the oracle's fp32 restatement of one block (FP8 fake-quant linears for the FP8 workload)
+    over `tokens` tokens of one sequence (default: the full L + 64) on the host cores. Every op of a
+    block with a fixed window is linear in the token count, so the sample is scaled by
+    (L + 64) / tokens, x depth blocks, x 2 CFG halves. Returns (seconds per full step, seconds measured)."""
+    from oracle import dit as odit
+    from sa3_b200.modules import TransformerBlock, init_synthetic_
+    torch.set_num_threads(threads)
+    cfg = model_cfg(wl["model"])
+    oc = odit.Cfg(embed_dim=cfg.embed_dim, depth=1, num_heads=cfg.num_heads, differential=cfg.differential,
+                  sliding_window=cfg.sliding_window, local_add_cond_dim=0, cond_token_dim=0)
+    blk = init_synthetic_(TransformerBlock(cfg, cross_attend=False), seed=0)
+    sd = {"L." + k: v.float() for k, v in blk.state_dict().items()}
+    N_full = wl["L"] + cfg.num_memory_tokens
+    N = min(tokens, N_full) if tokens else N_full
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1, N, cfg.embed_dim, generator=g)
+    g6 = torch.randn(1, 6 * cfg.embed_dim, generator=g) * 0.5
+    mode = "fp8" if wl["mode"] == "fp8" else "fp32"
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        odit.block_only(sd, "L", oc, x, g6, mode=mode)
+        dt = time.perf_counter() - t0
+    # one step = depth blocks x (cond + uncond) sequences; the cross-attention / local-cond / prologue
+    # work not in this sample is < 10% of a block and is left out (the figure is a lower bound on CPU time)
+    return dt * (N_full / N) * cfg.depth * 2 * wl["prompts"], dt
+
+
+def run_reference(args, wl, world, rank):
+    """The reference arm: the oracle port (the reference is Python; nothing compiles) on all host cores."""
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    tokens = 2 * wl["L"] * wl["prompts"]
+    sample_tokens = 4096
+    for _ in range(args.warmup):
+        cpu_block_sample(wl, threads, sample_tokens)
+    steps = []
+    for _ in range(args.steps):
+        s, _dt = cpu_block_sample(wl, threads, sample_tokens)
+        steps.append(s)
+    step_s = statistics.median(steps)
+    value = tokens / step_s
+    sample = (f"one {wl['model']} block ({wl['mode']} fake-quant linears, fp32) over {sample_tokens} tokens per "
+              f"step, scaled x(L+64)/{sample_tokens} x{model_cfg(wl['model']).depth} blocks x2 CFG halves")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "L": wl["L"], "prompts_per_gpu": wl["prompts"],
+                   "parallelism": f"dp{world}"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, wl, world, rank, local):
+    from sa3_b200 import ops, _lib
+    from sa3_b200.modules import DiffusionTransformer, init_synthetic_
+
+    dev = torch.device("cuda", local)
+    cfg = model_cfg(wl["model"])
+    model = init_synthetic_(DiffusionTransformer(cfg), seed=0).quantize(wl["mode"])
+    eng = model.engine()
+    x, t, cond, gemb, loc = make_inputs(wl, cfg, seed=100 + rank, device=dev)
+    cs, aps = wl["cfg_scale"], wl["apg_scale"]
+
+    # launches per step (one eager step; every C-ABI call is one kernel launch)
+    n0 = ops.LAUNCHES
+    with torch.inference_mode():
+        eng.forward(x, t, cond, gemb, loc, cfg_scale=cs, apg_scale=aps)
+    launches_per_step = ops.LAUNCHES - n0
+    torch.cuda.synchronize()
+
+    with torch.inference_mode():
+        step = eng.graphed(x, t, cond, gemb, loc, cfg_scale=cs, apg_scale=aps)
+        for _ in range(args.warmup):
+            step(x, t, cond, gemb, loc)
+        torch.cuda.synchronize()
+
+        clocks = ClockSampler(local)
+        clocks.start()
+        time.sleep(0.3)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = e0.elapsed_time(e1) / args.steps
+        clk = clocks.stop()
+    ms_max = max_over_ranks(ms, world)
+    tokens_per_gpu = 2 * wl["L"] * wl["prompts"]
+    value = tokens_per_gpu * world / (ms_max / 1e3)
+
+    # ---- e2e: the public module call with pinned HOST inputs (H2D inside), result read back to the host
+    model.enable_cuda_graph()
+    hx, ht, hc, hg, hl = (a.cpu().pin_memory() for a in (x, t, cond, gemb, loc))
+    with torch.inference_mode():
+        for _ in range(max(2, args.warmup)):
+            model(hx, ht, cross_attn_cond=hc, global_embed=hg, local_add_cond=hl, cfg_scale=cs, apg_scale=aps).cpu()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record()
+        for _ in range(args.steps):
+            v = model(hx, ht, cross_attn_cond=hc, global_embed=hg, local_add_cond=hl, cfg_scale=cs, apg_scale=aps)
+            out_host = v.to("cpu")
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    h2d = sum(a.numel() * a.element_size() for a in (hx, ht, hc, hg, hl))
+    d2h = out_host.numel() * out_host.element_size()
+
+    # ---- roofline of the dominant kernel: the FF GLU.proj FP8 GEMM (M=B*N, N=2*ff_inner, K=dim),
+    # timed live with CUDA events on the launching stream, operands from the step's own buffers
+    ws = eng.ws
+    lin = eng.lin["transformer.layers.0.ff.ff.0.proj"]
+    scale = ws.scale[4:5]
+    M, K, Nw = ws.a.shape[0], ws.a.shape[1], lin.w.shape[0]
+    reps = 20
+    with torch.inference_mode():
+        for _ in range(3):
+            eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)
+        e1.record()
+        torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * M * Nw * K
+    achieved = flops / (k_ms / 1e3) / 1e12
+    peaks = _peaks()
+    if wl["mode"] == "fp8":
+        if peaks:
+            peak, peak_src = 2 * peaks["bf16_tflops"], "2x measured bf16 burst (MEASURED_PEAKS.json; no fp8 entry)"
+        else:
+            peak, peak_src = 2 * 1590.0, "2x fallback bf16 1.59 PF"
+    else:
+        peak, peak_src = (peaks["bf16_tflops"], "measured bf16 burst") if peaks else (1590.0, "fallback")
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel<fp8> (FF GLU.proj, SwiGLU epilogue)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": peak_src, "traffic": None,
+                "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
+
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8-e4m3 linears / bf16 attention" if wl["mode"] == "fp8" else "bf16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "model": f"sa3-{wl['model']} DiT, random init",
+                       "dim": cfg.embed_dim, "depth": cfg.depth, "heads": cfg.num_heads,
+                       "differential": cfg.differential, "window": list(cfg.sliding_window), "L": wl["L"],
+                       "memory_tokens": cfg.num_memory_tokens, "context_tokens": wl["Tc"],
+                       "prompts_per_gpu": wl["prompts"], "global_batch": 2 * wl["prompts"] * world,
+                       "seq_len": wl["L"], "cfg_scale": wl["cfg_scale"], "parallelism": f"dp{world}",
+                       "l2": "working set > L2 (1.45 GB FP8 weights + activations per step); no flush"},
+            "clocks": clk,
+            "e2e": {"value": tokens_per_gpu * world / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "launches_per_step": launches_per_step,
+            "roofline": roofline,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = len(os.sched_getaffinity(0))
+            step_s, meas = cpu_block_sample(wl, threads)
+            res["cpu_baseline"] = {"value": tokens_per_gpu / step_s, "unit": UNIT, "cores": threads, "kind": "port",
+                                   "sample": f"oracle fp32 block over L+64 tokens ({meas:.1f} s measured), "
+                                             f"scaled x{cfg.depth} blocks x2 CFG halves"}
+        print(json.dumps(res), flush=True)
+    del step
+    model._graphs = None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="medium_fp8")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, wl, world, rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, wl, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -86,6 +86,7 @@ typedef struct {
   int seg_in;               /* output row remap: if > 0, out_row = (m / seg_in) * seg_out + seg_offset + m % seg_in */
   int seg_out;
   int seg_offset;
+  int c_f32;                /* nonzero: C and residual are fp32 (the fp32 residual stream), else bf16 */
 } sa3_epilogue;
 
 int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
@@ -105,11 +106,12 @@ int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long lo
  *   s = max(*quant_amax, 1e-12) / 448 first and saturates, and, if scale_out
  *   is non-NULL, stores s there for the consuming GEMM's a_scale).
  * mode SA3_NORM_AMAX writes nothing and atomically maxes |y| into *amax_out.
- * x is bf16 [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
+ * x is bf16 or fp32 (x_dtype) [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
  */
 #define SA3_NORM_WRITE 0
 #define SA3_NORM_AMAX 1
-int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, long long ldx, long long ldo, const float* gamma,
+int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D, long long ldx, long long ldo,
+                         const float* gamma,
                          float eps, const float* mod, long long ld_mod, int scale_off, int shift_off,
                          int rows_per_batch, const int* row_batch, int mode, int out_dtype,
                          const float* quant_amax, float* scale_out, float* amax_out, void* stream);
@@ -119,6 +121,13 @@ int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, long long ld
  * kernel only computes max|x| into it (no write). x is bf16. */
 int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, long long ldx, long long ldo,
                       const float* amax, float* scale_out, float* amax_out, void* stream);
+
+/* Element type conversion of a row-major [rows, cols] view: fp32 <-> bf16
+ * (round to nearest even). cols must be a multiple of 8, rows 16-byte aligned.
+ * Used to hand the fp32 residual stream to a bf16 GEMM operand (project_out,
+ * transformer.py:1267). */
+int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype, int rows, int cols, long long ldx,
+                long long ldo, void* stream);
 
 /* ---------------------------------------------- glue: qk-norm + partial RoPE (a5, a6)
  *

@@ -83,6 +83,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, wl: int = -1, w
     Rows with no visible key produce zeros (flash-attn convention).
     """
     d = q.shape[-1]
+    if (scale is None and wl >= 0 and wr >= 0 and q.shape[-2] == k.shape[-2] and q.shape[-2] > 2048
+            and wl + wr < q.shape[-2]):
+        # long windowed self-attention: the reference's own chunked-halo formulation (same values,
+        # no N x N score matrix)
+        return chunked_halo_attention(q, k, v, wl, wr)
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     s = torch.matmul(q, k.transpose(-1, -2)) * scale
     m = band_mask(q.shape[-2], k.shape[-2], wl, wr)

@@ -58,6 +58,24 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[
   }
 }
 
+__device__ __forceinline__ void load_f32x32(const float* p, float (&v)[32]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 u = q[i];
+    v[4 * i] = u.x;
+    v[4 * i + 1] = u.y;
+    v[4 * i + 2] = u.z;
+    v[4 * i + 3] = u.w;
+  }
+}
+
+__device__ __forceinline__ void store_f32x32(float* p, const float (&v)[32]) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const float (&v)[32]) {
   uint4* q = reinterpret_cast<uint4*>(p);
 #pragma unroll
@@ -204,7 +222,7 @@ __global__ void __launch_bounds__(128, 1)
         const int nc = nout0 + c * 32;
         if (row_ok && nc < Nout) {
           __nv_bfloat16* dst = C + (long long)orow * p.ldc + nc;
-          if (nc + 32 <= Nout && (p.ldc & 7) == 0) {
+          if (nc + 32 <= Nout && (p.ldc & 7) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
             store_bf16x32(dst, y);
           } else {
 #pragma unroll
@@ -223,20 +241,32 @@ __global__ void __launch_bounds__(128, 1)
         float v[32];
         tmem_ld32(trow + c * 32, v);
         apply_scale_bias(v, nc, p.N, sa, p.b_scale, e.bias);
-        const bool full_chunk = (nc + 32 <= p.N) && ((p.ldc & 7) == 0) && ((e.ld_residual & 7) == 0);
+        const bool full_chunk = (nc + 32 <= p.N) && ((p.ldc & 7) == 0) && ((e.ld_residual & 7) == 0) &&
+                                ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                                ((reinterpret_cast<uintptr_t>(e.residual) & 15) == 0);
         if (e.kind == SA3_EPI_SILU) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = siluf_(v[i]);
         } else if (e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL) {
           if (row_ok) {
-            const __nv_bfloat16* res =
-                reinterpret_cast<const __nv_bfloat16*>(e.residual) + (long long)orow * e.ld_residual + nc;
             float r[32];
-            if (full_chunk) {
-              load_bf16x32(res, r);
-            } else {
+            if (e.c_f32) {
+              const float* res = reinterpret_cast<const float*>(e.residual) + (long long)orow * e.ld_residual + nc;
+              if (full_chunk) {
+                load_f32x32(res, r);
+              } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) r[i] = (nc + i < p.N) ? __bfloat162float(res[i]) : 0.f;
+                for (int i = 0; i < 32; ++i) r[i] = (nc + i < p.N) ? res[i] : 0.f;
+              }
+            } else {
+              const __nv_bfloat16* res =
+                  reinterpret_cast<const __nv_bfloat16*>(e.residual) + (long long)orow * e.ld_residual + nc;
+              if (full_chunk) {
+                load_bf16x32(res, r);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = (nc + i < p.N) ? __bfloat162float(res[i]) : 0.f;
+              }
             }
             if (e.kind == SA3_EPI_GATED_RESIDUAL) {
               const float* gt = e.gate + (long long)batch * e.ld_gate + nc;
@@ -252,18 +282,30 @@ __global__ void __launch_bounds__(128, 1)
           }
         }
         if (row_ok) {
-          __nv_bfloat16* dst = C + (long long)orow * p.ldc + nc;
-          if (full_chunk) {
-            store_bf16x32(dst, v);
-          } else {
+          if (e.c_f32) {
+            float* dst = reinterpret_cast<float*>(p.C) + (long long)orow * p.ldc + nc;
+            if (full_chunk) {
+              store_f32x32(dst, v);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (nc + i < p.N) dst[i] = __float2bfloat16(v[i]);
+              for (int i = 0; i < 32; ++i)
+                if (nc + i < p.N) dst[i] = v[i];
+            }
+          } else {
+            __nv_bfloat16* dst = C + (long long)orow * p.ldc + nc;
+            if (full_chunk) {
+              store_bf16x32(dst, v);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (nc + i < p.N) dst[i] = __float2bfloat16(v[i]);
+            }
           }
           if (e.amax_out) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (nc + i < p.N) amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16(v[i]))));
+              if (nc + i < p.N)
+                amax = fmaxf(amax, fabsf(e.c_f32 ? v[i] : __bfloat162float(__float2bfloat16(v[i]))));
           }
         }
       }
@@ -308,6 +350,7 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (epi) e = *epi;
   if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_RESIDUAL) return SA3_ERR_ARG;
   if (e.kind == SA3_EPI_SWIGLU) {
+    if (e.c_f32) return SA3_ERR_UNSUPPORTED;
     if (N % GEMM_BN != 0) return SA3_ERR_UNSUPPORTED;
     if (ldc < N / 2) return SA3_ERR_ARG;
   } else if (ldc < N) {

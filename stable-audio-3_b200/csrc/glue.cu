@@ -73,7 +73,8 @@ __device__ __forceinline__ void block_amax_commit(float v, float* amax_out) {
 }
 
 struct NormParams {
-  const __nv_bfloat16* x;
+  const void* x;
+  int x_f32;
   void* out;
   int rows, D;
   long long ldx, ldo;
@@ -102,14 +103,22 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
   }
   float amax = 0.f;
   for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < p.rows; row += gridDim.x * (blockDim.x >> 5)) {
-    const __nv_bfloat16* xr = p.x + (long long)row * p.ldx;
     float v[MAXC][8];
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
       const int c = lane + i * 32;
       if (c < nchunk) {
-        unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+        if (p.x_f32) {
+          const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) +
+                                                             (long long)row * p.ldx + c * 8);
+          const float4 a = xr[0], b = xr[1];
+          v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+          v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+        } else {
+          const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + (long long)row * p.ldx;
+          unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
       }
@@ -257,6 +266,38 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
   }
 }
 
+struct ConvParams {
+  const void* x;
+  void* out;
+  int x_f32, out_f32;
+  int rows, cols;
+  long long ldx, ldo;
+};
+
+__global__ void __launch_bounds__(256) convert_kernel(ConvParams p) {
+  const int cpr = p.cols / 8;
+  const long long total = (long long)p.rows * cpr;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    float v[8];
+    if (p.x_f32) {
+      const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + r * p.ldx + c * 8);
+      const float4 a = s[0], b = s[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+      unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + r * p.ldx + c * 8), v);
+    }
+    if (p.out_f32) {
+      float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + r * p.ldo + c * 8);
+      d[0] = make_float4(v[0], v[1], v[2], v[3]);
+      d[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + r * p.ldo + c * 8) = pack8(v);
+    }
+  }
+}
+
 inline int grid_for(long long work_items, int per_block) {
   long long g = (work_items + per_block - 1) / per_block;
   const long long cap = 148LL * 16;
@@ -269,11 +310,12 @@ inline int grid_for(long long work_items, int per_block) {
 
 using namespace sa3;
 
-extern "C" int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, long long ldx, long long ldo,
-                                    const float* gamma, float eps, const float* mod, long long ld_mod, int scale_off,
+extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D, long long ldx,
+                                    long long ldo, const float* gamma, float eps, const float* mod, long long ld_mod, int scale_off,
                                     int shift_off, int rows_per_batch, const int* row_batch, int mode, int out_dtype,
                                     const float* quant_amax, float* scale_out, float* amax_out, void* stream) {
   if (!x || rows <= 0 || D <= 0 || (D % 8) || ldx < D) return SA3_ERR_ARG;
+  if (x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32) return SA3_ERR_DTYPE;
   if (!aligned16(x) || (ldx % 8)) return SA3_ERR_ALIGN;
   if (mode == SA3_NORM_AMAX) {
     if (!amax_out) return SA3_ERR_ARG;
@@ -292,7 +334,8 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, void* out, int rows, int D, l
   }
   if (mod && !row_batch && rows_per_batch <= 0) return SA3_ERR_ARG;
   NormParams p;
-  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.x = x;
+  p.x_f32 = x_dtype == SA3_DT_F32;
   p.out = out;
   p.rows = rows;
   p.D = D;
@@ -368,5 +411,16 @@ extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, in
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const long long items = (long long)rows * ngroups * heads;
   qk_norm_rope_kernel<<<grid_for(items, 32), 256, 0, st>>>(p);
+  return launch_status();
+}
+
+extern "C" int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype, int rows, int cols, long long ldx,
+                           long long ldo, void* stream) {
+  if (!x || !out || rows <= 0 || cols <= 0 || (cols % 8) || ldx < cols || ldo < cols) return SA3_ERR_ARG;
+  if ((x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32) || (out_dtype != SA3_DT_BF16 && out_dtype != SA3_DT_F32))
+    return SA3_ERR_DTYPE;
+  if (!aligned16(x) || !aligned16(out) || (ldx % 8) || (ldo % 8)) return SA3_ERR_ALIGN;
+  ConvParams p{x, out, x_dtype == SA3_DT_F32, out_dtype == SA3_DT_F32, rows, cols, ldx, ldo};
+  convert_kernel<<<grid_for((long long)rows * (cols / 8), 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return launch_status();
 }

@@ -8,6 +8,8 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "../../include/sa3b200.h"
 
@@ -52,12 +54,20 @@ inline int launch_status() {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// Raise the dynamic shared-memory limit of `func` (a host-side attribute of
-// the function on the current device; cheap and legal during stream capture).
+// Raise the dynamic shared-memory limit of `func` once per device, so later
+// calls (including those made during CUDA-graph stream capture) only launch.
 template <typename F>
 inline int ensure_smem(F func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;  // (kernel, device) pairs already configured
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SA3_ERR_LAUNCH;
+  const auto key = std::make_pair(reinterpret_cast<const void*>(func), dev);
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count(key)) return SA3_OK;
   if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return SA3_ERR_LAUNCH;
+  done.insert(key);
   return SA3_OK;
 }
 

@@ -47,6 +47,7 @@ class Epilogue(ctypes.Structure):
         ("seg_in", c_int),
         ("seg_out", c_int),
         ("seg_offset", c_int),
+        ("c_f32", c_int),
     ]
 
 
@@ -56,8 +57,9 @@ SIGNATURES = {
     "sa3_get_device_error": [ctypes.POINTER(c_int)],
     "sa3_gemm": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_ll, c_int, c_vp, c_vp,
                  ctypes.POINTER(Epilogue), c_vp],
-    "sa3_rmsnorm_modulate": [c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int, c_int,
-                             c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
+    "sa3_rmsnorm_modulate": [c_vp, c_int, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int,
+                             c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
+    "sa3_convert": [c_vp, c_int, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_vp],
     "sa3_quantize_e4m3": [c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_vp, c_vp, c_vp],
     "sa3_qk_norm_rope": [c_vp, c_int, c_ll, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_vp),
                          ctypes.POINTER(c_int), c_float, c_vp, c_int, c_int, c_vp, c_vp],

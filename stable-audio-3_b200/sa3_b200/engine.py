@@ -1,0 +1,364 @@
+"""DiT denoiser forward on the sm_100a kernels.
+
+DiTEngine takes a reference-shaped DiffusionTransformer (sa3_b200.modules,
+same parameter names as stable_audio_3/models/dit.py) and runs
+DiffusionTransformer.forward (dit.py:345-643) -> _forward (dit.py:179-309) ->
+ContinuousTransformer.forward (transformer.py:1161-1272) -> TransformerBlock.forward
+(transformer.py:996-1049) with every hot op in libsa3b200.so:
+
+  per block (token rows [B*N, D], N = L + memory tokens):
+    RMSNorm+adaLN modulate (+FP8 quant)   -> to_qkv GEMM -> qk RMSNorm + RoPE (in place)
+    -> windowed (differential) attention   -> to_out GEMM with gate*sigmoid(1-g)+residual epilogue
+    cross: RMSNorm (+quant) -> to_q GEMM -> q-norm ; ctx -> to_kv GEMM -> k-norm
+           -> full attention over the context -> to_out GEMM with residual epilogue
+    local cond: Linear+SiLU GEMM -> Linear GEMM adding into rows 64.. (left pad) of the stream
+    FF: RMSNorm+modulate (+quant) -> GLU.proj GEMM with SwiGLU epilogue (+amax) (-> quant)
+        -> linear_out GEMM with gate*sigmoid(1-g)+residual epilogue
+
+Exact rewrites of the reference (documented in DESIGN.md):
+  * preprocess_conv (1x1, +x) is folded into project_in: W_in (I + W_pre);
+    postprocess_conv (1x1, +y) into project_out: (I + W_post) W_out.
+  * GLU.proj rows are interleaved in blocks of 128 so the SwiGLU fuses into the GEMM epilogue.
+  * local_add_cond's 257 channels are zero-padded to 264 (16-byte rows for TMA).
+The residual stream (the token rows every block adds into) and the final
+projection are kept in fp32; GEMM operands and the other activations are bf16
+(or e4m3). The timestep is kept in fp32 through ExpoFourierFeatures (the
+reference's bf16 path rounds it first); the CFG / APG combine runs in fp32.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, Optional
+
+import torch
+
+from . import ops
+from . import _lib
+from .quant import interleave_swiglu_rows, quantize_weight_e4m3
+
+QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_kv",
+                  "cross_attn.to_out", "ff.ff.0.proj", "ff.ff.2")
+
+
+def _pad_cols(w: torch.Tensor, mult: int = 8) -> torch.Tensor:
+    k = w.shape[1]
+    kp = (k + mult - 1) // mult * mult
+    if kp == k:
+        return w
+    out = torch.zeros(w.shape[0], kp, dtype=w.dtype)
+    out[:, :k] = w
+    return out
+
+
+@dataclass
+class Lin:
+    """A prepared linear: weight [N, K] (bf16 or e4m3) on the device, optional fp32 per-row scale and bias."""
+
+    w: torch.Tensor
+    scale: Optional[torch.Tensor]
+    bias: Optional[torch.Tensor]
+    fp8: bool
+
+    @property
+    def n(self):
+        return self.w.shape[0]
+
+
+class _Workspace:
+    def __init__(self, cfg, B: int, L: int, Tc: int, dev, fp8: bool):
+        D = cfg.embed_dim
+        N = L + cfg.num_memory_tokens
+        M = B * N
+        nq = 5 if cfg.differential else 3
+        self.B, self.L, self.N, self.M, self.Tc = B, L, N, M, Tc
+        bf = torch.bfloat16
+        self.h = torch.empty(M, D, device=dev, dtype=torch.float32)  # fp32 residual stream
+        self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
+        self.qkv = torch.empty(M, nq * D, device=dev, dtype=bf)
+        self.o = torch.empty(M, D, device=dev, dtype=bf)
+        self.o8 = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
+        self.qx = torch.empty(M, (2 if cfg.differential else 1) * D, device=dev, dtype=bf)
+        self.kv = torch.empty(max(B * Tc, 1), (3 if cfg.differential else 2) * D, device=dev, dtype=bf)
+        self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
+        self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
+        self.t1 = torch.empty(B * L, D, device=dev, dtype=bf)
+        self.loc = torch.zeros(B * L, 264, device=dev, dtype=bf)
+        self.xin = torch.empty(B * L, cfg.io_channels, device=dev, dtype=bf)
+        self.hb = torch.empty(B * L, D, device=dev, dtype=bf)  # bf16 copy of the stream for project_out
+        self.out = torch.empty(B * L, cfg.io_channels, device=dev, dtype=torch.float32)
+        self.ctx = torch.empty(max(B * Tc, 1), D, device=dev, dtype=bf)
+        self.ctx8 = torch.empty(max(B * Tc, 1), D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
+        self.nslots = 8 * cfg.depth + 8
+        self.amax = torch.zeros(self.nslots, device=dev, dtype=torch.float32)
+        self.scale = torch.zeros(self.nslots, device=dev, dtype=torch.float32)
+        self.small = torch.empty(B, 8 * D, device=dev, dtype=bf)
+
+
+class DiTEngine:
+    def __init__(self, module, mode: str = "bf16", gptq_layers: Optional[dict] = None, device="cuda"):
+        if mode not in ("bf16", "fp8", "gptq"):
+            raise ValueError(mode)
+        if not torch.cuda.is_available():
+            raise RuntimeError("DiTEngine needs a CUDA device (no CPU path)")
+        _lib.load()
+        self.cfg = cfg = module.cfg
+        self.mode = mode
+        self.fp8 = mode == "fp8"
+        self.dev = torch.device(device)
+        if cfg.head_dim != 64:
+            raise NotImplementedError("head_dim must be 64")
+        sd = {k: v.detach().float().cpu() for k, v in module.state_dict().items()}
+        self.lin: Dict[str, Lin] = {}
+        for name in sorted({k[:-len(".weight")] for k in sd if k.endswith(".weight")}):
+            if name in ("preprocess_conv", "postprocess_conv", "transformer.project_in", "transformer.project_out"):
+                continue
+            quantized = self.fp8 and any(name.endswith(s) for s in QUANT_SUFFIXES)
+            self.lin[name] = self._prep(name, sd[name + ".weight"], sd.get(name + ".bias"), quantized)
+        D = cfg.embed_dim
+        eye = torch.eye(cfg.io_channels)
+        w_in = sd["transformer.project_in.weight"] @ (eye + sd["preprocess_conv.weight"][:, :, 0])
+        w_out = (eye + sd["postprocess_conv.weight"][:, :, 0]) @ sd["transformer.project_out.weight"]
+        self.lin["project_in"] = Lin(w_in.to(self.dev, torch.bfloat16).contiguous(), None, None, False)
+        self.lin["project_out"] = Lin(w_out.to(self.dev, torch.bfloat16).contiguous(), None, None, False)
+        self.memory = sd["transformer.memory_tokens"].to(self.dev, torch.float32) if cfg.num_memory_tokens else None
+        self.sst = torch.stack([sd[f"transformer.layers.{i}.to_scale_shift_gate"] for i in range(cfg.depth)]).to(
+            self.dev)
+        self.gam = {k: v.to(self.dev).contiguous() for k, v in sd.items() if k.endswith("gamma")}
+        self.rope = None
+        self.ws: Optional[_Workspace] = None
+        ramp = torch.linspace(0, 1, cfg.timestep_features_dim // 2, dtype=torch.float32)
+        self.t_freqs = torch.exp(ramp * (math.log(10000.0) - math.log(0.5)) + math.log(0.5)).to(self.dev)
+        if mode == "gptq":
+            raise NotImplementedError("GPTQ engine path is built on sa3_b200.gptq")
+
+    # ------------------------------------------------------------------ prep
+    def _prep(self, name, w, b, quantized: bool) -> Lin:
+        if name.endswith("ff.ff.0.proj"):
+            w, b = interleave_swiglu_rows(w, b)
+        w = _pad_cols(w)
+        bias = None if b is None else b.to(self.dev, torch.float32).contiguous()
+        if quantized:
+            wq, s = quantize_weight_e4m3(w)
+            return Lin(wq.to(self.dev).contiguous(), s.to(self.dev), bias, True)
+        return Lin(w.to(self.dev, torch.bfloat16).contiguous(), None, bias, False)
+
+    def _workspace(self, B, L, Tc) -> _Workspace:
+        ws = self.ws
+        if ws is None or (ws.B, ws.L, ws.Tc) != (B, L, Tc):
+            self.ws = ws = _Workspace(self.cfg, B, L, Tc, self.dev, self.fp8)
+        N = ws.N
+        if self.rope is None or self.rope.shape[0] < N:
+            self.rope = ops.rope_table(N, 32, device=self.dev)
+        return ws
+
+    # ------------------------------------------------------------------ helpers
+    def _gemm(self, x, lin: Lin, out=None, x_scale=None, **kw):
+        if lin.fp8 and x.dtype != torch.float8_e4m3fn:
+            raise RuntimeError("fp8 linear needs a quantized activation")
+        return ops.gemm(x, lin.w, out, a_scale=x_scale if lin.fp8 else None, b_scale=lin.scale, bias=lin.bias, **kw)
+
+    def _norm_to_a(self, ws, x, gamma, slot, mod=None, scale_off=0, shift_off=0):
+        """RMSNorm(+modulate) of the stream into ws.a; FP8: two passes (amax, quantize)."""
+        cfg = self.cfg
+        kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, rows_per_batch=ws.N)
+        if self.fp8:
+            am = ws.amax[slot:slot + 1]
+            sc = ws.scale[slot:slot + 1]
+            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, **kw)
+            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=ws.a, quant_amax=am, scale_out=sc, **kw)
+            return ws.a, sc
+        ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=ws.a, **kw)
+        return ws.a, None
+
+    def _quant(self, ws, x, out8, slot):
+        """FP8: quantize x (whose amax is already in slot) into out8; bf16: pass x through."""
+        if not self.fp8:
+            return x, None
+        sc = ws.scale[slot:slot + 1]
+        ops.quantize_e4m3(x, ws.amax[slot:slot + 1], out=out8, scale_out=sc)
+        return out8, sc
+
+    # ------------------------------------------------------------------ forward
+    @torch.no_grad()
+    def forward(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, cfg_scale: float = 1.0,
+                apg_scale: float = 1.0):
+        """DiffusionTransformer.forward for the rf_denoiser objective (dit.py:345-643)."""
+        dev = self.dev
+        x = x.to(dev)
+        t = t.to(dev, torch.float32)
+        if cfg_scale != 1.0 and cross_attn_cond is not None:
+            bx = torch.cat([x, x])
+            bt = torch.cat([t, t])
+            cc = cross_attn_cond.to(dev)
+            bc = torch.cat([cc, torch.zeros_like(cc)])
+            bg = torch.cat([global_embed, global_embed]).to(dev) if global_embed is not None else None
+            bl = torch.cat([local_add_cond, local_add_cond]).to(dev) if local_add_cond is not None else None
+            out = self.inner(bx, bt, bc, bg, bl)
+            return self.cfg_combine(x, t, out, cfg_scale, apg_scale)
+        return self.inner(x, t, cross_attn_cond, global_embed, local_add_cond)
+
+    def graphed(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, cfg_scale: float = 1.0,
+                apg_scale: float = 1.0) -> "GraphedStep":
+        """Capture one forward at these shapes into a CUDA graph (inputs are copied into static buffers)."""
+        return GraphedStep(self, (x, t, cross_attn_cond, global_embed, local_add_cond), cfg_scale, apg_scale)
+
+    def cfg_combine(self, x, t, out, cfg_scale, apg_scale):
+        """CFG + APG for rf_denoiser (dit.py:571-625; apg_project dit.py:311-343), fp32."""
+        x = x.float()
+        cond_out, uncond_out = out.float().chunk(2)
+        sigma = t.float()[:, None, None]
+        cond_den = x - cond_out * sigma
+        diff = (uncond_out - cond_out) * sigma  # cond_den - uncond_den
+        if apg_scale == 0.0:
+            cfg_diff = diff
+        else:
+            v1 = cond_den / cond_den.flatten(1).norm(dim=1).clamp_min(1e-12)[:, None, None]
+            par = (diff * v1).sum(dim=(1, 2), keepdim=True) * v1
+            orth = diff - par
+            cfg_diff = orth if apg_scale == 1.0 else apg_scale * orth + (1 - apg_scale) * diff
+        cfg_den = cond_den + (cfg_scale - 1) * cfg_diff
+        return (x - cfg_den) / sigma
+
+    @torch.no_grad()
+    def inner(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None):
+        """DiffusionTransformer._forward + ContinuousTransformer.forward on the kernels; returns fp32 [B, C, L]."""
+        cfg = self.cfg
+        D = cfg.embed_dim
+        B, C, L = x.shape
+        Tc = cross_attn_cond.shape[1] if cross_attn_cond is not None else 0
+        ws = self._workspace(B, L, Tc)
+        N, M = ws.N, ws.M
+        nm = cfg.num_memory_tokens
+        ln = self.lin
+        ws.amax.zero_()
+
+        # ---- conditioning prologue (dit.py:197-262, transformer.py:1210-1211)
+        tf = t.float()[:, None] * self.t_freqs[None, :] * (2 * math.pi)
+        feats = torch.cat([torch.cos(tf), torch.sin(tf)], dim=-1).to(torch.bfloat16)
+        sm = ws.small
+        temb1 = self._gemm(feats, ln["to_timestep_embed.0"], sm[:, 0:D], kind=_lib.EPI_SILU)
+        temb = self._gemm(temb1, ln["to_timestep_embed.2"], sm[:, D:2 * D])
+        if global_embed is not None:
+            ge = global_embed.to(torch.bfloat16).contiguous()
+            g1 = self._gemm(ge, ln["to_global_embed.0"], sm[:, 2 * D:3 * D], kind=_lib.EPI_SILU)
+            g = self._gemm(g1, ln["to_global_embed.2"], sm[:, 3 * D:4 * D], kind=_lib.EPI_RESIDUAL, residual=temb)
+        else:
+            g = temb
+        e1 = self._gemm(g, ln["transformer.global_cond_embedder.0"], sm[:, 4 * D:5 * D], kind=_lib.EPI_SILU)
+        g6 = self._gemm(e1, ln["transformer.global_cond_embedder.2"])  # [B, 6D]
+        ss = (self.sst[:, None, :] + g6.float()[None]).contiguous()    # [depth, B, 6D] fp32
+
+        ctx = None
+        if cross_attn_cond is not None:
+            cc = cross_attn_cond.reshape(B * Tc, -1).to(torch.bfloat16).contiguous()
+            c1 = self._gemm(cc, ln["to_cond_embed.0"], kind=_lib.EPI_SILU)
+            ctx = self._gemm(c1, ln["to_cond_embed.2"], ws.ctx)
+        ctx_a, ctx_s = ctx, None
+        if ctx is not None and self.fp8:
+            slot = 8 * cfg.depth
+            ops.absmax(ctx, ws.amax[slot:slot + 1])
+            ctx_a, ctx_s = self._quant(ws, ctx, ws.ctx8, slot)
+
+        has_local = local_add_cond is not None and cfg.local_add_cond_dim > 0
+        if has_local:
+            ws.loc.view(B, L, -1)[:, :, :cfg.local_add_cond_dim].copy_(local_add_cond.transpose(1, 2))
+
+        # ---- trunk input: project_in (preprocess conv folded) into rows nm.. of each sequence
+        ws.xin.view(B, L, C).copy_(x.transpose(1, 2))
+        h = ws.h
+        self._gemm(ws.xin, ln["project_in"], h, seg=(L, N, nm))
+        if nm:
+            h.view(B, N, D)[:, :nm].copy_(self.memory)
+
+        wl, wr = cfg.sliding_window if cfg.sliding_window is not None else (-1, -1)
+        diff = cfg.differential
+        qkv, o, qx, kv = ws.qkv, ws.o, ws.qx, ws.kv
+        H = cfg.num_heads
+        for i in range(cfg.depth):
+            p = f"transformer.layers.{i}."
+            ssi = ss[i]
+            s0 = 8 * i
+            # -- self-attention with adaLN (transformer.py:1018-1029)
+            a, asc = self._norm_to_a(ws, h, self.gam[p + "pre_norm.gamma"], s0, ssi, 0, D)
+            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc)
+            gq, gk = self.gam[p + "self_attn.q_norm.gamma"], self.gam[p + "self_attn.k_norm.gamma"]
+            if diff:
+                ops.qk_norm_rope(qkv, H, [0, D, 3 * D, 4 * D], [gq, gk, gq, gk], [True] * 4, cfg.qk_norm_eps,
+                                 self.rope, rows_per_batch=N)
+                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
+                              k2=qkv[:, 4 * D:5 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N,
+                              window=(wl, wr), out=o, amax_out=ws.amax[s0 + 1:s0 + 2] if self.fp8 else None)
+            else:
+                ops.qk_norm_rope(qkv, H, [0, D], [gq, gk], [True] * 2, cfg.qk_norm_eps, self.rope, rows_per_batch=N)
+                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, batch=B, max_seqlen_q=N,
+                              max_seqlen_k=N, window=(wl, wr), out=o,
+                              amax_out=ws.amax[s0 + 1:s0 + 2] if self.fp8 else None)
+            oa, osc = self._quant(ws, o, ws.o8, s0 + 1)
+            self._gemm(oa, ln[p + "self_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
+                       gate=ssi[:, 2 * D:3 * D], rows_per_batch=N)
+            # -- cross-attention (transformer.py:1031-1035), no adaLN, no RoPE
+            if ctx is not None and (p + "cross_attn.to_q") in ln:
+                c, csc = self._norm_to_a(ws, h, self.gam[p + "cross_attend_norm.gamma"], s0 + 2)
+                self._gemm(c, ln[p + "cross_attn.to_q"], qx, x_scale=csc)
+                self._gemm(ctx_a, ln[p + "cross_attn.to_kv"], kv, x_scale=ctx_s)
+                gq, gk = self.gam[p + "cross_attn.q_norm.gamma"], self.gam[p + "cross_attn.k_norm.gamma"]
+                am = ws.amax[s0 + 3:s0 + 4] if self.fp8 else None
+                if diff:
+                    ops.qk_norm_rope(qx, H, [0, D], [gq, gq], [False, False], cfg.qk_norm_eps)
+                    ops.qk_norm_rope(kv, H, [0, D], [gk, gk], [False, False], cfg.qk_norm_eps)
+                    ops.attention(qx[:, 0:D], kv[:, 0:D], kv[:, 2 * D:3 * D], q2=qx[:, D:2 * D], k2=kv[:, D:2 * D],
+                                  heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc, out=o, amax_out=am)
+                else:
+                    ops.qk_norm_rope(qx, H, [0], [gq], [False], cfg.qk_norm_eps)
+                    ops.qk_norm_rope(kv, H, [0], [gk], [False], cfg.qk_norm_eps)
+                    ops.attention(qx, kv[:, 0:D], kv[:, D:2 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc,
+                                  out=o, amax_out=am)
+                oa, osc = self._quant(ws, o, ws.o8, s0 + 3)
+                self._gemm(oa, ln[p + "cross_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_RESIDUAL, residual=h)
+            # -- local additive conditioning, left-padded over the memory tokens (transformer.py:978-994, 77-88)
+            if has_local and (p + "to_local_embed.0") in ln:
+                self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
+                self._gemm(ws.t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h, seg=(L, N, nm))
+            # -- feed-forward with adaLN (transformer.py:1042-1049)
+            f, fsc = self._norm_to_a(ws, h, self.gam[p + "ff_norm.gamma"], s0 + 4, ssi, 3 * D, 4 * D)
+            self._gemm(f, ln[p + "ff.ff.0.proj"], ws.u, x_scale=fsc, kind=_lib.EPI_SWIGLU,
+                       amax_out=ws.amax[s0 + 5:s0 + 6] if self.fp8 else None)
+            ua, usc = self._quant(ws, ws.u, ws.u8, s0 + 5)
+            self._gemm(ua, ln[p + "ff.ff.2"], h, x_scale=usc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
+                       gate=ssi[:, 5 * D:6 * D], rows_per_batch=N)
+
+        # ---- drop memory tokens, project_out (postprocess conv folded) (transformer.py:1265-1267, dit.py:297-304)
+        for b in range(B):
+            ops.convert(h[b * N + nm:(b + 1) * N], ws.hb[b * L:(b + 1) * L])
+        self._gemm(ws.hb, ln["project_out"], ws.out)
+        return ws.out.view(B, L, C).transpose(1, 2)
+
+
+class GraphedStep:
+    """One denoiser forward captured in a CUDA graph, replayed with new inputs copied into static buffers.
+
+    Mirrors the reference TensorRT runner's graph-captured DiT step (optimized/tensorRT/scripts/
+    sa3_trt_core.py:511-694): all kernel launches of the step replay with no host work.
+    """
+
+    def __init__(self, engine: DiTEngine, inputs, cfg_scale: float, apg_scale: float):
+        self.engine = engine
+        self.static = [None if a is None else a.to(engine.dev).clone() for a in inputs]
+        self.cfg_scale, self.apg_scale = cfg_scale, apg_scale
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale)
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale)
+
+    def __call__(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None) -> torch.Tensor:
+        for dst, src in zip(self.static, (x, t, cross_attn_cond, global_embed, local_add_cond)):
+            if dst is not None:
+                dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.out

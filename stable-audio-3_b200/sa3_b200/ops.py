@@ -17,6 +17,14 @@ from ._lib import Epilogue
 
 E4M3_MAX = 448.0
 
+# Number of kernel launches issued through the C ABI by this process (one per call).
+LAUNCHES = 0
+
+
+def _count():
+    global LAUNCHES
+    LAUNCHES += 1
+
 
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
@@ -67,8 +75,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
         if seg is not None:
             raise RuntimeError("row remap needs an explicit out")
         out = torch.empty(M, ncols, device=a.device, dtype=torch.bfloat16)
-    if out.dtype != torch.bfloat16:
-        raise RuntimeError("gemm output is bf16")
+    if out.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("gemm output is bf16 or fp32")
+    if kind == _lib.EPI_SWIGLU and out.dtype != torch.bfloat16:
+        raise RuntimeError("SwiGLU epilogue writes bf16")
+    if residual is not None and residual.dtype != out.dtype:
+        raise RuntimeError("residual and output must share a dtype")
     for t, nm in ((a_scale, "a_scale"), (b_scale, "b_scale"), (bias, "bias"), (gate, "gate"), (amax_out, "amax")):
         if t is not None and t.dtype != torch.float32:
             raise RuntimeError(f"{nm} must be float32")
@@ -84,6 +96,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     epi.amax_out = _ptr(amax_out)
     if seg is not None:
         epi.seg_in, epi.seg_out, epi.seg_offset = seg
+    epi.c_f32 = 1 if out.dtype == torch.float32 else 0
+    _count()
     rc = _lib.load().sa3_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _row_stride(a), _row_stride(b),
                               _row_stride(out), _dt(a), _ptr(a_scale), _ptr(b_scale), ctypes.byref(epi), _stream())
     _lib.check(rc, "sa3_gemm")
@@ -99,7 +113,8 @@ def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float,
     rows, D = x.shape
     lib = _lib.load()
     if amax_only is not None:
-        rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), None, rows, D, _row_stride(x), 0, _ptr(gamma), eps, _ptr(mod),
+        _count()
+        rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), _dt(x), None, rows, D, _row_stride(x), 0, _ptr(gamma), eps, _ptr(mod),
                                       _row_stride(mod) if mod is not None else 0, scale_off, shift_off,
                                       rows_per_batch, _ptr(row_batch), _lib.NORM_AMAX, _lib.DT_BF16, None, None,
                                       amax_only.data_ptr(), _stream())
@@ -107,7 +122,8 @@ def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float,
         return None
     if out is None:
         out = torch.empty(rows, D, device=x.device, dtype=out_dtype)
-    rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), out.data_ptr(), rows, D, _row_stride(x), _row_stride(out),
+    _count()
+    rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), _dt(x), out.data_ptr(), rows, D, _row_stride(x), _row_stride(out),
                                   _ptr(gamma), eps, _ptr(mod), _row_stride(mod) if mod is not None else 0, scale_off,
                                   shift_off, rows_per_batch, _ptr(row_batch), _lib.NORM_WRITE, _dt(out),
                                   _ptr(quant_amax), _ptr(scale_out), None, _stream())
@@ -120,6 +136,7 @@ def quantize_e4m3(x: torch.Tensor, amax: torch.Tensor, out=None, scale_out=None)
     rows, cols = x.shape
     if out is None:
         out = torch.empty(rows, cols, device=x.device, dtype=torch.float8_e4m3fn)
+    _count()
     rc = _lib.load().sa3_quantize_e4m3(x.data_ptr(), out.data_ptr(), rows, cols, _row_stride(x), _row_stride(out),
                                        amax.data_ptr(), _ptr(scale_out), None, _stream())
     _lib.check(rc, "sa3_quantize_e4m3")
@@ -129,9 +146,21 @@ def quantize_e4m3(x: torch.Tensor, amax: torch.Tensor, out=None, scale_out=None)
 def absmax(x: torch.Tensor, amax_out: torch.Tensor) -> None:
     _need_cuda(x, amax_out)
     rows, cols = x.shape
+    _count()
     rc = _lib.load().sa3_quantize_e4m3(x.data_ptr(), None, rows, cols, _row_stride(x), 0, None, None,
                                        amax_out.data_ptr(), _stream())
     _lib.check(rc, "sa3_quantize_e4m3(amax)")
+
+
+def convert(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = x cast between fp32 and bf16 (2-D row-major views of equal shape)."""
+    _need_cuda(x, out)
+    rows, cols = x.shape
+    _count()
+    rc = _lib.load().sa3_convert(x.data_ptr(), _dt(x), out.data_ptr(), _dt(out), rows, cols, _row_stride(x),
+                                 _row_stride(out), _stream())
+    _lib.check(rc, "sa3_convert")
+    return out
 
 
 def qk_norm_rope(buf: torch.Tensor, heads: int, col_offsets: Sequence[int], gammas: Sequence[Optional[torch.Tensor]],
@@ -145,6 +174,7 @@ def qk_norm_rope(buf: torch.Tensor, heads: int, col_offsets: Sequence[int], gamm
     gps = (ctypes.c_void_p * n)(*[_ptr(g) for g in gammas])
     rps = (ctypes.c_int * n)(*[1 if r else 0 for r in rope])
     max_pos = cos_sin.shape[0] if cos_sin is not None else 0
+    _count()
     rc = _lib.load().sa3_qk_norm_rope(buf.data_ptr(), rows, _row_stride(buf), heads, n, offs, gps, rps, eps,
                                       _ptr(cos_sin), max_pos, rows_per_batch, _ptr(row_pos), _stream())
     _lib.check(rc, "sa3_qk_norm_rope")
@@ -182,6 +212,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, 
         if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
             raise RuntimeError("cu_seqlens must be int32")
     wl, wr = (int(window[0]), int(window[1]))
+    _count()
     rc = _lib.load().sa3_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q2), _ptr(k2), out.data_ptr(),
                                    _ptr(cu_seqlens_q), _ptr(cu_seqlens_k), batch_n, max_seqlen_q, max_seqlen_k,
                                    total_q, total_k, heads, 64, _row_stride(q), _row_stride(k), _row_stride(v),

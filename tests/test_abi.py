@@ -1,0 +1,43 @@
+"""CPU: the C-ABI library builds for sm_100a, loads, and exports every entry point include/sa3b200.h declares."""
+import ctypes
+import os
+import re
+
+from sa3_b200 import _lib, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "sa3b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\bint\s+(sa3_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "sa3_gemm" in syms and "sa3_attention" in syms
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_library_exports_every_declared_symbol():
+    path = build.build()
+    lib = ctypes.CDLL(path)
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+
+
+def test_version_callable_without_gpu():
+    assert _lib.load().sa3_version() >= 100
+
+
+def test_host_side_argument_errors_need_no_gpu():
+    lib = _lib.load()
+    # null pointers and bad sizes are rejected on the host before any CUDA call
+    assert lib.sa3_gemm(None, None, None, 0, 0, 0, 0, 0, 0, 0, None, None, None, None) == -1
+    assert lib.sa3_attention(None, None, None, None, None, None, None, None, 1, 1, 1, 1, 1, 1, 64, 64, 64, 64, 64,
+                             -1, -1, 0.125, 0, None, None) == -1
+    assert lib.sa3_rmsnorm_modulate(None, 0, None, 0, 0, 0, 0, None, 1e-5, None, 0, 0, 0, 0, None, 0, 0, None,
+                                    None, None, None) == -1
+    assert lib.sa3_convert(None, 0, None, 0, 0, 0, 0, 0, None) == -1

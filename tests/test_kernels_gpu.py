@@ -123,6 +123,39 @@ def test_gemm_epilogues(cuda):
     assert max_rel(outd, ref.view(-1, D)) < 1e-2
 
 
+def test_gemm_fp32_residual_stream(cuda):
+    from sa3_b200 import ops, _lib
+
+    g = _gen(21)
+    B, T, D, K = 2, 190, 256, 192
+    a = torch.randn(B * T, K, generator=g).bfloat16()
+    w = (torch.randn(D, K, generator=g) * 0.05).bfloat16()
+    res = torch.randn(B * T, D, generator=g)
+    gate = torch.randn(B, D, generator=g)
+    h = a.float() @ w.float().T
+    out = res.clone().to(cuda)
+    ops.gemm(a.to(cuda), w.to(cuda), out, kind=_lib.EPI_GATED_RESIDUAL, residual=out, gate=gate.to(cuda),
+             rows_per_batch=T)
+    ref = orf.gate_residual(h.view(B, T, D), gate[:, None, :], res.view(B, T, D)).view(-1, D)
+    assert (out.cpu() - ref).abs().max().item() < 1e-4 * ref.abs().max().item() + 1e-5
+    out32 = ops.gemm(a.to(cuda), w.to(cuda), torch.empty(B * T, D, device=cuda))
+    assert (out32.cpu() - h).abs().max().item() < 1e-4 * h.abs().max().item()
+
+
+def test_convert_and_fp32_norm_input(cuda):
+    from sa3_b200 import ops
+
+    g = _gen(23)
+    x = torch.randn(301, 1536, generator=g)
+    xb = ops.convert(x.to(cuda), torch.empty(301, 1536, device=cuda, dtype=torch.bfloat16))
+    assert torch.equal(xb.cpu(), x.bfloat16())
+    back = ops.convert(xb, torch.empty(301, 1536, device=cuda))
+    assert torch.equal(back.cpu(), x.bfloat16().float())
+    gamma = 1 + 0.1 * torch.randn(1536, generator=g)
+    y = ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5)
+    assert max_rel(y, orf.rms_norm(x, gamma, 1e-5)) < 1e-2
+
+
 # ----------------------------------------------------------------------------- glue
 def test_rmsnorm_modulate(cuda):
     from sa3_b200 import ops
