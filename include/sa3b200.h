@@ -159,15 +159,32 @@ int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, int ngroups, 
  * a negative wl / wr means unbounded on that side.
  * Sequences: if cu_seqlens_q is NULL, sequence b has rows [b*Lq, (b+1)*Lq)
  * (same for k with Lk); otherwise rows [cu[b], cu[b+1]) (int32, device).
- * q, k, v, q2, k2, out are token-row buffers with the given row strides;
- * head h sits at columns h*64 of each. q2/k2 NULL = not differential.
- * dtype: SA3_DT_BF16 (or SA3_DT_F16). head_dim must be 64.
+ * q, k, v, q2, k2, v2, out are token-row buffers with the given row strides;
+ * head h sits at columns h*64 of each. q2/k2 NULL = not differential;
+ * v2 NULL = the second stream reuses v (the DiT's differential attention),
+ * otherwise it reads its own values (the SAME-L plugin op below).
+ * dtype: SA3_DT_BF16 or SA3_DT_F16 (operands, P and output). head_dim must be 64.
+ * amax_out (optional): atomic max of |stored output| for a following FP8 quantisation.
  */
-int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2, void* out,
+int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2, const void* v2,
+                  void* out,
                   const int* cu_seqlens_q, const int* cu_seqlens_k, int batch, int max_seqlen_q, int max_seqlen_k,
                   int total_q, int total_k, int heads, int head_dim, long long ldq, long long ldk, long long ldv,
                   long long ldo, int window_left, int window_right, float softmax_scale, int dtype,
                   float* amax_out, void* stream);
+
+/* ---------------------------------------------- SWA plugin op (a15, f3)
+ *
+ * The operator of the TensorRT plugin samel::diff_attn_swa
+ * (optimized/tensorRT/scripts/diff_attn_nocast_plugin.py:14-41, kernel
+ * triton_swa_v2.py:94-119): q_bat, k_bat, v_bat are [B, N, 2H, d] with the two
+ * differential streams stacked on the head axis; out [B, N, H, d] =
+ * attn(heads 0..H-1) - attn(heads H..2H-1), each with its own q/k/v, window
+ * |i - j| <= window, scale d^-1/2. Writes into the caller-owned out on stream.
+ * dtype SA3_DT_BF16 or SA3_DT_F16 (fp32 callers convert first).
+ */
+int sa3_diff_attn_swa(const void* q_bat, const void* k_bat, const void* v_bat, void* out, int dtype, int batch,
+                      int seqlen, int num_heads, int head_dim, int window, void* stream);
 
 #ifdef __cplusplus
 }

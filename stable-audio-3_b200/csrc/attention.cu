@@ -36,6 +36,7 @@ constexpr int ATT_SMEM = ATT_TILE_BYTES * (1 + 2 + 1 + 2) + 1024 + 256;
 constexpr int ATT_TMEM_COLS = 256;
 
 struct AttnParams {
+  int f16;  // 1: fp16 operands / output, 0: bf16
   const int* cu_q;
   const int* cu_k;
   int Lq, Lk;  // uniform lengths when cu_q / cu_k are NULL
@@ -43,10 +44,18 @@ struct AttnParams {
   int wl, wr;
   float scale_log2;
   int npass;
-  __nv_bfloat16* out;
+  void* out;
   long long ldo;
   float* amax_out;
 };
+
+__device__ __forceinline__ uint32_t pack_2(float lo, float hi, bool f16) {
+  if (f16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  return pack_bf16x2(lo, hi);
+}
 
 __device__ __forceinline__ void att_issue(const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int col, int row) {
   mbar_arrive_expect_tx(bar, ATT_TILE_BYTES);
@@ -56,7 +65,8 @@ __device__ __forceinline__ void att_issue(const CUtensorMap* tm, uint8_t* dst, u
 __global__ void __launch_bounds__(128, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ2,
-                        const __grid_constant__ CUtensorMap tmK2, AttnParams p) {
+                        const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2,
+                        AttnParams p) {
   const int t = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int qs = p.cu_q ? __ldg(p.cu_q + b) : b * p.Lq;
   const int lq = p.cu_q ? __ldg(p.cu_q + b + 1) - qs : p.Lq;
@@ -101,6 +111,7 @@ __global__ void __launch_bounds__(128, 2)
     if (p.npass > 1) {
       tma_prefetch_desc(&tmQ2);
       tma_prefetch_desc(&tmK2);
+      tma_prefetch_desc(&tmV2);
     }
   }
   if (warp == 0) {
@@ -118,8 +129,9 @@ __global__ void __launch_bounds__(128, 2)
   const int i = i0 + tid;  // this thread's query row (sequence coordinate)
   const float NEG_INF = -INFINITY;
 
-  const uint32_t idesc_s = make_idesc(128, 128, 1, 1, 0, 0);
-  const uint32_t idesc_o = make_idesc(128, 64, 1, 1, 0, 1);
+  const int fmt = p.f16 ? 0 : 1;  // kind::f16 operand format: 0 = f16, 1 = bf16
+  const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
+  const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
 
   float o_prev[64];
   float o[64];
@@ -134,6 +146,7 @@ __global__ void __launch_bounds__(128, 2)
   for (int pass = 0; pass < p.npass; ++pass) {
     const CUtensorMap* tq = pass ? &tmQ2 : &tmQ;
     const CUtensorMap* tk = pass ? &tmK2 : &tmK;
+    const CUtensorMap* tv = pass ? &tmV2 : &tmV;
     float m_i = NEG_INF, l_i = 0.f;
 #pragma unroll
     for (int d = 0; d < 64; ++d) o[d] = 0.f;
@@ -144,7 +157,7 @@ __global__ void __launch_bounds__(128, 2)
       const int bf = gidx & 1;
       att_issue(tk, SK(bf), &bar_kv[bf], col, ks + j_lo);
       if (bf) ++kv_issued1; else ++kv_issued0;
-      att_issue(&tmV, sV, bar_v, col, ks + j_lo);  // previous P V retired (bar_o waited)
+      att_issue(tv, sV, bar_v, col, ks + j_lo);  // previous P V retired (bar_o waited)
       ++v_issued;
     }
 
@@ -210,10 +223,10 @@ __global__ void __launch_bounds__(128, 2)
         for (int q = 0; q < 4; ++q) {
           const int ch = ((c & 1) * 4 + q) ^ (tid & 7);
           uint4 u;
-          u.x = pack_bf16x2(pv[q * 8 + 0], pv[q * 8 + 1]);
-          u.y = pack_bf16x2(pv[q * 8 + 2], pv[q * 8 + 3]);
-          u.z = pack_bf16x2(pv[q * 8 + 4], pv[q * 8 + 5]);
-          u.w = pack_bf16x2(pv[q * 8 + 6], pv[q * 8 + 7]);
+          u.x = pack_2(pv[q * 8 + 0], pv[q * 8 + 1], p.f16);
+          u.y = pack_2(pv[q * 8 + 2], pv[q * 8 + 3], p.f16);
+          u.z = pack_2(pv[q * 8 + 4], pv[q * 8 + 5], p.f16);
+          u.w = pack_2(pv[q * 8 + 6], pv[q * 8 + 7], p.f16);
           *reinterpret_cast<uint4*>(rowbase + ch * 16) = u;
         }
       }
@@ -241,7 +254,7 @@ __global__ void __launch_bounds__(128, 2)
       tc_fence_after();
       if (tid == 0 && it + 1 < ntiles && !*abort_flag) {
         // sV is free once P V of this tile retired: refill it for the next tile.
-        att_issue(&tmV, sV, bar_v, col, ks + j0 + ATT_BN);
+        att_issue(tv, sV, bar_v, col, ks + j0 + ATT_BN);
         ++v_issued;
       }
       {
@@ -271,19 +284,21 @@ __global__ void __launch_bounds__(128, 2)
   // ---- store (row-major token rows, this head's 64 columns)
   float amax = 0.f;
   if (i <= i_last && !bad && !*abort_flag) {
-    __nv_bfloat16* dst = p.out + (long long)(qs + i) * p.ldo + col;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(qs + i) * p.ldo + col;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       uint4 u;
-      u.x = pack_bf16x2(o_prev[q * 8 + 0], o_prev[q * 8 + 1]);
-      u.y = pack_bf16x2(o_prev[q * 8 + 2], o_prev[q * 8 + 3]);
-      u.z = pack_bf16x2(o_prev[q * 8 + 4], o_prev[q * 8 + 5]);
-      u.w = pack_bf16x2(o_prev[q * 8 + 6], o_prev[q * 8 + 7]);
+      u.x = pack_2(o_prev[q * 8 + 0], o_prev[q * 8 + 1], p.f16);
+      u.y = pack_2(o_prev[q * 8 + 2], o_prev[q * 8 + 3], p.f16);
+      u.z = pack_2(o_prev[q * 8 + 4], o_prev[q * 8 + 5], p.f16);
+      u.w = pack_2(o_prev[q * 8 + 6], o_prev[q * 8 + 7], p.f16);
       reinterpret_cast<uint4*>(dst)[q] = u;
     }
     if (p.amax_out) {
 #pragma unroll
-      for (int d = 0; d < 64; ++d) amax = fmaxf(amax, fabsf(__bfloat162float(__float2bfloat16(o_prev[d]))));
+      for (int d = 0; d < 64; ++d)
+        amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o_prev[d]))
+                                       : __bfloat162float(__float2bfloat16(o_prev[d]))));
     }
   }
   if (p.amax_out) {
@@ -309,7 +324,8 @@ __global__ void __launch_bounds__(128, 2)
 
 using namespace sa3;
 
-extern "C" int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2, void* out,
+extern "C" int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2,
+                             const void* v2, void* out,
                              const int* cu_seqlens_q, const int* cu_seqlens_k, int batch, int max_seqlen_q,
                              int max_seqlen_k, int total_q, int total_k, int heads, int head_dim, long long ldq,
                              long long ldk, long long ldv, long long ldo, int window_left, int window_right,
@@ -317,8 +333,9 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   if (!q || !k || !v || !out || batch <= 0 || heads <= 0 || max_seqlen_q <= 0 || max_seqlen_k <= 0)
     return SA3_ERR_ARG;
   if (head_dim != 64) return SA3_ERR_UNSUPPORTED;
-  if (dtype != SA3_DT_BF16) return SA3_ERR_DTYPE;
+  if (dtype != SA3_DT_BF16 && dtype != SA3_DT_F16) return SA3_ERR_DTYPE;
   if ((q2 == nullptr) != (k2 == nullptr)) return SA3_ERR_ARG;
+  if (v2 && !q2) return SA3_ERR_ARG;
   if ((cu_seqlens_q == nullptr) != (cu_seqlens_k == nullptr)) return SA3_ERR_ARG;
   if (!cu_seqlens_q) {
     total_q = batch * max_seqlen_q;
@@ -330,8 +347,8 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   if (!aligned16(out) || (ldo % 8)) return SA3_ERR_ALIGN;
   if (batch > 65535 || heads > 65535) return SA3_ERR_UNSUPPORTED;
 
-  CUtensorMap mq, mk, mv, mq2, mk2;
-  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap mq, mk, mv, mq2, mk2, mv2;
+  const auto dt = dtype == SA3_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int rc;
   if ((rc = make_tmap_2d(&mq, q, dt, 2, width, total_q, ldq, 64, 128))) return rc;
   if ((rc = make_tmap_2d(&mk, k, dt, 2, width, total_k, ldk, 64, 128))) return rc;
@@ -343,7 +360,13 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
     mq2 = mq;
     mk2 = mk;
   }
+  if (v2) {
+    if ((rc = make_tmap_2d(&mv2, v2, dt, 2, width, total_k, ldv, 64, 128))) return rc;
+  } else {
+    mv2 = mv;
+  }
   AttnParams p;
+  p.f16 = dtype == SA3_DT_F16;
   p.cu_q = cu_seqlens_q;
   p.cu_k = cu_seqlens_k;
   p.Lq = max_seqlen_q;
@@ -353,12 +376,27 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   p.wr = window_right;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.npass = q2 ? 2 : 1;
-  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.out = out;
   p.ldo = ldo;
   p.amax_out = amax_out;
   dim3 grid((max_seqlen_q + ATT_BM - 1) / ATT_BM, heads, batch);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
-  attention_tc_kernel<<<grid, 128, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, p);
+  attention_tc_kernel<<<grid, 128, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p);
   return launch_status();
+}
+
+extern "C" int sa3_diff_attn_swa(const void* q_bat, const void* k_bat, const void* v_bat, void* out, int dtype,
+                                 int batch, int seqlen, int num_heads, int head_dim, int window, void* stream) {
+  // q/k/v_bat: [B, N, 2H, d] (stream 1 = heads 0..H-1, stream 2 = heads H..2H-1); out: [B, N, H, d].
+  if (!q_bat || !k_bat || !v_bat || !out || batch <= 0 || seqlen <= 0 || num_heads <= 0) return SA3_ERR_ARG;
+  if (head_dim != 64) return SA3_ERR_UNSUPPORTED;
+  const size_t esz = 2;
+  const long long hw = (long long)num_heads * head_dim;  // elements of one stream's heads in a row
+  const char* q = static_cast<const char*>(q_bat);
+  const char* k = static_cast<const char*>(k_bat);
+  const char* v = static_cast<const char*>(v_bat);
+  return sa3_attention(q, k, v, q + hw * esz, k + hw * esz, v + hw * esz, out, nullptr, nullptr, batch, seqlen,
+                       seqlen, batch * seqlen, batch * seqlen, num_heads, head_dim, 2 * hw, 2 * hw, 2 * hw, hw,
+                       window, window, 1.0f / sqrtf((float)head_dim), dtype, nullptr, stream);
 }

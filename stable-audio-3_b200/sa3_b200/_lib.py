@@ -63,8 +63,9 @@ SIGNATURES = {
     "sa3_quantize_e4m3": [c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_vp, c_vp, c_vp],
     "sa3_qk_norm_rope": [c_vp, c_int, c_ll, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_vp),
                          ctypes.POINTER(c_int), c_float, c_vp, c_int, c_int, c_vp, c_vp],
-    "sa3_attention": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int,
-                      c_int, c_ll, c_ll, c_ll, c_ll, c_int, c_int, c_float, c_int, c_vp, c_vp],
+    "sa3_attention": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
+                      c_int, c_int, c_ll, c_ll, c_ll, c_ll, c_int, c_int, c_float, c_int, c_vp, c_vp],
+    "sa3_diff_attn_swa": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp],
 }
 
 _lib = None

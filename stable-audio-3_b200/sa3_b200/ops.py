@@ -190,14 +190,14 @@ def rope_table(max_pos: int, rot_dim: int = 32, base: float = 10000.0, device="c
 
 
 # ---------------------------------------------------------------------- attention
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, q2=None, k2=None,
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, q2=None, k2=None, v2=None,
               cu_seqlens_q=None, cu_seqlens_k=None, batch: int = 1, max_seqlen_q: int = 0, max_seqlen_k: int = 0,
               window=(-1, -1), softmax_scale: Optional[float] = None, out=None, amax_out=None) -> torch.Tensor:
     """Windowed / full attention on token-row views (head h at columns h*64); differential if q2/k2 given.
 
     Without cu_seqlens the rows are `batch` sequences of max_seqlen_q (q) / max_seqlen_k (k) tokens.
     """
-    _need_cuda(q, k, v, q2, k2, cu_seqlens_q, cu_seqlens_k, out, amax_out)
+    _need_cuda(q, k, v, q2, k2, v2, cu_seqlens_q, cu_seqlens_k, out, amax_out)
     total_q, total_k = q.shape[0], k.shape[0]
     if out is None:
         out = torch.empty(total_q, heads * 64, device=q.device, dtype=q.dtype)
@@ -213,9 +213,27 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads: int, 
             raise RuntimeError("cu_seqlens must be int32")
     wl, wr = (int(window[0]), int(window[1]))
     _count()
-    rc = _lib.load().sa3_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q2), _ptr(k2), out.data_ptr(),
+    rc = _lib.load().sa3_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(q2), _ptr(k2), _ptr(v2),
+                                   out.data_ptr(),
                                    _ptr(cu_seqlens_q), _ptr(cu_seqlens_k), batch_n, max_seqlen_q, max_seqlen_k,
                                    total_q, total_k, heads, 64, _row_stride(q), _row_stride(k), _row_stride(v),
                                    _row_stride(out), wl, wr, float(softmax_scale), _dt(q), _ptr(amax_out), _stream())
     _lib.check(rc, "sa3_attention")
+    return out
+
+
+def diff_attn_swa(q_bat: torch.Tensor, k_bat: torch.Tensor, v_bat: torch.Tensor, num_heads: int, window: int,
+                  out: torch.Tensor) -> torch.Tensor:
+    """SAME-L plugin operator: out[B,N,H,d] = attn(heads :H) - attn(heads H:) with window +-`window`."""
+    _need_cuda(q_bat, k_bat, v_bat, out)
+    B, N, H2, d = q_bat.shape
+    for t in (q_bat, k_bat, v_bat, out):
+        if not t.is_contiguous():
+            raise RuntimeError("diff_attn_swa needs contiguous [B, N, heads, d] tensors")
+    if H2 != 2 * num_heads or tuple(out.shape) != (B, N, num_heads, d):
+        raise RuntimeError("q_bat must stack 2*num_heads heads and out must be [B, N, num_heads, d]")
+    _count()
+    rc = _lib.load().sa3_diff_attn_swa(q_bat.data_ptr(), k_bat.data_ptr(), v_bat.data_ptr(), out.data_ptr(),
+                                       _dt(q_bat), B, N, num_heads, d, int(window), _stream())
+    _lib.check(rc, "sa3_diff_attn_swa")
     return out

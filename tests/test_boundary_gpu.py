@@ -1,0 +1,129 @@
+"""The reference-facing operator API on a B200 vs the CPU oracle.
+
+* flash_attn_func / flash_attn_varlen_func shims (the calls of Attention.apply_attn,
+  stable_audio_3/models/transformer.py:641-666): max|out-ref|/max|ref| <= 1e-2 (bf16; fp16 the same).
+* samel::diff_attn_swa plugin operator (diff_attn_nocast_plugin.py:22-41): same bound.
+* QuantLinearFP8 (nn.Linear drop-in): relative Frobenius <= 2e-2 vs the FP8 definition (asserted 5e-3).
+"""
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle import ref as orf
+
+pytestmark = pytest.mark.gpu
+
+
+def max_rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).abs().max() / b.abs().max()).item()
+
+
+def _bhnd(x):  # [B, N, H, d] -> [B, H, N, d] fp32 cpu
+    return x.float().cpu().permute(0, 2, 1, 3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,Nq,Nk,H,window,causal", [(2, 646, 646, 4, (256, 256), False),
+                                                     (1, 300, 300, 2, (-1, -1), True),
+                                                     (1, 200, 333, 2, (-1, -1), False),
+                                                     (1, 257, 257, 3, (17, 17), False)])
+def test_flash_attn_func_shim(cuda, dtype, B, Nq, Nk, H, window, causal):
+    from sa3_b200.flash_shim import flash_attn_func
+
+    g = torch.Generator().manual_seed(Nq + H)
+    q = torch.randn(B, Nq, H, 64, generator=g).to(dtype)
+    k = torch.randn(B, Nk, H, 64, generator=g).to(dtype)
+    v = torch.randn(B, Nk, H, 64, generator=g).to(dtype)
+    out = flash_attn_func(q.to(cuda), k.to(cuda), v.to(cuda), causal=causal, window_size=window)
+    assert out.dtype == dtype and out.shape == q.shape
+    wl, wr = window
+    if causal:
+        wr = 0
+    ref = orf.attention(_bhnd(q), _bhnd(k), _bhnd(v), wl, wr)
+    assert max_rel(_bhnd(out), ref) < 1e-2
+
+
+def test_flash_attn_shim_accepts_apply_attn_layout(cuda):
+    """apply_attn rearranges [B,H,N,d] -> [B,N,H,d] (a non-contiguous view) before the call."""
+    from sa3_b200.flash_shim import flash_attn_func
+
+    g = torch.Generator().manual_seed(1)
+    qh, kh, vh = (torch.randn(1, 4, 300, 64, generator=g).bfloat16() for _ in range(3))
+    out = flash_attn_func(*(t.to(cuda).permute(0, 2, 1, 3) for t in (qh, kh, vh)), window_size=(64, 64))
+    ref = orf.attention(qh.float(), kh.float(), vh.float(), 64, 64)
+    assert max_rel(_bhnd(out), ref) < 1e-2
+
+
+def test_flash_attn_varlen_shim(cuda):
+    from sa3_b200.flash_shim import flash_attn_varlen_func, index_first_axis, pad_input
+
+    g = torch.Generator().manual_seed(2)
+    lens = [130, 64, 400]
+    H = 2
+    cu = torch.tensor([0, 130, 194, 594], dtype=torch.int32)
+    q, k, v = (torch.randn(594, H, 64, generator=g).bfloat16() for _ in range(3))
+    out = flash_attn_varlen_func(q.to(cuda), k.to(cuda), v.to(cuda), cu.to(cuda), cu.to(cuda), 400, 400,
+                                 window_size=(32, 32))
+    for i, L in enumerate(lens):
+        s, e = int(cu[i]), int(cu[i + 1])
+        hh = lambda t: t[s:e].float().cpu().permute(1, 0, 2)[None]  # noqa: E731
+        ref = orf.attention(hh(q), hh(k), hh(v), 32, 32)
+        assert max_rel(hh(out), ref) < 1e-2
+    # bert_padding helpers round-trip
+    mask = torch.zeros(3, 400, dtype=torch.bool)
+    for i, L in enumerate(lens):
+        mask[i, :L] = True
+    idx = torch.nonzero(mask.flatten()).flatten().to(cuda)
+    x = torch.randn(3, 400, 8, device=cuda)
+    packed = index_first_axis(x.view(1200, 8), idx)
+    back = pad_input(packed, idx, 3, 400)
+    assert torch.equal(back[mask.to(cuda)], x[mask.to(cuda)])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_diff_attn_swa_plugin(cuda, dtype):
+    from sa3_b200.plugin import diff_attn_swa, diff_attn_swa_shape
+
+    g = torch.Generator().manual_seed(4)
+    B, N, H = 1, 1836, 24
+    qb, kb, vb = (torch.randn(B, N, 2 * H, 64, generator=g).to(dtype) for _ in range(3))
+    out = diff_attn_swa(qb.to(cuda), kb.to(cuda), vb.to(cuda), H)
+    assert tuple(out.shape) == diff_attn_swa_shape(qb.shape) and out.dtype == dtype
+    x = lambda t: _bhnd(t.bfloat16())  # noqa: E731  (the kernel computes from bf16 operands)
+    ref = (orf.attention(x(qb)[:, :H], x(kb)[:, :H], x(vb)[:, :H], 17, 17)
+           - orf.attention(x(qb)[:, H:], x(kb)[:, H:], x(vb)[:, H:], 17, 17))
+    assert max_rel(_bhnd(out), ref) < 1e-2
+
+
+def test_quant_linear_fp8(cuda):
+    from torch import nn
+
+    from sa3_b200.quant import QuantLinearFP8
+
+    g = torch.Generator().manual_seed(5)
+    lin = nn.Linear(1536, 2048)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(2048, 1536, generator=g) * 0.02)
+        lin.bias.copy_(torch.randn(2048, generator=g) * 0.1)
+    q = QuantLinearFP8.from_linear(lin, device=cuda)
+    x = torch.randn(3, 333, 1536, generator=g).bfloat16()
+    y = q(x.to(cuda))
+    assert y.shape == (3, 333, 2048)
+    wq, sw = oq.quantize_weight_e4m3(lin.weight.detach())
+    ref = oq.fp8_linear(x.float().reshape(-1, 1536), wq, sw, lin.bias.detach()).reshape(3, 333, 2048)
+    err = ((y.float().cpu() - ref).norm() / ref.norm()).item()
+    assert err < 5e-3
+
+
+def test_quantize_linears_walk(cuda):
+    from sa3_b200.modules import DiTConfig, TransformerBlock
+    from sa3_b200.quant import QuantLinearFP8, quantize_linears_fp8
+
+    blk = TransformerBlock(DiTConfig(embed_dim=256, num_heads=4, depth=1))
+    quantize_linears_fp8(blk)
+    kinds = {n: type(m).__name__ for n, m in blk.named_modules()}
+    for n in ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_kv", "ff.ff.0.proj",
+              "ff.ff.2"):
+        assert kinds[n] == QuantLinearFP8.__name__, n
+    assert kinds["to_local_embed.0"] == "Linear"
