@@ -1,0 +1,131 @@
+"""Per-kernel timing at the medium DiT shapes (CUDA events, after warm-up), also used as the
+bounded workload for ncu captures of a single kernel.
+
+  PYTHONPATH=stable-audio-3_b200 python -m sa3_b200.kernel_bench [--case NAME[,NAME]|all] [--iters N]
+
+Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
+  ff1_fp8    GLU.proj    FP8 GEMM  M x 12288 x 1536, SwiGLU epilogue
+  qkv_fp8    to_qkv      FP8 GEMM  M x 7680 x 1536
+  ff2_fp8    linear_out  FP8 GEMM  M x 1536 x 6144, gate + fp32 residual epilogue
+  out_fp8    to_out      FP8 GEMM  M x 1536 x 1536, gate + fp32 residual epilogue
+  attn_diff  differential SWA, 24 heads, window (256, 256)
+  attn_cross differential cross-attention over 128 context tokens
+  norm_fp8   RMSNorm + modulate of the fp32 stream: amax pass + e4m3 write pass
+  qknorm     qk RMSNorm + RoPE on q, k, q_diff, k_diff in place
+Each case's operands exceed the 126 MB L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib, ops
+from .quant import interleave_swiglu_rows, quantize_weight_e4m3
+
+B, L, NM, D, H = 2, 8183, 64, 1536, 24
+N = L + NM
+M = B * N
+
+
+def _time(fn, iters: int, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _fp8_weight(n, k, dev, g):
+    wq, s = quantize_weight_e4m3(torch.randn(n, k, generator=g) * 0.02)
+    return wq, s
+
+
+def case(name: str, iters: int) -> dict:
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(0)
+    one = torch.ones(1, device=dev)
+    if name in ("ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8"):
+        n, k = {"ff1_fp8": (12288, 1536), "qkv_fp8": (7680, 1536), "ff2_fp8": (1536, 6144),
+                "out_fp8": (1536, 1536)}[name]
+        a = torch.randn(M, k, device=dev).to(torch.float8_e4m3fn)
+        wq, s = _fp8_weight(n, k, dev, g)
+        if name == "ff1_fp8":
+            w8, s = interleave_swiglu_rows(wq.view(torch.uint8), s)
+            wq = w8.view(torch.float8_e4m3fn)
+        wq, s = wq.to(dev), s.to(dev)
+        if name == "ff1_fp8":
+            out = torch.empty(M, n // 2, device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s, kind=_lib.EPI_SWIGLU)  # noqa: E731
+        elif name == "qkv_fp8":
+            out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s)  # noqa: E731
+        else:
+            h = torch.randn(M, n, device=dev)
+            gate = torch.randn(B, n, device=dev)
+            fn = lambda: ops.gemm(a, wq, h, a_scale=one, b_scale=s, kind=_lib.EPI_GATED_RESIDUAL,  # noqa: E731
+                                  residual=h, gate=gate, rows_per_batch=N)
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "tflops": 2.0 * M * n * k / ms / 1e9}
+    if name == "attn_diff":
+        qkv = torch.randn(M, 5 * D, device=dev).bfloat16()
+        q, k, v, q2, k2 = (qkv[:, i * D:(i + 1) * D] for i in range(5))
+        fn = lambda: ops.attention(q, k, v, q2=q2, k2=k2, heads=H, batch=B, max_seqlen_q=N,  # noqa: E731
+                                   max_seqlen_k=N, window=(256, 256))
+        pairs = N * 513 - 256 * 257
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "tflops": 4.0 * 64 * pairs * H * 2 * B / ms / 1e9}
+    if name == "attn_cross":
+        q = torch.randn(M, 2 * D, device=dev).bfloat16()
+        kv = torch.randn(B * 128, 3 * D, device=dev).bfloat16()
+        fn = lambda: ops.attention(q[:, :D], kv[:, :D], kv[:, 2 * D:], q2=q[:, D:], k2=kv[:, D:2 * D],  # noqa
+                                   heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=128)
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "tflops": 4.0 * 64 * N * 128 * H * 2 * B / ms / 1e9}
+    if name == "norm_fp8":
+        x = torch.randn(M, D, device=dev)
+        gam = torch.ones(D, device=dev)
+        mod = torch.randn(B, 6 * D, device=dev) * 0.1
+        am = torch.zeros(1, device=dev)
+        sc = torch.zeros(1, device=dev)
+        out = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn)
+
+        def fn():
+            ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, amax_only=am)
+            ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, out=out,
+                                 quant_amax=am, scale_out=sc)
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "GBps": (2 * M * D * 4 + M * D) / ms / 1e6}
+    if name == "qknorm":
+        qkv = torch.randn(M, 5 * D, device=dev).bfloat16()
+        gam = torch.ones(64, device=dev)
+        tab = ops.rope_table(N, device=dev)
+        fn = lambda: ops.qk_norm_rope(qkv, H, [0, D, 3 * D, 4 * D], [gam] * 4, [True] * 4, 1e-6, tab,  # noqa
+                                      rows_per_batch=N)
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "GBps": 2 * M * 4 * D * 2 / ms / 1e6}
+    raise ValueError(name)
+
+
+CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "attn_diff", "attn_cross", "norm_fp8", "qknorm"]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all")
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    names = CASES if args.case == "all" else args.case.split(",")
+    for n in names:
+        print(json.dumps(case(n, args.iters)), flush=True)
+    print(json.dumps({"device_error": _lib.device_error()}))
+
+
+if __name__ == "__main__":
+    main()
