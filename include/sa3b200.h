@@ -173,6 +173,30 @@ int sa3_attention(const void* q, const void* k, const void* v, const void* q2, c
                   long long ldo, int window_left, int window_right, float softmax_scale, int dtype,
                   float* amax_out, void* stream);
 
+/* ---------------------------------------------- allocation-free FP8 linear
+ *
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory, such as a TensorRT plugin's enqueue (TensorRT
+ * plans all memory ahead and an enqueue must not allocate), or a host with a
+ * fixed device-memory budget that cannot risk the implicit device
+ * synchronisation of cudaMalloc mid-stream.
+ *
+ * out[M, N] (bf16) = (e4m3(x / s_x) * s_x) . (w * w_scale[n])^T + bias[n], i.e.
+ * the same FP8 linear as sa3_quantize_e4m3 (max|x| pass, quantise pass) followed
+ * by sa3_gemm, but its scratch (max|x|, s_x and the M*K-byte e4m3 copy of x)
+ * lives in a file-scope device array of 16 MiB, so the call allocates nothing.
+ * x: bf16 [M, K] (row stride ldx); w: e4m3 [N, K] (ldw); w_scale fp32 [N]
+ * (or NULL); bias fp32 [N] (or NULL); K a multiple of 16.
+ * Limit: M * K <= SA3_FP8_NOALLOC_MAX_ELEMS, else SA3_ERR_UNSUPPORTED with
+ * nothing launched. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream
+ * capture. The array is shared by every call and keeps the last call's
+ * contents; calls that overlap on the GPU race on it.
+ */
+#define SA3_FP8_NOALLOC_MAX_ELEMS ((16LL << 20) - 256)
+int sa3_fp8_linear_noalloc(const void* x, const void* w, const float* w_scale, const float* bias, void* out, int M,
+                           int N, int K, long long ldx, long long ldw, long long ldo, void* stream);
+
 /* ---------------------------------------------- SWA plugin op (a15, f3)
  *
  * The operator of the TensorRT plugin samel::diff_attn_swa

@@ -66,6 +66,7 @@ SIGNATURES = {
     "sa3_attention": [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int,
                       c_int, c_int, c_ll, c_ll, c_ll, c_ll, c_int, c_int, c_float, c_int, c_vp, c_vp],
     "sa3_diff_attn_swa": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp],
+    "sa3_fp8_linear_noalloc": [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_ll, c_vp],
 }
 
 _lib = None
