@@ -322,6 +322,301 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 1) tmem_dealloc(tmem, GEMM_TMEM_COLS);
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// Persistent variant: one CTA per SM walks output tiles (n fastest) with a static stride.
+//   warp 0 / lane 0 : TMA producer over a STAGES-deep ring that runs on across tiles.
+//   warp 1 / lane 0 : MMA issuer; the accumulator alternates between two 256-column TMEM
+//                     buffers, so tile i+1's main loop overlaps tile i's epilogue.
+//   warps 2..9      : epilogue; warp w reads TMEM lane quarter w % 4 and column half (w - 2) / 4,
+//                     vectorised loads of per-column scale / bias / gate, 16-byte stores.
+// Requirements (checked on the host): N % 32 == 0 (N % 256 for SwiGLU), 16-byte aligned C,
+// residual, b_scale, bias and gate rows.
+constexpr int PG_THREADS = 320;
+constexpr int PG_EPI_WARPS = 8;
+constexpr int PG_TMEM_COLS = 512;
+constexpr int PG_SMEM = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+__device__ __forceinline__ void ldg_f32x32(const float* p, float (&v)[32]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 u = __ldg(q + i);
+    v[4 * i] = u.x;
+    v[4 * i + 1] = u.y;
+    v[4 * i + 2] = u.z;
+    v[4 * i + 3] = u.w;
+  }
+}
+
+// acc * sa * b_scale[n] + bias[n] for 32 columns starting at n (vectorised, no bounds checks).
+__device__ __forceinline__ void scale_bias32(float (&v)[32], int n, float sa, const float* b_scale,
+                                             const float* bias) {
+  if (b_scale) {
+    float s[32];
+    ldg_f32x32(b_scale + n, s);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= sa * s[i];
+  } else if (sa != 1.f) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= sa;
+  }
+  if (bias) {
+    float b[32];
+    ldg_f32x32(bias + n, b);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] += b[i];
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int orow, int batch, int nc, float (&v)[32],
+                                               float& amax) {
+  const sa3_epilogue& e = p.epi;
+  if (KIND == SA3_EPI_SILU) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = v[i] * fast_sigmoid(v[i]);
+  }
+  if (m >= p.M) return;
+  if (KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) {
+    float r[32];
+    if (e.c_f32)
+      load_f32x32(reinterpret_cast<const float*>(e.residual) + (long long)orow * e.ld_residual + nc, r);
+    else
+      load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(e.residual) + (long long)orow * e.ld_residual + nc, r);
+    if (KIND == SA3_EPI_GATED_RESIDUAL) {
+      float g[32];
+      ldg_f32x32(e.gate + (long long)batch * e.ld_gate + nc, g);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = r[i] + v[i] * fast_sigmoid(1.f - g[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += r[i];
+    }
+  }
+  if (e.c_f32) {
+    store_f32x32(reinterpret_cast<float*>(p.C) + (long long)orow * p.ldc + nc, v);
+    if (e.amax_out) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+  } else {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)orow * p.ldc + nc;
+    uint4* q = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 u;
+      u.x = pack_bf16x2(v[i * 8 + 0], v[i * 8 + 1]);
+      u.y = pack_bf16x2(v[i * 8 + 2], v[i * 8 + 3]);
+      u.z = pack_bf16x2(v[i * 8 + 4], v[i * 8 + 5]);
+      u.w = pack_bf16x2(v[i * 8 + 6], v[i * 8 + 7]);
+      q[i] = u;
+      if (e.amax_out) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+  }
+}
+
+template <bool FP8, int KIND>
+__global__ void __launch_bounds__(PG_THREADS, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           GemmParams p, int tiles_n, int num_tiles) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
+  uint64_t* empty = full + GEMM_STAGES;
+  uint64_t* acc_full = empty + GEMM_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr int BK = FP8 ? 128 : 64;
+  const int nkb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GEMM_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], PG_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, PG_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * GEMM_BM;
+        const int n0 = (t % tiles_n) * GEMM_BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % GEMM_STAGES;
+          if (it >= (uint32_t)GEMM_STAGES &&
+              !mbar_wait(&empty[s], ((it / GEMM_STAGES) - 1) & 1, abort_flag, 31))
+            break;
+          uint8_t* st = smem + s * GEMM_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], GEMM_STAGE_BYTES);
+          tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
+          tma_load_2d(st + GEMM_A_BYTES, &tmB, &full[s], kb * BK, n0);
+        }
+      }
+      if (*abort_flag) {
+        // Drain this thread's loads that may still be in flight before the CTA exits.
+        volatile int never = 0;
+        const uint32_t first = it > (uint32_t)GEMM_STAGES ? it - GEMM_STAGES : 0;
+        for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % GEMM_STAGES], (j / GEMM_STAGES) & 1, &never, 34);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(GEMM_BM, GEMM_BN, FP8 ? 0 : 1, FP8 ? 0 : 1, 0, 0);
+      uint32_t it = 0, lt = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const uint32_t a = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[a], ((lt >> 1) - 1) & 1, abort_flag, 32)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * GEMM_BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % GEMM_STAGES;
+          if (!mbar_wait(&full[s], (it / GEMM_STAGES) & 1, abort_flag, 33)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * GEMM_STAGE_BYTES);
+          const uint64_t ad = sdesc_kmajor_sw128(a_addr);
+          const uint64_t bd = sdesc_kmajor_sw128(a_addr + GEMM_A_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (FP8)
+              mma_f8_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            else
+              mma_f16_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          }
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[a]);
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // column half of the tile
+    const sa3_epilogue& e = p.epi;
+    const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
+    float amax = 0.f;
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
+      const uint32_t a = lt & 1;
+      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 35)) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * GEMM_BM;
+      const int n0 = (t % tiles_n) * GEMM_BN;
+      const int m = m0 + q * 32 + lane;
+      const int orow = out_row_of(e, m < p.M ? m : p.M - 1);
+      int batch = 0;
+      if (KIND == SA3_EPI_GATED_RESIDUAL && m < p.M)
+        batch = e.row_batch ? __ldg(e.row_batch + m) : m / e.rows_per_batch;
+      const uint32_t trow = tmem + a * GEMM_BN + ((uint32_t)(q * 32) << 16);
+      if (KIND == SA3_EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int col = half * 64 + c * 32;
+          float x[32], g[32];
+          tmem_ld32(trow + col, x);
+          tmem_ld32(trow + 128 + col, g);
+          scale_bias32(x, n0 + col, sa, p.b_scale, e.bias);
+          scale_bias32(g, n0 + 128 + col, sa, p.b_scale, e.bias);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = x[i] * g[i] * fast_sigmoid(g[i]);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int col = half * 128 + c * 32;
+          const int nc = n0 + col;
+          if (nc >= p.N) break;  // uniform per warp
+          float v[32];
+          tmem_ld32(trow + col, v);
+          scale_bias32(v, nc, sa, p.b_scale, e.bias);
+          pg_store_chunk<KIND>(p, m, orow, batch, nc, v, amax);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+    if (e.amax_out) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) atomic_max_nonneg(e.amax_out, amax);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, PG_TMEM_COLS);
+}
+
+template <bool FP8>
+static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int kind,
+                             cudaStream_t st) {
+  const int tiles_n = (p.N + GEMM_BN - 1) / GEMM_BN;
+  const int tiles_m = (p.M + GEMM_BM - 1) / GEMM_BM;
+  const int num_tiles = tiles_n * tiles_m;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  int rc;
+#define SA3_PG_CASE(K)                                                                                   \
+  case K:                                                                                                \
+    if ((rc = ensure_smem(gemm_persistent_kernel<FP8, K>, PG_SMEM))) return rc;                          \
+    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, p, tiles_n, num_tiles); \
+    break;
+  switch (kind) {
+    SA3_PG_CASE(SA3_EPI_STORE)
+    SA3_PG_CASE(SA3_EPI_SILU)
+    SA3_PG_CASE(SA3_EPI_SWIGLU)
+    SA3_PG_CASE(SA3_EPI_GATED_RESIDUAL)
+    SA3_PG_CASE(SA3_EPI_RESIDUAL)
+    default:
+      return SA3_ERR_ARG;
+  }
+#undef SA3_PG_CASE
+  return launch_status();
+}
+
 }  // namespace sa3
 
 using namespace sa3;
@@ -379,9 +674,19 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   p.b_scale = b_scale;
   p.epi = e;
 
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // Fast path: persistent kernel with an overlapped, vectorised epilogue.
+  auto al16 = [](const void* q) { return q == nullptr || aligned16(q); };
+  const bool res_kind = e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL;
+  const int celt = e.c_f32 ? 4 : 2;
+  bool fast = (N % 32 == 0) && aligned16(C) && ((ldc * celt) % 16 == 0) && al16(b_scale) && al16(e.bias) &&
+              (e.kind != SA3_EPI_SWIGLU || N % GEMM_BN == 0);
+  if (res_kind) fast = fast && aligned16(e.residual) && ((e.ld_residual * celt) % 16 == 0);
+  if (e.kind == SA3_EPI_GATED_RESIDUAL) fast = fast && aligned16(e.gate) && (e.ld_gate % 4 == 0);
+  if (fast) return fp8 ? launch_persistent<true>(tmA, tmB, p, e.kind, st) : launch_persistent<false>(tmA, tmB, p, e.kind, st);
+
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);
   if (grid.y > 65535) return SA3_ERR_UNSUPPORTED;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (fp8) {
     if ((rc = ensure_smem(gemm_tc_kernel<true>, GEMM_SMEM))) return rc;
     gemm_tc_kernel<true><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
