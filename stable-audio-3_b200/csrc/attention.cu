@@ -4,25 +4,26 @@
 // (stable_audio_3/models/transformer.py:620-666, window_size=(wl, wr)) and its
 // math-equivalent fallbacks (_sliding_window_chunked_halo_sdpa :143-159,
 // _sliding_window_additive_mask :118-127), plus the differential combine
-// out - out_diff of Attention.forward (:790-795): both softmax passes run in
-// the same CTA and share the V tiles.
+// out - out_diff of Attention.forward (:790-795).
 //
-// One CTA = 128 query rows of one head of one sequence, 128 threads (thread i
-// owns query row i: its S row and O row live in TMEM lane i).
-//   * The key range is clipped to the window of the tile's queries
-//     ([i0 - wl, i1 + wr] intersected with the sequence), so key tiles that are
-//     fully masked are never loaded or multiplied; the two edge tiles are
-//     masked element-wise.
-//   * Thread 0 issues TMA and the tcgen05.mma ops: S = Q K^T (M=128, N=128,
-//     K=64) into TMEM columns [0,128); O_tile = P V (M=128, N=64, K=128) into
-//     columns [128,192). Q is loaded once per pass, K tiles are double-buffered
-//     (tile t+1 loads during tile t), and the single V buffer is refilled as
-//     soon as P V of the previous tile retires, overlapping the next S MMA and
-//     softmax. Shared memory: Q 16 KB + K 2x16 KB + V 16 KB + P 32 KB = 96 KB,
-//     so two CTAs (2 x 256 TMEM columns) share an SM.
-//   * Softmax is online in fp32 (exp2 domain). P is written to shared memory
-//     as bf16 in the 128-byte-swizzled K-major layout the MMA reads; V is used
-//     MN-major straight from its TMA tile.
+// Work unit = 128 query rows x one head x one softmax stream. A CTA runs two
+// units side by side: the two streams of a differential head (same rows; the
+// combine o1/l1 - o2/l2 happens on chip), or two consecutive query tiles of a
+// plain head. 384 threads, warp-specialised:
+//   warp 0 (lane 0)  TMA: Q once per unit, then K and V tiles, double-buffered.
+//   warp 1 (lane 0)  tcgen05.mma: S_u = Q_u K^T (M=128, N=128, K=64) into TMEM
+//                    columns [128u, 128u+128); O_u = P_u V (M=128, N=64, K=128)
+//                    into [256+64u, 256+64u+64).
+//   warps 4..7, 8..11  softmax warpgroup of unit 0 / unit 1; thread r owns query
+//                    row r (TMEM lane r). While one warpgroup runs its softmax the
+//                    tensor core works on the other unit's S and P V.
+// The key range of a unit is clipped to the window of its queries, so fully
+// masked key tiles are never loaded or multiplied; tiles that lie entirely
+// inside every row's band skip masking, edge tiles use one range test per
+// element. Online softmax in fp32 (exp2 domain); P is stored as bf16/fp16 in
+// the 128-byte-swizzled K-major layout the MMA reads, V is read MN-major
+// straight from its TMA tile; each O tile is accumulated in registers.
+// Shared memory: per unit Q 16 KB + K 2x16 KB + V 2x16 KB + P 32 KB = 112 KB.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -31,9 +32,11 @@ SA3_DEFINE_ERROR_READER(read_error_attention)
 
 constexpr int ATT_BM = 128;
 constexpr int ATT_BN = 128;
-constexpr int ATT_TILE_BYTES = 128 * 128;  // 128 rows x 64 bf16
-constexpr int ATT_SMEM = ATT_TILE_BYTES * (1 + 2 + 1 + 2) + 1024 + 256;
-constexpr int ATT_TMEM_COLS = 256;
+constexpr int ATT_TILE = 128 * 128;  // 128 rows x 64 16-bit elements
+constexpr int ATT_UNIT_TILES = 7;    // Q, K0, K1, V0, V1, P (2 tiles)
+constexpr int ATT_THREADS = 384;
+constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 512;
+constexpr int ATT_TMEM_COLS = 512;
 
 struct AttnParams {
   int f16;  // 1: fp16 operands / output, 0: bf16
@@ -43,11 +46,36 @@ struct AttnParams {
   int heads;
   int wl, wr;
   float scale_log2;
-  int npass;
+  int diff;  // differential: unit 1 = second stream of the same rows
   void* out;
   long long ldo;
   float* amax_out;
 };
+
+struct Unit {
+  int qs, ks, lq, lk, i0, dlt, j_lo, ntiles;
+  bool valid;
+};
+
+__device__ __forceinline__ Unit make_unit(const AttnParams& p, int b, int tile) {
+  Unit u;
+  u.qs = p.cu_q ? __ldg(p.cu_q + b) : b * p.Lq;
+  u.lq = p.cu_q ? __ldg(p.cu_q + b + 1) - u.qs : p.Lq;
+  u.ks = p.cu_k ? __ldg(p.cu_k + b) : b * p.Lk;
+  u.lk = p.cu_k ? __ldg(p.cu_k + b + 1) - u.ks : p.Lk;
+  u.i0 = tile * ATT_BM;
+  u.valid = u.i0 < u.lq;
+  u.dlt = u.lk - u.lq;
+  u.j_lo = 0;
+  u.ntiles = 0;
+  if (u.valid) {
+    const int i_last = min(u.i0 + ATT_BM, u.lq) - 1;
+    u.j_lo = p.wl < 0 ? 0 : max(0, u.i0 + u.dlt - p.wl);
+    const int j_hi = p.wr < 0 ? u.lk : min(u.lk, i_last + u.dlt + p.wr + 1);
+    u.ntiles = j_hi > u.j_lo ? (j_hi - u.j_lo + ATT_BN - 1) / ATT_BN : 0;
+  }
+  return u;
+}
 
 __device__ __forceinline__ uint32_t pack_2(float lo, float hi, bool f16) {
   if (f16) {
@@ -57,58 +85,43 @@ __device__ __forceinline__ uint32_t pack_2(float lo, float hi, bool f16) {
   return pack_bf16x2(lo, hi);
 }
 
-__device__ __forceinline__ void att_issue(const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int col, int row) {
-  mbar_arrive_expect_tx(bar, ATT_TILE_BYTES);
-  tma_load_2d(dst, tm, bar, col, row);
-}
-
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ2,
                         const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2,
                         AttnParams p) {
-  const int t = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int qs = p.cu_q ? __ldg(p.cu_q + b) : b * p.Lq;
-  const int lq = p.cu_q ? __ldg(p.cu_q + b + 1) - qs : p.Lq;
-  const int ks = p.cu_k ? __ldg(p.cu_k + b) : b * p.Lk;
-  const int lk = p.cu_k ? __ldg(p.cu_k + b + 1) - ks : p.Lk;
-  const int i0 = t * ATT_BM;
-  if (i0 >= lq) return;  // uniform per CTA, before any barrier / TMEM use
-  const int i_last = min(i0 + ATT_BM, lq) - 1;
-  const int dlt = lk - lq;
-  const int j_lo = p.wl < 0 ? 0 : max(0, i0 + dlt - p.wl);
-  const int j_hi = p.wr < 0 ? lk : min(lk, i_last + dlt + p.wr + 1);
-  const int ntiles = j_hi > j_lo ? (j_hi - j_lo + ATT_BN - 1) / ATT_BN : 0;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int tile0 = p.diff ? blockIdx.x : 2 * blockIdx.x;
+  Unit U[2];
+  U[0] = make_unit(p, b, tile0);
+  U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
+  if (!U[0].valid) return;  // uniform per CTA, before any barrier / TMEM use
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  // K tiles at smem + (1 + buf) * TILE.
-#define SK(bf) (smem + (1 + (bf)) * ATT_TILE_BYTES)
-  uint8_t* sV = smem + 3 * ATT_TILE_BYTES;
-  uint8_t* sP = smem + 4 * ATT_TILE_BYTES;  // two 16 KB K-major sub-tiles (kv 0..63, 64..127)
-  uint64_t* bar_q = reinterpret_cast<uint64_t*>(smem + 6 * ATT_TILE_BYTES);
-  uint64_t* bar_kv = bar_q + 1;  // [2]: K tiles
-  uint64_t* bar_s = bar_q + 3;
-  uint64_t* bar_o = bar_q + 4;
-  uint64_t* bar_v = bar_q + 5;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_q + 6);
+#define SQ(u) (smem + ((u) * ATT_UNIT_TILES + 0) * ATT_TILE)
+#define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + 1 + (s)) * ATT_TILE)
+#define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + 3 + (s)) * ATT_TILE)
+#define SP(u) (smem + ((u) * ATT_UNIT_TILES + 5) * ATT_TILE)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE);
+  uint64_t* q_full = bars;          // [2]
+  uint64_t* kv_full = bars + 2;     // [2][2]  (unit, buffer)
+  uint64_t* kv_empty = bars + 6;    // [2][2]
+  uint64_t* s_full = bars + 10;     // [2]
+  uint64_t* p_full = bars + 12;     // [2]  (4 arrivals: one per softmax warp)
+  uint64_t* o_full = bars + 14;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(bar_q, 1);
-    mbar_init(&bar_kv[0], 1);
-    mbar_init(&bar_kv[1], 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
-    mbar_init(bar_v, 1);
+    for (int i = 0; i < 16; ++i) mbar_init(&bars[i], (i == 12 || i == 13) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
-    if (p.npass > 1) {
+    if (p.diff) {
       tma_prefetch_desc(&tmQ2);
       tma_prefetch_desc(&tmK2);
       tma_prefetch_desc(&tmV2);
@@ -122,82 +135,139 @@ __global__ void __launch_bounds__(128, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's lanes, S columns
-  const uint32_t t_o = t_s + 128;                              // O columns
-
   const int col = h * 64;
-  const int i = i0 + tid;  // this thread's query row (sequence coordinate)
-  const float NEG_INF = -INFINITY;
+  const int jmax = max(U[0].ntiles, U[1].ntiles);
 
-  const int fmt = p.f16 ? 0 : 1;  // kind::f16 operand format: 0 = f16, 1 = bf16
-  const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
-  const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
-
-  float o_prev[64];
-  float o[64];
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued[2][2] = {{0, 0}, {0, 0}};
+      int q_issued[2] = {0, 0};
+      for (int u = 0; u < 2; ++u) {
+        if (U[u].ntiles == 0) continue;
+        const CUtensorMap* tq = (p.diff && u) ? &tmQ2 : &tmQ;
+        mbar_arrive_expect_tx(&q_full[u], ATT_TILE);
+        tma_load_2d(SQ(u), tq, &q_full[u], col, U[u].qs + U[u].i0);
+        q_issued[u] = 1;
+      }
+      for (int j = 0; j < jmax && !*abort_flag; ++j) {
+        for (int u = 0; u < 2; ++u) {
+          if (j >= U[u].ntiles) continue;
+          const int s = j & 1;
+          if (j >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((j >> 1) - 1) & 1, abort_flag, 40)) break;
+          const CUtensorMap* tk = (p.diff && u) ? &tmK2 : &tmK;
+          const CUtensorMap* tv = (p.diff && u) ? &tmV2 : &tmV;
+          const int row = U[u].ks + U[u].j_lo + j * ATT_BN;
+          mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
+          tma_load_2d(SK(u, s), tk, &kv_full[u * 2 + s], col, row);
+          tma_load_2d(SV(u, s), tv, &kv_full[u * 2 + s], col, row);
+          issued[u][s]++;
+        }
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        for (int u = 0; u < 2; ++u) {
+          if (q_issued[u]) mbar_wait(&q_full[u], 0, &never, 41);
+          for (int s = 0; s < 2; ++s)
+            if (issued[u][s]) mbar_wait(&kv_full[u * 2 + s], (issued[u][s] - 1) & 1, &never, 42);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int fmt = p.f16 ? 0 : 1;
+      const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
+      const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
+      bool ok = true;
+      for (int u = 0; u < 2 && ok; ++u) {
+        if (U[u].ntiles == 0) continue;
+        ok = mbar_wait(&q_full[u], 0, abort_flag, 43) && mbar_wait(&kv_full[u * 2], 0, abort_flag, 44);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+        const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, 0)));
 #pragma unroll
-  for (int d = 0; d < 64; ++d) o_prev[d] = 0.f;
-
-  uint32_t q_phase = 0;
-  int gidx = 0;  // global K/V tile counter across passes (buffer = gidx & 1)
-  int kv_issued0 = 0, kv_issued1 = 0, v_issued = 0;
-  bool bad = false;
-
-  for (int pass = 0; pass < p.npass; ++pass) {
-    const CUtensorMap* tq = pass ? &tmQ2 : &tmQ;
-    const CUtensorMap* tk = pass ? &tmK2 : &tmK;
-    const CUtensorMap* tv = pass ? &tmV2 : &tmV;
+        for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+        tc_commit(&s_full[u]);
+      }
+      for (int j = 0; j < jmax && ok; ++j) {
+        for (int u = 0; u < 2; ++u) {
+          if (j >= U[u].ntiles) continue;
+          const int s = j & 1;
+          if (!mbar_wait(&p_full[u], j & 1, abort_flag, 45)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t pd = sdesc_kmajor_sw128(smem_u32(SP(u) + (k >> 2) * ATT_TILE)) + 2 * (k & 3);
+            const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(SV(u, s)) + k * 2048, ATT_TILE);
+            mma_f16_ss(tmem + 256 + 64 * u, pd, vd, idesc_o, k != 0);
+          }
+          tc_commit(&o_full[u]);
+          tc_commit(&kv_empty[u * 2 + s]);
+          if (j + 1 < U[u].ntiles) {
+            const int s1 = (j + 1) & 1;
+            if (!mbar_wait(&kv_full[u * 2 + s1], ((j + 1) >> 1) & 1, abort_flag, 46)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+            const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, s1)));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+            tc_commit(&s_full[u]);
+          }
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int u = (warp - 4) >> 2;
+    const int wq = warp & 3;  // TMEM lane quarter
+    const int r = wq * 32 + lane;
+    const Unit un = u ? U[1] : U[0];
+    const int i = un.i0 + r;  // query row within its sequence
+    const uint32_t t_s = tmem + ((uint32_t)(wq * 32) << 16) + 128 * u;
+    const uint32_t t_o = tmem + ((uint32_t)(wq * 32) << 16) + 256 + 64 * u;
+    // visible keys of this row: [lo_j, hi_j) in sequence coordinates
+    const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
+    const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
+    const float NEG_INF = -INFINITY;
     float m_i = NEG_INF, l_i = 0.f;
+    float o[64];
 #pragma unroll
     for (int d = 0; d < 64; ++d) o[d] = 0.f;
+    bool bad = false;
+    uint8_t* prow = SP(u) + r * 128;
 
-    if (tid == 0 && ntiles > 0 && !*abort_flag) {
-      mbar_arrive_expect_tx(bar_q, ATT_TILE_BYTES);
-      tma_load_2d(sQ, tq, bar_q, col, qs + i0);
-      const int bf = gidx & 1;
-      att_issue(tk, SK(bf), &bar_kv[bf], col, ks + j_lo);
-      if (bf) ++kv_issued1; else ++kv_issued0;
-      att_issue(tv, sV, bar_v, col, ks + j_lo);  // previous P V retired (bar_o waited)
-      ++v_issued;
-    }
-
-    for (int it = 0; it < ntiles; ++it, ++gidx) {
-      const int bf = gidx & 1;
-      const uint32_t ph = (uint32_t)(gidx >> 1) & 1;
-      const int j0 = j_lo + it * ATT_BN;
-      if (tid == 0) {
-        if (it + 1 < ntiles && !*abort_flag) {
-          const int nb = (gidx + 1) & 1;
-          att_issue(tk, SK(nb), &bar_kv[nb], col, ks + j0 + ATT_BN);
-          if (nb) ++kv_issued1; else ++kv_issued0;
-        }
-        bool ok = true;
-        if (it == 0) ok = mbar_wait(bar_q, q_phase, abort_flag, 20);
-        ok = ok && mbar_wait(&bar_kv[bf], ph, abort_flag, 21);
-        if (ok) {
-          tc_fence_after();
-          const uint64_t qd = sdesc_kmajor_sw128(smem_u32(sQ));
-          const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(bf)));
-#pragma unroll
-          for (int k = 0; k < 4; ++k) mma_f16_ss(tmem, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
-        }
-        tc_commit(bar_s);
-      }
-      if (!mbar_wait(bar_s, (uint32_t)gidx & 1, abort_flag, 22)) bad = true;
+    for (int j = 0; j < un.ntiles; ++j) {
+      if (!mbar_wait(&s_full[u], j & 1, abort_flag, 47)) bad = true;
       tc_fence_after();
-
-      // ---- online softmax over this thread's row of S
+      const int j0 = un.j_lo + j * ATT_BN;
+      const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
+      // Same decision for the whole warp keeps the masked path rare: a tile is "full" for the
+      // warp when every row of the warp sees all 128 columns.
+      const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
+      const unsigned span = (unsigned)max(chi - max(clo, 0), 0);
+      const int cbeg = max(clo, 0);
       float mx = NEG_INF;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float sv[32];
         tmem_ld32(t_s + c * 32, sv);
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = j0 + c * 32 + e;
-          const int dj = j - i - dlt;
-          const bool valid = (j < j_hi) && (p.wl < 0 || dj >= -p.wl) && (p.wr < 0 || dj <= p.wr);
-          mx = valid ? fmaxf(mx, sv[e]) : mx;
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
+            mx = valid ? fmaxf(mx, sv[e]) : mx;
+          }
         }
       }
       const float m_new = fmaxf(m_i, mx * p.scale_log2);
@@ -209,115 +279,110 @@ __global__ void __launch_bounds__(128, 2)
         float sv[32];
         tmem_ld32(t_s + c * 32, sv);
         float pv[32];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = j0 + c * 32 + e;
-          const int dj = j - i - dlt;
-          const bool valid = (j < j_hi) && (p.wl < 0 || dj >= -p.wl) && (p.wr < 0 || dj <= p.wr);
-          pv[e] = valid ? fast_exp2(sv[e] * p.scale_log2 - m_use) : 0.f;
-          rowsum += pv[e];
+          for (int e = 0; e < 32; ++e) {
+            pv[e] = fast_exp2(fmaf(sv[e], p.scale_log2, -m_use));
+            rowsum += pv[e];
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
+            pv[e] = valid ? fast_exp2(fmaf(sv[e], p.scale_log2, -m_use)) : 0.f;
+            rowsum += pv[e];
+          }
         }
-        // Row `tid` of P: columns c*32.. in sub-tile c/2, 16-byte chunks (c%2)*4 + q.
-        uint8_t* rowbase = sP + (c >> 1) * ATT_TILE_BYTES + tid * 128;
+        uint8_t* rb = prow + (c >> 1) * ATT_TILE;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ch = ((c & 1) * 4 + q) ^ (tid & 7);
-          uint4 u;
-          u.x = pack_2(pv[q * 8 + 0], pv[q * 8 + 1], p.f16);
-          u.y = pack_2(pv[q * 8 + 2], pv[q * 8 + 3], p.f16);
-          u.z = pack_2(pv[q * 8 + 4], pv[q * 8 + 5], p.f16);
-          u.w = pack_2(pv[q * 8 + 6], pv[q * 8 + 7], p.f16);
-          *reinterpret_cast<uint4*>(rowbase + ch * 16) = u;
+        for (int qd = 0; qd < 4; ++qd) {
+          const int ch = ((c & 1) * 4 + qd) ^ (r & 7);
+          uint4 w;
+          w.x = pack_2(pv[qd * 8 + 0], pv[qd * 8 + 1], p.f16);
+          w.y = pack_2(pv[qd * 8 + 2], pv[qd * 8 + 3], p.f16);
+          w.z = pack_2(pv[qd * 8 + 4], pv[qd * 8 + 5], p.f16);
+          w.w = pack_2(pv[qd * 8 + 6], pv[qd * 8 + 7], p.f16);
+          *reinterpret_cast<uint4*>(rb + ch * 16) = w;
         }
       }
       l_i = l_i * alpha + rowsum;
       m_i = m_new;
-#pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] *= alpha;
-
       fence_proxy_async_smem();
       tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        if (mbar_wait(bar_v, (uint32_t)gidx & 1, abort_flag, 25)) {
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint64_t pd = sdesc_kmajor_sw128(smem_u32(sP + (k >> 2) * ATT_TILE_BYTES)) + 2 * (k & 3);
-            const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(sV) + k * 2048, ATT_TILE_BYTES);
-            mma_f16_ss(tmem + 128, pd, vd, idesc_o, k != 0);
-          }
-        }
-        tc_commit(bar_o);
-      }
-      if (!mbar_wait(bar_o, (uint32_t)gidx & 1, abort_flag, 23)) bad = true;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[u]);
+      if (!mbar_wait(&o_full[u], j & 1, abort_flag, 48)) bad = true;
       tc_fence_after();
-      if (tid == 0 && it + 1 < ntiles && !*abort_flag) {
-        // sV is free once P V of this tile retired: refill it for the next tile.
-        att_issue(tv, sV, bar_v, col, ks + j0 + ATT_BN);
-        ++v_issued;
-      }
       {
         float ov[32];
         tmem_ld32(t_o, ov);
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[d] += ov[d];
+        for (int d = 0; d < 32; ++d) o[d] = fmaf(o[d], alpha, ov[d]);
         tmem_ld32(t_o + 32, ov);
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[32 + d] += ov[d];
+        for (int d = 0; d < 32; ++d) o[32 + d] = fmaf(o[32 + d], alpha, ov[d]);
       }
       tc_fence_before();
     }
-    q_phase ^= 1;
     const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
-    if (pass == 0) {
 #pragma unroll
-      for (int d = 0; d < 64; ++d) o_prev[d] = o[d] * inv_l;
-    } else {
-#pragma unroll
-      for (int d = 0; d < 64; ++d) o_prev[d] -= o[d] * inv_l;
-    }
-    // Every thread must be done with sQ before thread 0 reloads it for the next pass.
-    __syncthreads();
-  }
+    for (int d = 0; d < 64; ++d) o[d] *= inv_l;
 
-  // ---- store (row-major token rows, this head's 64 columns)
-  float amax = 0.f;
-  if (i <= i_last && !bad && !*abort_flag) {
-    uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(qs + i) * p.ldo + col;
+    bool store = i < un.lq && !bad;
+    if (p.diff) {
+      // unit 1 hands o2 / l2 to unit 0 through its (now idle) P buffer, swizzled by 16-byte chunk.
+      float* xrow = reinterpret_cast<float*>(SP(1) + r * 256);
+      if (u == 1) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint4 u;
-      u.x = pack_2(o_prev[q * 8 + 0], o_prev[q * 8 + 1], p.f16);
-      u.y = pack_2(o_prev[q * 8 + 2], o_prev[q * 8 + 3], p.f16);
-      u.z = pack_2(o_prev[q * 8 + 4], o_prev[q * 8 + 5], p.f16);
-      u.w = pack_2(o_prev[q * 8 + 6], o_prev[q * 8 + 7], p.f16);
-      reinterpret_cast<uint4*>(dst)[q] = u;
+        for (int c = 0; c < 16; ++c)
+          reinterpret_cast<float4*>(xrow)[c ^ (r & 15)] =
+              make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (u == 0) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float4 w = reinterpret_cast<const float4*>(xrow)[c ^ (r & 15)];
+          o[4 * c] -= w.x;
+          o[4 * c + 1] -= w.y;
+          o[4 * c + 2] -= w.z;
+          o[4 * c + 3] -= w.w;
+        }
+      }
+      store = store && u == 0;
+    }
+    float amax = 0.f;
+    if (store && !*abort_flag) {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
+#pragma unroll
+      for (int qd = 0; qd < 8; ++qd) {
+        uint4 w;
+        w.x = pack_2(o[qd * 8 + 0], o[qd * 8 + 1], p.f16);
+        w.y = pack_2(o[qd * 8 + 2], o[qd * 8 + 3], p.f16);
+        w.z = pack_2(o[qd * 8 + 4], o[qd * 8 + 5], p.f16);
+        w.w = pack_2(o[qd * 8 + 6], o[qd * 8 + 7], p.f16);
+        reinterpret_cast<uint4*>(dst)[qd] = w;
+      }
+      if (p.amax_out) {
+#pragma unroll
+        for (int d = 0; d < 64; ++d)
+          amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o[d])) : __bfloat162float(__float2bfloat16(o[d]))));
+      }
     }
     if (p.amax_out) {
 #pragma unroll
-      for (int d = 0; d < 64; ++d)
-        amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o_prev[d]))
-                                       : __bfloat162float(__float2bfloat16(o_prev[d]))));
+      for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
+      if (lane == 0) atomic_max_nonneg(p.amax_out, amax);
     }
   }
-  if (p.amax_out) {
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
-    if ((tid & 31) == 0) atomic_max_nonneg(p.amax_out, amax);
-  }
 
-  // ---- teardown: drain any TMA still in flight after an abort, free TMEM.
-  if (tid == 0 && *abort_flag) {
-    volatile int never = 0;
-    if (kv_issued0 > 0) mbar_wait(&bar_kv[0], (uint32_t)(kv_issued0 - 1) & 1, &never, 24);
-    if (kv_issued1 > 0) mbar_wait(&bar_kv[1], (uint32_t)(kv_issued1 - 1) & 1, &never, 24);
-    if (v_issued > 0) mbar_wait(bar_v, (uint32_t)(v_issued - 1) & 1, &never, 26);
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, ATT_TMEM_COLS);
+#undef SQ
 #undef SK
+#undef SV
+#undef SP
 }
 
 }  // namespace sa3
@@ -325,11 +390,10 @@ __global__ void __launch_bounds__(128, 2)
 using namespace sa3;
 
 extern "C" int sa3_attention(const void* q, const void* k, const void* v, const void* q2, const void* k2,
-                             const void* v2, void* out,
-                             const int* cu_seqlens_q, const int* cu_seqlens_k, int batch, int max_seqlen_q,
-                             int max_seqlen_k, int total_q, int total_k, int heads, int head_dim, long long ldq,
-                             long long ldk, long long ldv, long long ldo, int window_left, int window_right,
-                             float softmax_scale, int dtype, float* amax_out, void* stream) {
+                             const void* v2, void* out, const int* cu_seqlens_q, const int* cu_seqlens_k, int batch,
+                             int max_seqlen_q, int max_seqlen_k, int total_q, int total_k, int heads, int head_dim,
+                             long long ldq, long long ldk, long long ldv, long long ldo, int window_left,
+                             int window_right, float softmax_scale, int dtype, float* amax_out, void* stream) {
   if (!q || !k || !v || !out || batch <= 0 || heads <= 0 || max_seqlen_q <= 0 || max_seqlen_k <= 0)
     return SA3_ERR_ARG;
   if (head_dim != 64) return SA3_ERR_UNSUPPORTED;
@@ -375,14 +439,15 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   p.wl = window_left;
   p.wr = window_right;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.npass = q2 ? 2 : 1;
+  p.diff = q2 ? 1 : 0;
   p.out = out;
   p.ldo = ldo;
   p.amax_out = amax_out;
-  dim3 grid((max_seqlen_q + ATT_BM - 1) / ATT_BM, heads, batch);
+  const int qtiles = (max_seqlen_q + ATT_BM - 1) / ATT_BM;
+  dim3 grid(p.diff ? qtiles : (qtiles + 1) / 2, heads, batch);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
-  attention_tc_kernel<<<grid, 128, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p);
+  attention_tc_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p);
   return launch_status();
 }
 
