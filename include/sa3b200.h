@@ -72,6 +72,10 @@ int sa3_get_device_error(int* err);
 #define SA3_EPI_SWIGLU 2         /* B rows interleaved in blocks of 128 [x|gate]; C[:, N/2] = x*silu(gate) */
 #define SA3_EPI_GATED_RESIDUAL 3 /* C = residual + acc * sigmoid(1 - gate[batch(row), n]) */
 #define SA3_EPI_RESIDUAL 4       /* C = residual + acc */
+#define SA3_EPI_QK_NORM 5        /* C = acc, then per 64-column head: RMSNorm(gamma of its column group) and
+                                    RoPE on dims 0..31 where enabled (fuses sa3_qk_norm_rope into to_qkv /
+                                    to_q / to_kv; Attention.apply_qk_layernorm + apply_rotary_pos_emb,
+                                    transformer.py:589-595, 302-322, 755-781) */
 
 typedef struct {
   int kind;                 /* SA3_EPI_* */
@@ -87,6 +91,17 @@ typedef struct {
   int seg_out;
   int seg_offset;
   int c_f32;                /* nonzero: C and residual are fp32 (the fp32 residual stream), else bf16 */
+  /* SA3_EPI_QK_NORM only: columns form groups of qk_group_width (a multiple of 64); group g's heads are
+     RMS-normalised with qk_gamma[g] (64 fp32, 16-byte aligned; NULL = left as is) and, if bit g of
+     qk_rope_mask is set, rotated at position row_pos[m] (or m % rows_per_batch) with the cos/sin
+     table of sa3_qk_norm_rope. */
+  const float* qk_gamma[8];
+  int qk_group_width;
+  unsigned qk_rope_mask;
+  float qk_eps;
+  const float* cos_sin;
+  int max_pos;
+  const int* row_pos;
 } sa3_epilogue;
 
 int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,

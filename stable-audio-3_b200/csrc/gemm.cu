@@ -425,6 +425,42 @@ __device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int o
   }
 }
 
+// RMSNorm over one 64-column head (v = dims 0..31, w = dims 32..63) with its group's gamma, then
+// rotate_half RoPE on dims 0..31 (pairs i, i+16) at this row's position; fp32 throughout.
+__device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int nc, float (&v)[32], float (&w)[32]) {
+  const int g = nc / e.qk_group_width;
+  const float* gam = nullptr;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (g == i) gam = e.qk_gamma[i];
+  if (gam) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], fmaf(w[i], w[i], ss));
+    const float r = rsqrtf(ss * (1.f / 64.f) + e.qk_eps);
+    float gv[32];
+    ldg_f32x32(gam, gv);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= r * gv[i];
+    ldg_f32x32(gam + 32, gv);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] *= r * gv[i];
+  }
+  if ((e.qk_rope_mask >> g) & 1u) {
+    int pos = e.row_pos ? __ldg(e.row_pos + (m < 0 ? 0 : m)) : (e.rows_per_batch > 0 ? m % e.rows_per_batch : 0);
+    if (pos >= e.max_pos) pos = e.max_pos - 1;
+    if (pos < 0) pos = 0;
+    float cs[32];
+    ldg_f32x32(e.cos_sin + (long long)pos * 32, cs);  // cos[0..15], sin[0..15]
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = v[i], b = v[i + 16];
+      v[i] = fmaf(a, cs[i], -b * cs[16 + i]);
+      v[i + 16] = fmaf(b, cs[i], a * cs[16 + i]);
+    }
+  }
+}
+
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -556,6 +592,21 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
           for (int i = 0; i < 32; ++i) x[i] = x[i] * g[i] * fast_sigmoid(g[i]);
           pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
         }
+      } else if (KIND == SA3_EPI_QK_NORM) {
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int col = half * 128 + hh * 64;
+          const int nc = n0 + col;
+          if (nc >= p.N) break;  // uniform per warp
+          float v[32], w[32];
+          tmem_ld32(trow + col, v);
+          tmem_ld32(trow + col + 32, w);
+          scale_bias32(v, nc, sa, p.b_scale, e.bias);
+          scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
+          qk_norm_rope64(e, m, nc, v, w);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc, v, amax);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc + 32, w, amax);
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -610,6 +661,7 @@ static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, con
     SA3_PG_CASE(SA3_EPI_SWIGLU)
     SA3_PG_CASE(SA3_EPI_GATED_RESIDUAL)
     SA3_PG_CASE(SA3_EPI_RESIDUAL)
+    SA3_PG_CASE(SA3_EPI_QK_NORM)
     default:
       return SA3_ERR_ARG;
   }
@@ -643,7 +695,15 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (!aligned16(A) || !aligned16(B) || ((lda * esz) % 16) || ((ldb * esz) % 16)) return SA3_ERR_ALIGN;
   sa3_epilogue e{};
   if (epi) e = *epi;
-  if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_RESIDUAL) return SA3_ERR_ARG;
+  if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_QK_NORM) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_QK_NORM) {
+    if (e.qk_group_width <= 0 || e.qk_group_width % 64 || N > 8 * e.qk_group_width) return SA3_ERR_ARG;
+    for (int g = 0; g < 8; ++g)
+      if (e.qk_gamma[g] && !aligned16(e.qk_gamma[g])) return SA3_ERR_ALIGN;
+    if (e.qk_rope_mask && (!e.cos_sin || !aligned16(e.cos_sin) || e.max_pos <= 0 ||
+                           (!e.row_pos && e.rows_per_batch <= 0)))
+      return SA3_ERR_ARG;
+  }
   if (e.kind == SA3_EPI_SWIGLU) {
     if (e.c_f32) return SA3_ERR_UNSUPPORTED;
     if (N % GEMM_BN != 0) return SA3_ERR_UNSUPPORTED;
@@ -683,6 +743,7 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
               (e.kind != SA3_EPI_SWIGLU || N % GEMM_BN == 0);
   if (res_kind) fast = fast && aligned16(e.residual) && ((e.ld_residual * celt) % 16 == 0);
   if (e.kind == SA3_EPI_GATED_RESIDUAL) fast = fast && aligned16(e.gate) && (e.ld_gate % 4 == 0);
+  if (!fast && e.kind == SA3_EPI_QK_NORM) return SA3_ERR_UNSUPPORTED;  // only the persistent kernel fuses it
   if (fast) return fp8 ? launch_persistent<true>(tmA, tmB, p, e.kind, st) : launch_persistent<false>(tmA, tmB, p, e.kind, st);
 
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);

@@ -91,9 +91,40 @@ struct NormParams {
   float* amax_out;
 };
 
-// One warp per row; each lane owns chunks of 8 columns at lane*8 + i*256.
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 template <int MAXC>
-__global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
+__device__ __forceinline__ void norm_load_row(const NormParams& p, int row, float (&v)[MAXC][8]) {
+  const int lane = threadIdx.x & 31;
+  const int nchunk = p.D / 8;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
+      if (p.x_f32) {
+        const float4* xr =
+            reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (long long)row * p.ldx + c * 8);
+        const float4 a = xr[0], b = xr[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      } else {
+        const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + (long long)row * p.ldx;
+        unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+      }
+    }
+  }
+}
+
+// One warp per row; each lane owns chunks of 8 columns at lane*8 + i*256. Warps are persistent and
+// load row r + stride before normalising row r, so two rows of every warp are in flight. VEC: gamma
+// and the modulation rows are 16-byte aligned and come in as float4 loads.
+template <int MAXC, bool VEC>
+__global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunk = p.D / 8;
   float s = 1.f;
@@ -102,27 +133,21 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
     if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
   }
   float amax = 0.f;
-  for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < p.rows; row += gridDim.x * (blockDim.x >> 5)) {
-    float v[MAXC][8];
+  const int stride = gridDim.x * (blockDim.x >> 5);
+  int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  float v[MAXC][8];
+  if (row < p.rows) norm_load_row<MAXC>(p, row, v);
+  while (row < p.rows) {
+    const int nrow = row + stride;
+    float nv[MAXC][8];
+    if (nrow < p.rows) norm_load_row<MAXC>(p, nrow, nv);
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = lane + i * 32;
-      if (c < nchunk) {
-        if (p.x_f32) {
-          const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) +
-                                                             (long long)row * p.ldx + c * 8);
-          const float4 a = xr[0], b = xr[1];
-          v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-          v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
-        } else {
-          const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + (long long)row * p.ldx;
-          unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
-        }
+    for (int i = 0; i < MAXC; ++i)
+      if (lane + i * 32 < nchunk) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
       }
-    }
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)p.D + p.eps);
     const float* msc = nullptr;
@@ -136,13 +161,26 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
     for (int i = 0; i < MAXC; ++i) {
       const int c = lane + i * 32;
       if (c < nchunk) {
-        float y[8];
+        float y[8], gm[8], sc[8], sh[8];
+        if (VEC) {
+          if (p.gamma) ld8f(p.gamma + c * 8, gm);
+          if (msc) {
+            ld8f(msc + c * 8, sc);
+            ld8f(msh + c * 8, sh);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            gm[j] = p.gamma ? __ldg(p.gamma + c * 8 + j) : 1.f;
+            sc[j] = msc ? __ldg(msc + c * 8 + j) : 0.f;
+            sh[j] = msh ? __ldg(msh + c * 8 + j) : 0.f;
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int col = c * 8 + j;
           float t = v[i][j] * r;
-          if (p.gamma) t *= __ldg(p.gamma + col);
-          if (msc) t = t * (1.f + __ldg(msc + col)) + __ldg(msh + col);
+          if (p.gamma) t *= gm[j];
+          if (msc) t = fmaf(t, 1.f + sc[j], sh[j]);
           y[j] = t;
         }
         if (p.mode == SA3_NORM_AMAX) {
@@ -157,6 +195,13 @@ __global__ void __launch_bounds__(256) rmsnorm_modulate_kernel(NormParams p) {
         }
       }
     }
+    if (nrow < p.rows) {
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = nv[i][j];
+    }
+    row = nrow;
   }
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
@@ -225,7 +270,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
     const int gh = active ? (int)(item - row * per_row) : 0;
     const int g = gh / p.heads;
     const int h = gh - g * p.heads;
-    __nv_bfloat16* ptr = p.buf + row * p.ld + p.col_off[g] + h * 64 + sub * 8;
+    // per-group parameters selected without indexing the parameter arrays (keeps them in registers)
+    const int coff = g == 0 ? p.col_off[0] : g == 1 ? p.col_off[1] : g == 2 ? p.col_off[2] : p.col_off[3];
+    const float* gm = g == 0 ? p.gamma[0] : g == 1 ? p.gamma[1] : g == 2 ? p.gamma[2] : p.gamma[3];
+    const int rope = g == 0 ? p.rope[0] : g == 1 ? p.rope[1] : g == 2 ? p.rope[2] : p.rope[3];
+    __nv_bfloat16* ptr = p.buf + row * p.ld + coff + h * 64 + sub * 8;
     float v[8];
     if (active) unpack8(*reinterpret_cast<const uint4*>(ptr), v);
     else {
@@ -234,33 +283,38 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
     }
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
     ss += __shfl_xor_sync(0xffffffffu, ss, 4);
     const float r = rsqrtf(ss * (1.f / 64.f) + p.eps);
-    const float* gm = p.gamma[g];
+    if (gm) {
+      float gv[8];
+      ld8f(gm + sub * 8, gv);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = v[j] * r * (gm ? __ldg(gm + sub * 8 + j) : 1.f);
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * r * gv[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= r;
+    }
     // rotate_half pairs dim d with d +- 16: lanes sub and sub^2 within the first 32 dims.
     float partner[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, v[j], 2);
-    if (active && p.rope[g] && sub < 4) {
+    if (active && rope && sub < 4) {
       int pos = p.row_pos ? __ldg(p.row_pos + row) : (int)(row % p.rows_per_batch);
       if (pos >= p.max_pos) {
         record_error(2, 10);
         pos = p.max_pos - 1;
       }
-      const float* cs = p.cos_sin + (long long)pos * 32;
+      // dims sub*8 .. sub*8+7 use frequencies (sub & 1) * 8 .. +7
+      const float* cs = p.cos_sin + (long long)pos * 32 + (sub & 1) * 8;
+      float cv[8], sv[8];
+      ld8f(cs, cv);
+      ld8f(cs + 16, sv);
+      const float sgn = sub < 2 ? -1.f : 1.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int d = sub * 8 + j;   // 0..31
-        const int f = d & 15;
-        const float c = __ldg(cs + f), sn = __ldg(cs + 16 + f);
-        const float rh = (d < 16) ? -partner[j] : partner[j];
-        v[j] = v[j] * c + rh * sn;
-      }
+      for (int j = 0; j < 8; ++j) v[j] = fmaf(v[j], cv[j], sgn * partner[j] * sv[j]);
     }
     if (active) *reinterpret_cast<uint4*>(ptr) = pack8(v);
   }
@@ -355,16 +409,28 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   p.scale_out = scale_out;
   p.amax_out = amax_out;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int grid = grid_for(rows, 8);
   const int nchunk = D / 8;
-  if (nchunk <= 32 * 4)
-    rmsnorm_modulate_kernel<4><<<grid, 256, 0, st>>>(p);
-  else if (nchunk <= 32 * 8)
-    rmsnorm_modulate_kernel<8><<<grid, 256, 0, st>>>(p);
-  else if (nchunk <= 32 * 16)
-    rmsnorm_modulate_kernel<16><<<grid, 256, 0, st>>>(p);
-  else
+  int grid = (rows + 3) / 4;  // 4 warps (rows) per 128-thread block
+  if (grid > 148 * 3) grid = 148 * 3;  // one wave at 3 blocks per SM
+  const bool vec = aligned16(gamma) && (!mod || (aligned16(mod) && ld_mod % 4 == 0 && scale_off % 4 == 0 &&
+                                                    shift_off % 4 == 0));
+#define SA3_NORM_LAUNCH(C)                                      \
+  if (vec)                                                      \
+    rmsnorm_modulate_kernel<C, true><<<grid, 128, 0, st>>>(p);  \
+  else                                                          \
+    rmsnorm_modulate_kernel<C, false><<<grid, 128, 0, st>>>(p);
+  if (nchunk <= 32 * 4) {
+    SA3_NORM_LAUNCH(4)
+  } else if (nchunk <= 32 * 6) {
+    SA3_NORM_LAUNCH(6)
+  } else if (nchunk <= 32 * 8) {
+    SA3_NORM_LAUNCH(8)
+  } else if (nchunk <= 32 * 16) {
+    SA3_NORM_LAUNCH(16)
+  } else {
     return SA3_ERR_UNSUPPORTED;
+  }
+#undef SA3_NORM_LAUNCH
   return launch_status();
 }
 
@@ -399,6 +465,7 @@ extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, in
     if (col_off[g] < 0 || (col_off[g] % 8) || col_off[g] + heads * 64 > ld) return SA3_ERR_ARG;
     p.col_off[g] = col_off[g];
     p.gamma[g] = gamma ? gamma[g] : nullptr;
+    if (p.gamma[g] && !aligned16(p.gamma[g])) return SA3_ERR_ALIGN;
     p.rope[g] = rope ? rope[g] : 0;
     any_rope |= p.rope[g] != 0;
   }

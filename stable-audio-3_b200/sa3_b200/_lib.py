@@ -27,7 +27,7 @@ STATUS_NAMES = {
 }
 
 DT_BF16, DT_F16, DT_E4M3, DT_F32 = 0, 1, 2, 3
-EPI_STORE, EPI_SILU, EPI_SWIGLU, EPI_GATED_RESIDUAL, EPI_RESIDUAL = 0, 1, 2, 3, 4
+EPI_STORE, EPI_SILU, EPI_SWIGLU, EPI_GATED_RESIDUAL, EPI_RESIDUAL, EPI_QK_NORM = 0, 1, 2, 3, 4, 5
 NORM_WRITE, NORM_AMAX = 0, 1
 
 
@@ -48,6 +48,13 @@ class Epilogue(ctypes.Structure):
         ("seg_out", c_int),
         ("seg_offset", c_int),
         ("c_f32", c_int),
+        ("qk_gamma", c_vp * 8),
+        ("qk_group_width", c_int),
+        ("qk_rope_mask", ctypes.c_uint),
+        ("qk_eps", c_float),
+        ("cos_sin", c_vp),
+        ("max_pos", c_int),
+        ("row_pos", c_vp),
     ]
 
 

@@ -7,9 +7,9 @@ ContinuousTransformer.forward (transformer.py:1161-1272) -> TransformerBlock.for
 (transformer.py:996-1049) with every hot op in libsa3b200.so:
 
   per block (token rows [B*N, D], N = L + memory tokens):
-    RMSNorm+adaLN modulate (+FP8 quant)   -> to_qkv GEMM -> qk RMSNorm + RoPE (in place)
+    RMSNorm+adaLN modulate (+FP8 quant)   -> to_qkv GEMM with qk RMSNorm + RoPE in its epilogue
     -> windowed (differential) attention   -> to_out GEMM with gate*sigmoid(1-g)+residual epilogue
-    cross: RMSNorm (+quant) -> to_q GEMM -> q-norm ; ctx -> to_kv GEMM -> k-norm
+    cross: RMSNorm (+quant) -> to_q GEMM (+q-norm epilogue) ; ctx -> to_kv GEMM (+k-norm epilogue)
            -> full attention over the context -> to_out GEMM with residual epilogue
     local cond: Linear+SiLU GEMM -> Linear GEMM adding into rows 64.. (left pad) of the stream
     FF: RMSNorm+modulate (+quant) -> GLU.proj GEMM with SwiGLU epilogue (+amax) (-> quant)
@@ -281,37 +281,38 @@ class DiTEngine:
             s0 = 8 * i
             # -- self-attention with adaLN (transformer.py:1018-1029)
             a, asc = self._norm_to_a(ws, h, self.gam[p + "pre_norm.gamma"], s0, ssi, 0, D)
-            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc)
             gq, gk = self.gam[p + "self_attn.q_norm.gamma"], self.gam[p + "self_attn.k_norm.gamma"]
+            # to_qkv with qk RMSNorm + RoPE fused into the epilogue (groups q | k | v | q_diff | k_diff)
+            groups = [gq, gk, None, gq, gk] if diff else [gq, gk, None]
+            rope = [True, True, False, True, True] if diff else [True, True, False]
+            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM, rows_per_batch=N,
+                       qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope))
+            am1 = ws.amax[s0 + 1:s0 + 2] if self.fp8 else None
             if diff:
-                ops.qk_norm_rope(qkv, H, [0, D, 3 * D, 4 * D], [gq, gk, gq, gk], [True] * 4, cfg.qk_norm_eps,
-                                 self.rope, rows_per_batch=N)
                 ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
                               k2=qkv[:, 4 * D:5 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N,
-                              window=(wl, wr), out=o, amax_out=ws.amax[s0 + 1:s0 + 2] if self.fp8 else None)
+                              window=(wl, wr), out=o, amax_out=am1)
             else:
-                ops.qk_norm_rope(qkv, H, [0, D], [gq, gk], [True] * 2, cfg.qk_norm_eps, self.rope, rows_per_batch=N)
                 ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, batch=B, max_seqlen_q=N,
-                              max_seqlen_k=N, window=(wl, wr), out=o,
-                              amax_out=ws.amax[s0 + 1:s0 + 2] if self.fp8 else None)
+                              max_seqlen_k=N, window=(wl, wr), out=o, amax_out=am1)
             oa, osc = self._quant(ws, o, ws.o8, s0 + 1)
             self._gemm(oa, ln[p + "self_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
                        gate=ssi[:, 2 * D:3 * D], rows_per_batch=N)
             # -- cross-attention (transformer.py:1031-1035), no adaLN, no RoPE
             if ctx is not None and (p + "cross_attn.to_q") in ln:
                 c, csc = self._norm_to_a(ws, h, self.gam[p + "cross_attend_norm.gamma"], s0 + 2)
-                self._gemm(c, ln[p + "cross_attn.to_q"], qx, x_scale=csc)
-                self._gemm(ctx_a, ln[p + "cross_attn.to_kv"], kv, x_scale=ctx_s)
                 gq, gk = self.gam[p + "cross_attn.q_norm.gamma"], self.gam[p + "cross_attn.k_norm.gamma"]
+                # to_q / to_kv with the qk RMSNorm fused into the epilogue (no RoPE on cross-attention)
+                self._gemm(c, ln[p + "cross_attn.to_q"], qx, x_scale=csc, kind=_lib.EPI_QK_NORM,
+                           qk=dict(gammas=[gq, gq] if diff else [gq], group_width=D, eps=cfg.qk_norm_eps))
+                self._gemm(ctx_a, ln[p + "cross_attn.to_kv"], kv, x_scale=ctx_s, kind=_lib.EPI_QK_NORM,
+                           qk=dict(gammas=[gk, gk, None] if diff else [gk, None], group_width=D,
+                                   eps=cfg.qk_norm_eps))
                 am = ws.amax[s0 + 3:s0 + 4] if self.fp8 else None
                 if diff:
-                    ops.qk_norm_rope(qx, H, [0, D], [gq, gq], [False, False], cfg.qk_norm_eps)
-                    ops.qk_norm_rope(kv, H, [0, D], [gk, gk], [False, False], cfg.qk_norm_eps)
                     ops.attention(qx[:, 0:D], kv[:, 0:D], kv[:, 2 * D:3 * D], q2=qx[:, D:2 * D], k2=kv[:, D:2 * D],
                                   heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc, out=o, amax_out=am)
                 else:
-                    ops.qk_norm_rope(qx, H, [0], [gq], [False], cfg.qk_norm_eps)
-                    ops.qk_norm_rope(kv, H, [0], [gk], [False], cfg.qk_norm_eps)
                     ops.attention(qx, kv[:, 0:D], kv[:, D:2 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc,
                                   out=o, amax_out=am)
                 oa, osc = self._quant(ws, o, ws.o8, s0 + 3)

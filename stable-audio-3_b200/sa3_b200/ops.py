@@ -61,8 +61,12 @@ def _dt(t: torch.Tensor) -> int:
 # ---------------------------------------------------------------------- GEMM
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_scale=None, b_scale=None,
          bias=None, kind: int = _lib.EPI_STORE, residual=None, gate=None, rows_per_batch: int = 0,
-         row_batch=None, amax_out=None, seg=None) -> torch.Tensor:
-    """out = epilogue(a @ b.T * a_scale * b_scale + bias); a [M,K], b [N,K] (K-major), bf16 or e4m3."""
+         row_batch=None, amax_out=None, seg=None, qk=None) -> torch.Tensor:
+    """out = epilogue(a @ b.T * a_scale * b_scale + bias); a [M,K], b [N,K] (K-major), bf16 or e4m3.
+
+    qk (for kind EPI_QK_NORM): dict(gammas=[per column group: fp32 [64] or None], group_width=int,
+    rope=[bool per group], eps=float, cos_sin=fp32 [max_pos, 32] or None, row_pos=int32 [M] or None).
+    """
     _need_cuda(a, b, out, a_scale, b_scale, bias, residual, gate, row_batch, amax_out)
     if a.dtype != b.dtype:
         raise RuntimeError("a and b must have the same dtype")
@@ -97,6 +101,18 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     if seg is not None:
         epi.seg_in, epi.seg_out, epi.seg_offset = seg
     epi.c_f32 = 1 if out.dtype == torch.float32 else 0
+    if qk is not None:
+        gams = list(qk["gammas"])
+        _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"))
+        for i, gm in enumerate(gams):
+            epi.qk_gamma[i] = _ptr(gm)
+        epi.qk_group_width = int(qk["group_width"])
+        epi.qk_rope_mask = sum(1 << i for i, r in enumerate(qk.get("rope", [])) if r)
+        epi.qk_eps = float(qk.get("eps", 1e-6))
+        cs = qk.get("cos_sin")
+        epi.cos_sin = _ptr(cs)
+        epi.max_pos = cs.shape[0] if cs is not None else 0
+        epi.row_pos = _ptr(qk.get("row_pos"))
     _count()
     rc = _lib.load().sa3_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _row_stride(a), _row_stride(b),
                               _row_stride(out), _dt(a), _ptr(a_scale), _ptr(b_scale), ctypes.byref(epi), _stream())

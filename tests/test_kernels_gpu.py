@@ -280,3 +280,41 @@ def test_no_device_error_recorded(cuda):
     from sa3_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_gemm_qk_norm_rope_epilogue(cuda, fp8):
+    """to_qkv GEMM with qk RMSNorm + RoPE fused into the epilogue vs oracle linear -> rms_norm -> apply_rotary."""
+    from sa3_b200 import ops, _lib
+
+    g = _gen(31)
+    B, T, H, K = 2, 300, 4, 512
+    D = H * 64
+    x = torch.randn(B * T, K, generator=g)
+    w = torch.randn(5 * D, K, generator=g) * 0.05
+    gq = 1 + 0.1 * torch.randn(64, generator=g)
+    gk = 1 + 0.1 * torch.randn(64, generator=g)
+    table = ops.rope_table(T, device=cuda)
+    if fp8:
+        wq, sw = oq.quantize_weight_e4m3(w)
+        xd = x.bfloat16().to(cuda)
+        amax, s = torch.zeros(1, device=cuda), torch.zeros(1, device=cuda)
+        ops.absmax(xd, amax)
+        a = ops.quantize_e4m3(xd, amax, scale_out=s)
+        y = oq.fp8_linear(x.bfloat16().float(), wq, sw)
+        kw = dict(a_scale=s, b_scale=sw.to(cuda))
+        bmat = wq.to(cuda)
+    else:
+        a = x.bfloat16().to(cuda)
+        bmat = w.bfloat16().to(cuda)
+        y = x.bfloat16().float() @ w.bfloat16().float().T
+        kw = {}
+    out = ops.gemm(a, bmat, kind=_lib.EPI_QK_NORM, rows_per_batch=T,
+                   qk=dict(gammas=[gq.to(cuda), gk.to(cuda), None, gq.to(cuda), gk.to(cuda)], group_width=D,
+                           rope=[True, True, False, True, True], eps=1e-6, cos_sin=table), **kw)
+    freqs = orf.rotary_freqs(T, 32)
+    ref = y.view(B, T, 5, H, 64).clone()
+    for part, gm in ((0, gq), (1, gk), (3, gq), (4, gk)):
+        t = ref[:, :, part].permute(0, 2, 1, 3)
+        ref[:, :, part] = orf.apply_rotary(orf.rms_norm(t, gm, 1e-6), freqs).permute(0, 2, 1, 3)
+    assert max_rel(out.view(B, T, 5, H, 64), ref) < 1e-2
