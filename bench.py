@@ -35,6 +35,8 @@ import torch  # noqa: E402
 WORKLOADS = {
     # the headline configuration: medium DiT, FP8 linears, L = 8183, one prompt = one CFG pair per GPU
     "medium_fp8": dict(model="medium", mode="fp8", L=8183, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
+    # medium DiT with GPTQ int4 weight-only linears (group 128, act-order), L = 2584, batch 16 (8 CFG pairs)
+    "medium_gptq": dict(model="medium", mode="gptq", L=2584, prompts=8, Tc=128, cfg_scale=7.0, apg_scale=1.0),
     # small DiT in bf16 (24 blocks, dim 1024, L = 2584, CFG pair)
     "small_bf16": dict(model="small", mode="bf16", L=2584, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
 }
@@ -207,7 +209,12 @@ def run_ours(args, wl, world, rank, local):
 
     dev = torch.device("cuda", local)
     cfg = model_cfg(wl["model"])
-    model = init_synthetic_(DiffusionTransformer(cfg), seed=0).quantize(wl["mode"])
+    model = init_synthetic_(DiffusionTransformer(cfg), seed=0)
+    if wl["mode"] == "gptq":
+        from sa3_b200.gptq import random_model_layers
+        model.quantize("gptq", gptq_layers=random_model_layers(model, seed=1, device=dev))
+    else:
+        model.quantize(wl["mode"])
     eng = model.engine()
     x, t, cond, gemb, loc = make_inputs(wl, cfg, seed=100 + rank, device=dev)
     cs, aps = wl["cfg_scale"], wl["apg_scale"]
@@ -262,20 +269,30 @@ def run_ours(args, wl, world, rank, local):
     h2d = sum(a.numel() * a.element_size() for a in (hx, ht, hc, hg, hl))
     d2h = out_host.numel() * out_host.element_size()
 
-    # ---- roofline of the dominant kernel: the FF GLU.proj FP8 GEMM (M=B*N, N=2*ff_inner, K=dim),
-    # timed live with CUDA events on the launching stream, operands from the step's own buffers
+    # ---- roofline of the dominant kernel: the FF GLU.proj GEMM (M=B*N, N=2*ff_inner, K=dim) with its SwiGLU
+    # epilogue, timed live with CUDA events on the launching stream, operands from the step's own buffers
     ws = eng.ws
     lin = eng.lin["transformer.layers.0.ff.ff.0.proj"]
-    scale = ws.scale[4:5]
-    M, K, Nw = ws.a.shape[0], ws.a.shape[1], lin.w.shape[0]
+    M, K = ws.a.shape
+    Nw = lin.n
+    if lin.gptq is not None:
+        g = lin.gptq
+        xp = ops.permute_cols(ws.a, g["perm"], ws.xperm[:M, :K])
+        run_k = lambda: ops.gptq_gemm(xp, g["qw"], g["sz"], Nw, ws.u, kind=_lib.EPI_SWIGLU, bias=lin.bias)  # noqa
+        kname = "gemm_gptq_kernel<SwiGLU> (FF GLU.proj, int4 dequant in smem)"
+    else:
+        scale = ws.scale[4:5]
+        run_k = lambda: eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)  # noqa: E731
+        kname = ("gemm_persistent_kernel<fp8, SwiGLU>" if lin.fp8 else "gemm_persistent_kernel<bf16, SwiGLU>") + \
+            " (FF GLU.proj)"
     reps = 20
     with torch.inference_mode():
         for _ in range(3):
-            eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)
+            run_k()
         torch.cuda.synchronize()
         e0.record()
         for _ in range(reps):
-            eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)
+            run_k()
         e1.record()
         torch.cuda.synchronize()
     k_ms = e0.elapsed_time(e1) / reps
@@ -288,17 +305,19 @@ def run_ours(args, wl, world, rank, local):
         else:
             peak, peak_src = 2 * 1590.0, "2x fallback bf16 1.59 PF"
     else:
-        peak, peak_src = (peaks["bf16_tflops"], "measured bf16 burst") if peaks else (1590.0, "fallback")
-    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel<fp8> (FF GLU.proj, SwiGLU epilogue)",
-                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": peak_src, "traffic": None,
+        peak, peak_src = (peaks["bf16_tflops"], "measured bf16 burst (MEASURED_PEAKS.json)") if peaks else \
+            (1590.0, "fallback bf16 1.59 PF")
+    roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": peak_src, "traffic": None,
                 "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
 
     if rank == 0:
         res = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "fp8-e4m3 linears / bf16 attention" if wl["mode"] == "fp8" else "bf16",
+            "vs_baseline": None,
+            "dtype": {"fp8": "fp8-e4m3 linears / bf16 attention", "gptq": "int4 weights (GPTQ) / bf16 activations",
+                      "bf16": "bf16"}[wl["mode"]],
             "data": "synthetic",
             "config": {"workload": args.workload, "model": f"sa3-{wl['model']} DiT, random init",
                        "dim": cfg.embed_dim, "depth": cfg.depth, "heads": cfg.num_heads,

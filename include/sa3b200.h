@@ -108,6 +108,33 @@ int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long lo
              long long ldc, int ab_dtype, const float* a_scale, const float* b_scale, const sa3_epilogue* epi,
              void* stream);
 
+/* ---------------------------------------------- GPTQ int4 weight-only linear (a3, a4)
+ *
+ * C = epilogue(A . W^T) with W stored 4-bit: replaces the same nn.Linear calls as
+ * sa3_gemm (transformer.py:547-560, 432, 485) for GPTQ checkpoints (asymmetric,
+ * group size gs, act-order). The reference has no quantized code; the layout below
+ * is this library's, produced from the usual GPTQ tensors (qweight [K/8, N],
+ * qzeros [G, N/8], fp16 scales [G, N], g_idx [K]) by sa3_b200.gptq.repack:
+ *   perm int32 [K]    : input channels sorted by group (stable argsort of g_idx);
+ *                       A must hold x[:, perm] (sa3_permute_cols)
+ *   qw   int32 [N, K/8] : word (n, w) = q[n, perm[8w + j]] in bits [4j, 4j+4), LSB first
+ *   sz   fp32  [G, 2N]  : row g = [ s[g, :] | z[g, :] * s[g, :] ]
+ * W[n, k'] = (q - z) * s computed as fma(q, s, -z*s) in fp32 (exact), rounded once to bf16
+ * in shared memory, multiplied on tcgen05 (kind::f16) with fp32 accumulation.
+ * A bf16 [M, K] (lda); K % gs == 0, gs % 64 == 0, N % 256 == 0. Epilogue as sa3_gemm
+ * (a_scale / b_scale do not apply).
+ */
+int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, void* C, int M, int N, int K, long long lda,
+                  long long ldc, int group_size, const sa3_epilogue* epi, void* stream);
+
+/* Dequantise the packed GPTQ weight to bf16 W [N, K] (row n contiguous over the sorted channels),
+ * with the exact arithmetic of sa3_gptq_gemm's shared-memory stage. */
+int sa3_gptq_dequant(const void* qw, const float* sz, void* out, int N, int K, int group_size, void* stream);
+
+/* out[r, j] = x[r, perm[j]] for a bf16 [rows, K] view (the act-order gather of GPTQ inputs). */
+int sa3_permute_cols(const void* x, const int* perm, void* out, int rows, int K, long long ldx, long long ldo,
+                     void* stream);
+
 /* ---------------------------------------------- glue: norms / modulation (a7, a9)
  *
  * y[r, :] = RMSNorm(x[r, :]) * gamma * (1 + scale[b, :]) + shift[b, :]

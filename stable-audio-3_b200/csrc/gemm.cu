@@ -461,6 +461,61 @@ __device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int
   }
 }
 
+// Epilogue of one 128 x 256 accumulator tile for the 32 rows of TMEM lane quarter q and column
+// half `half` (tmem_tile = the tile's first TMEM column). Shared by the FP8/bf16 and GPTQ kernels.
+template <int KIND>
+__device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t tmem_tile, int m0, int n0, int q,
+                                                 int half, float sa, float& amax) {
+  const sa3_epilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+      const int m = m0 + q * 32 + lane;
+      const int orow = out_row_of(e, m < p.M ? m : p.M - 1);
+      int batch = 0;
+      if (KIND == SA3_EPI_GATED_RESIDUAL && m < p.M)
+        batch = e.row_batch ? __ldg(e.row_batch + m) : m / e.rows_per_batch;
+      const uint32_t trow = tmem_tile + ((uint32_t)(q * 32) << 16);
+      if (KIND == SA3_EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          const int col = half * 64 + c * 32;
+          float x[32], g[32];
+          tmem_ld32(trow + col, x);
+          tmem_ld32(trow + 128 + col, g);
+          scale_bias32(x, n0 + col, sa, p.b_scale, e.bias);
+          scale_bias32(g, n0 + 128 + col, sa, p.b_scale, e.bias);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = x[i] * g[i] * fast_sigmoid(g[i]);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
+        }
+      } else if (KIND == SA3_EPI_QK_NORM) {
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int col = half * 128 + hh * 64;
+          const int nc = n0 + col;
+          if (nc >= p.N) break;  // uniform per warp
+          float v[32], w[32];
+          tmem_ld32(trow + col, v);
+          tmem_ld32(trow + col + 32, w);
+          scale_bias32(v, nc, sa, p.b_scale, e.bias);
+          scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
+          qk_norm_rope64(e, m, nc, v, w);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc, v, amax);
+          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc + 32, w, amax);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int col = half * 128 + c * 32;
+          const int nc = n0 + col;
+          if (nc >= p.N) break;  // uniform per warp
+          float v[32];
+          tmem_ld32(trow + col, v);
+          scale_bias32(v, nc, sa, p.b_scale, e.bias);
+          pg_store_chunk<KIND>(p, m, orow, batch, nc, v, amax);
+        }
+      }
+}
+
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -573,52 +628,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       tc_fence_after();
       const int m0 = (t / tiles_n) * GEMM_BM;
       const int n0 = (t % tiles_n) * GEMM_BN;
-      const int m = m0 + q * 32 + lane;
-      const int orow = out_row_of(e, m < p.M ? m : p.M - 1);
-      int batch = 0;
-      if (KIND == SA3_EPI_GATED_RESIDUAL && m < p.M)
-        batch = e.row_batch ? __ldg(e.row_batch + m) : m / e.rows_per_batch;
-      const uint32_t trow = tmem + a * GEMM_BN + ((uint32_t)(q * 32) << 16);
-      if (KIND == SA3_EPI_SWIGLU) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          const int col = half * 64 + c * 32;
-          float x[32], g[32];
-          tmem_ld32(trow + col, x);
-          tmem_ld32(trow + 128 + col, g);
-          scale_bias32(x, n0 + col, sa, p.b_scale, e.bias);
-          scale_bias32(g, n0 + 128 + col, sa, p.b_scale, e.bias);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = x[i] * g[i] * fast_sigmoid(g[i]);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
-        }
-      } else if (KIND == SA3_EPI_QK_NORM) {
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const int col = half * 128 + hh * 64;
-          const int nc = n0 + col;
-          if (nc >= p.N) break;  // uniform per warp
-          float v[32], w[32];
-          tmem_ld32(trow + col, v);
-          tmem_ld32(trow + col + 32, w);
-          scale_bias32(v, nc, sa, p.b_scale, e.bias);
-          scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
-          qk_norm_rope64(e, m, nc, v, w);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc, v, amax);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc + 32, w, amax);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          const int col = half * 128 + c * 32;
-          const int nc = n0 + col;
-          if (nc >= p.N) break;  // uniform per warp
-          float v[32];
-          tmem_ld32(trow + col, v);
-          scale_bias32(v, nc, sa, p.b_scale, e.bias);
-          pg_store_chunk<KIND>(p, m, orow, batch, nc, v, amax);
-        }
-      }
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
@@ -667,6 +677,233 @@ static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, con
   }
 #undef SA3_PG_CASE
   return launch_status();
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// GPTQ int4 weight-only GEMM: C = epilogue(A . W^T), A bf16 [M, K] (input channels already in
+// group-sorted act-order), W given as
+//   qw  int32 [N, K/8]  : word (n, w) holds q[n, k] for k = 8w + j in bits [4j, 4j+4)
+//   sz  fp32  [G, 2N]   : row g = [ s[g, 0..N) | z*s[g, 0..N) ], group g covers k in [g*gs, (g+1)*gs)
+// W[n, k] = q*s - z*s = (q - z) * s (exact in fp32), rounded once to bf16 in shared memory.
+// Persistent, 14 warps: warp 0 TMA (A tile, packed W tile, s and z*s rows), warp 1 tcgen05.mma
+// (kind::f16, bf16), warps 2..5 epilogue (TMEM double buffer), warps 6..13 dequantise the packed
+// tile into a 128-byte-swizzled K-major bf16 B tile.
+constexpr int GQ_STAGES = 3;
+constexpr int GQ_A_BYTES = 16384;   // 128 x 64 bf16
+constexpr int GQ_BD_BYTES = 32768;  // 256 x 64 bf16 (dequantised)
+constexpr int GQ_BP_BYTES = 8192;   // 256 x 8 packed words
+constexpr int GQ_SZ_BYTES = 2048;   // 256 s + 256 z*s
+constexpr int GQ_STAGE_BYTES = GQ_A_BYTES + GQ_BD_BYTES + GQ_BP_BYTES + GQ_SZ_BYTES;
+constexpr int GQ_THREADS = 448;
+constexpr int GQ_SMEM = GQ_STAGES * GQ_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint4 gptq_dequant8(uint32_t word, float sc, float zs) {
+  float w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t q = (word >> (4 * j)) & 0xFu;
+    const float f = __uint_as_float(0x4B000000u | q) - 8388608.f;  // exact float(q)
+    w[j] = fmaf(f, sc, -zs);                                        // (q - z) * s, exact
+  }
+  uint4 u;
+  u.x = pack_bf16x2(w[0], w[1]);
+  u.y = pack_bf16x2(w[2], w[3]);
+  u.z = pack_bf16x2(w[4], w[5]);
+  u.w = pack_bf16x2(w[6], w[7]);
+  return u;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(GQ_THREADS, 1)
+    gemm_gptq_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmSZ, GemmParams p, int tiles_n, int num_tiles,
+                     int group_size) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GQ_STAGES * GQ_STAGE_BYTES);
+  uint64_t* dq = full + GQ_STAGES;
+  uint64_t* empty = dq + GQ_STAGES;
+  uint64_t* acc_full = empty + GQ_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+#define GQ_A(s) (smem + (s) * GQ_STAGE_BYTES)
+#define GQ_BD(s) (smem + (s) * GQ_STAGE_BYTES + GQ_A_BYTES)
+#define GQ_BP(s) (smem + (s) * GQ_STAGE_BYTES + GQ_A_BYTES + GQ_BD_BYTES)
+#define GQ_SZ(s) (smem + (s) * GQ_STAGE_BYTES + GQ_A_BYTES + GQ_BD_BYTES + GQ_BP_BYTES)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkb = p.K / 64;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < GQ_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&dq[i], 8);
+      mbar_init(&empty[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmSZ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, PG_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * GEMM_BM;
+        const int n0 = (t % tiles_n) * GEMM_BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % GQ_STAGES;
+          if (it >= (uint32_t)GQ_STAGES && !mbar_wait(&empty[s], ((it / GQ_STAGES) - 1) & 1, abort_flag, 51)) break;
+          const int g = (kb * 64) / group_size;
+          mbar_arrive_expect_tx(&full[s], GQ_A_BYTES + GQ_BP_BYTES + GQ_SZ_BYTES);
+          tma_load_2d(GQ_A(s), &tmA, &full[s], kb * 64, m0);
+          tma_load_2d(GQ_BP(s), &tmW, &full[s], kb * 8, n0);
+          tma_load_2d(GQ_SZ(s), &tmSZ, &full[s], n0, g);
+          tma_load_2d(GQ_SZ(s) + 1024, &tmSZ, &full[s], p.N + n0, g);
+        }
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        // the last GQ_STAGES issued stages are the only ones that can still be in flight
+        for (int s = 0; s < GQ_STAGES; ++s) mbar_wait(&full[s], 0, &never, 52);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(GEMM_BM, GEMM_BN, 1, 1, 0, 0);
+      uint32_t it = 0, lt = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++lt) {
+        const uint32_t a = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[a], ((lt >> 1) - 1) & 1, abort_flag, 53)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * GEMM_BN;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % GQ_STAGES;
+          if (!mbar_wait(&dq[s], (it / GQ_STAGES) & 1, abort_flag, 54)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sdesc_kmajor_sw128(smem_u32(GQ_A(s)));
+          const uint64_t bd = sdesc_kmajor_sw128(smem_u32(GQ_BD(s)));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_f16_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&acc_full[a]);
+        if (!ok) break;
+      }
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;
+    float amax = 0.f;
+    uint32_t lt = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
+      const uint32_t a = lt & 1;
+      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 55)) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * GEMM_BM;
+      const int n0 = (t % tiles_n) * GEMM_BN;
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, 0, 1.f, amax);
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, 1, 1.f, amax);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+    if (p.epi.amax_out) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) atomic_max_nonneg(p.epi.amax_out, amax);
+    }
+  } else {
+    // ---------------- dequantisation warps: thread t handles words t + 256 i (n = word / 8, w = word % 8)
+    const int t = (warp - 6) * 32 + lane;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % GQ_STAGES;
+        if (!mbar_wait(&full[s], (it / GQ_STAGES) & 1, abort_flag, 56)) break;
+        const uint32_t* bp = reinterpret_cast<const uint32_t*>(GQ_BP(s));
+        const float* sc = reinterpret_cast<const float*>(GQ_SZ(s));
+        uint8_t* bd = GQ_BD(s);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int item = i * 256 + t;
+          const int n = item >> 3, w = item & 7;
+          const uint4 u = gptq_dequant8(bp[item], sc[n], sc[256 + n]);
+          *reinterpret_cast<uint4*>(bd + n * 128 + ((w ^ (n & 7)) << 4)) = u;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq[s]);
+      }
+      if (*abort_flag) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, PG_TMEM_COLS);
+#undef GQ_A
+#undef GQ_BD
+#undef GQ_BP
+#undef GQ_SZ
+}
+
+__global__ void __launch_bounds__(256) gptq_dequant_kernel(const uint32_t* qw, const float* sz, __nv_bfloat16* out,
+                                                           int N, int K, int group_size) {
+  const long long words = (long long)N * (K / 8);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / (K / 8));
+    const int w = (int)(i - (long long)n * (K / 8));
+    const int g = (w * 8) / group_size;
+    const uint4 u = gptq_dequant8(qw[i], sz[(long long)g * 2 * N + n], sz[(long long)g * 2 * N + N + n]);
+    *reinterpret_cast<uint4*>(out + (long long)n * K + w * 8) = u;
+  }
+}
+
+// out[r, j] = x[r, perm[j]] (bf16); one row staged in shared memory per iteration.
+__global__ void __launch_bounds__(256) permute_cols_kernel(const __nv_bfloat16* x, const int* perm, __nv_bfloat16* out,
+                                                           int rows, int K, long long ldx, long long ldo) {
+  extern __shared__ __align__(16) uint8_t prow_raw[];
+  __nv_bfloat16* rowbuf = reinterpret_cast<__nv_bfloat16*>(prow_raw);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + (long long)r * ldx);
+    for (int c = threadIdx.x; c < K / 8; c += blockDim.x) reinterpret_cast<uint4*>(rowbuf)[c] = src[c];
+    __syncthreads();
+    for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+      const int4 p0 = __ldg(reinterpret_cast<const int4*>(perm) + 2 * c);
+      const int4 p1 = __ldg(reinterpret_cast<const int4*>(perm) + 2 * c + 1);
+      __nv_bfloat162 h0, h1, h2, h3;
+      h0.x = rowbuf[p0.x]; h0.y = rowbuf[p0.y];
+      h1.x = rowbuf[p0.z]; h1.y = rowbuf[p0.w];
+      h2.x = rowbuf[p1.x]; h2.y = rowbuf[p1.y];
+      h3.x = rowbuf[p1.z]; h3.y = rowbuf[p1.w];
+      uint4 u;
+      u.x = *reinterpret_cast<uint32_t*>(&h0);
+      u.y = *reinterpret_cast<uint32_t*>(&h1);
+      u.z = *reinterpret_cast<uint32_t*>(&h2);
+      u.w = *reinterpret_cast<uint32_t*>(&h3);
+      reinterpret_cast<uint4*>(out + (long long)r * ldo)[c] = u;
+    }
+    __syncthreads();
+  }
 }
 
 }  // namespace sa3
@@ -755,5 +992,103 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
     if ((rc = ensure_smem(gemm_tc_kernel<false>, GEMM_SMEM))) return rc;
     gemm_tc_kernel<false><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
   }
+  return launch_status();
+}
+
+
+extern "C" int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, void* C, int M, int N, int K,
+                             long long lda, long long ldc, int group_size, const sa3_epilogue* epi, void* stream) {
+  if (!A || !qw || !sz || !C || M <= 0 || N <= 0 || K <= 0) return SA3_ERR_ARG;
+  if (group_size <= 0 || group_size % 64 || K % group_size || N % GEMM_BN) return SA3_ERR_UNSUPPORTED;
+  if (!aligned16(A) || !aligned16(qw) || !aligned16(sz) || !aligned16(C) || (lda % 8) || lda < K) return SA3_ERR_ALIGN;
+  sa3_epilogue e{};
+  if (epi) e = *epi;
+  if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_QK_NORM) return SA3_ERR_ARG;
+  const int celt = e.c_f32 ? 4 : 2;
+  if ((ldc * celt) % 16) return SA3_ERR_ALIGN;
+  if (e.kind == SA3_EPI_SWIGLU ? ldc < N / 2 : ldc < N) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_SWIGLU && e.c_f32) return SA3_ERR_UNSUPPORTED;
+  const bool res_kind = e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL;
+  if (res_kind && (!e.residual || !aligned16(e.residual) || (e.ld_residual * celt) % 16)) return SA3_ERR_ARG;
+  if (e.kind == SA3_EPI_GATED_RESIDUAL &&
+      (!e.gate || !aligned16(e.gate) || e.ld_gate % 4 || (!e.row_batch && e.rows_per_batch <= 0)))
+    return SA3_ERR_ARG;
+  if (e.bias && !aligned16(e.bias)) return SA3_ERR_ALIGN;
+  if (e.kind == SA3_EPI_QK_NORM) {
+    if (e.qk_group_width <= 0 || e.qk_group_width % 64 || N > 8 * e.qk_group_width) return SA3_ERR_ARG;
+    if (e.qk_rope_mask && (!e.cos_sin || e.max_pos <= 0 || (!e.row_pos && e.rows_per_batch <= 0)))
+      return SA3_ERR_ARG;
+  }
+  if (e.seg_in < 0 || (e.seg_in > 0 && e.seg_out <= 0)) return SA3_ERR_ARG;
+  CUtensorMap tmA, tmW, tmSZ;
+  int rc;
+  if ((rc = make_tmap_2d(&tmA, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, 64, GEMM_BM))) return rc;
+  if ((rc = make_tmap_2d(&tmW, qw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, K / 8, N, K / 8, 8, GEMM_BN,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  const int G = K / group_size;
+  if ((rc = make_tmap_2d(&tmSZ, sz, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 2 * (uint64_t)N, G, 2 * (uint64_t)N, 256, 1,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.C = C;
+  p.a_scale = nullptr;
+  p.b_scale = nullptr;
+  p.epi = e;
+  const int tiles_n = N / GEMM_BN;
+  const int num_tiles = tiles_n * ((M + GEMM_BM - 1) / GEMM_BM);
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define SA3_GQ_CASE(K_)                                                                                        \
+  case K_:                                                                                                     \
+    if ((rc = ensure_smem(gemm_gptq_kernel<K_>, GQ_SMEM))) return rc;                                          \
+    gemm_gptq_kernel<K_><<<grid, GQ_THREADS, GQ_SMEM, st>>>(tmA, tmW, tmSZ, p, tiles_n, num_tiles, group_size); \
+    break;
+  switch (e.kind) {
+    SA3_GQ_CASE(SA3_EPI_STORE)
+    SA3_GQ_CASE(SA3_EPI_SILU)
+    SA3_GQ_CASE(SA3_EPI_SWIGLU)
+    SA3_GQ_CASE(SA3_EPI_GATED_RESIDUAL)
+    SA3_GQ_CASE(SA3_EPI_RESIDUAL)
+    SA3_GQ_CASE(SA3_EPI_QK_NORM)
+    default:
+      return SA3_ERR_ARG;
+  }
+#undef SA3_GQ_CASE
+  return launch_status();
+}
+
+extern "C" int sa3_gptq_dequant(const void* qw, const float* sz, void* out, int N, int K, int group_size,
+                                void* stream) {
+  if (!qw || !sz || !out || N <= 0 || K <= 0 || K % 8 || group_size <= 0 || K % group_size) return SA3_ERR_ARG;
+  if (!aligned16(out) || K % 8) return SA3_ERR_ALIGN;
+  const long long words = (long long)N * (K / 8);
+  long long grid = (words + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  gptq_dequant_kernel<<<(int)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint32_t*>(qw), sz, reinterpret_cast<__nv_bfloat16*>(out), N, K, group_size);
+  return launch_status();
+}
+
+extern "C" int sa3_permute_cols(const void* x, const int* perm, void* out, int rows, int K, long long ldx,
+                                long long ldo, void* stream) {
+  if (!x || !perm || !out || rows <= 0 || K <= 0 || K % 8 || ldx < K || ldo < K) return SA3_ERR_ARG;
+  if (!aligned16(x) || !aligned16(out) || !aligned16(perm) || ldx % 8 || ldo % 8) return SA3_ERR_ALIGN;
+  const int smem = K * 2;
+  if (smem > 96 * 1024) return SA3_ERR_UNSUPPORTED;
+  int rc;
+  // the attribute is set once per device, so set it to the largest row this kernel accepts
+  if ((rc = ensure_smem(permute_cols_kernel, 96 * 1024))) return rc;
+  const int grid = rows < 148 * 8 ? rows : 148 * 8;
+  permute_cols_kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), perm, reinterpret_cast<__nv_bfloat16*>(out), rows, K, ldx, ldo);
   return launch_status();
 }

@@ -35,7 +35,8 @@ import torch
 
 from . import ops
 from . import _lib
-from .quant import interleave_swiglu_rows, quantize_weight_e4m3
+from . import gptq as _gptq
+from .quant import interleave_swiglu_rows, quantize_weight_e4m3, swiglu_interleave_index
 
 QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_kv",
                   "cross_attn.to_out", "ff.ff.0.proj", "ff.ff.2")
@@ -55,18 +56,19 @@ def _pad_cols(w: torch.Tensor, mult: int = 8) -> torch.Tensor:
 class Lin:
     """A prepared linear: weight [N, K] (bf16 or e4m3) on the device, optional fp32 per-row scale and bias."""
 
-    w: torch.Tensor
+    w: Optional[torch.Tensor]
     scale: Optional[torch.Tensor]
     bias: Optional[torch.Tensor]
     fp8: bool
+    gptq: Optional[dict] = None  # repacked int4 layer (sa3_b200.gptq.repack layout) on the device
 
     @property
     def n(self):
-        return self.w.shape[0]
+        return self.gptq["n"] if self.gptq is not None else self.w.shape[0]
 
 
 class _Workspace:
-    def __init__(self, cfg, B: int, L: int, Tc: int, dev, fp8: bool):
+    def __init__(self, cfg, B: int, L: int, Tc: int, dev, fp8: bool, gptq_k: int = 0):
         D = cfg.embed_dim
         N = L + cfg.num_memory_tokens
         M = B * N
@@ -93,6 +95,8 @@ class _Workspace:
         self.amax = torch.zeros(self.nslots, device=dev, dtype=torch.float32)
         self.scale = torch.zeros(self.nslots, device=dev, dtype=torch.float32)
         self.small = torch.empty(B, 8 * D, device=dev, dtype=bf)
+        # act-order gather buffer of the GPTQ path (inputs of every int4 linear)
+        self.xperm = torch.empty(max(M, B * Tc), gptq_k, device=dev, dtype=bf) if gptq_k else None
 
 
 class DiTEngine:
@@ -109,6 +113,9 @@ class DiTEngine:
         if cfg.head_dim != 64:
             raise NotImplementedError("head_dim must be 64")
         sd = {k: v.detach().float().cpu() for k, v in module.state_dict().items()}
+        self.gptq_layers = gptq_layers or {}
+        if mode == "gptq" and not self.gptq_layers:
+            raise ValueError("mode 'gptq' needs gptq_layers (name -> GPTQ tensors or a repacked layer)")
         self.lin: Dict[str, Lin] = {}
         for name in sorted({k[:-len(".weight")] for k in sd if k.endswith(".weight")}):
             if name in ("preprocess_conv", "postprocess_conv", "transformer.project_in", "transformer.project_out"):
@@ -129,11 +136,21 @@ class DiTEngine:
         self.ws: Optional[_Workspace] = None
         ramp = torch.linspace(0, 1, cfg.timestep_features_dim // 2, dtype=torch.float32)
         self.t_freqs = torch.exp(ramp * (math.log(10000.0) - math.log(0.5)) + math.log(0.5)).to(self.dev)
-        if mode == "gptq":
-            raise NotImplementedError("GPTQ engine path is built on sa3_b200.gptq")
+        self.gptq_k = max([ln.gptq["k"] for ln in self.lin.values() if ln.gptq is not None], default=0)
 
     # ------------------------------------------------------------------ prep
     def _prep(self, name, w, b, quantized: bool) -> Lin:
+        if self.mode == "gptq" and name in self.gptq_layers:
+            packed = self.gptq_layers[name]
+            if not isinstance(packed, dict):  # raw GPTQ tensors (qweight, qzeros, scales, g_idx)
+                packed = _gptq.repack(*packed)
+            packed = _gptq.to_device(packed, self.dev)
+            if name.endswith("ff.ff.0.proj"):
+                idx = swiglu_interleave_index(packed["n"])
+                packed = _gptq.reorder_rows(packed, idx)
+                b = None if b is None else b[idx]
+            bias = None if b is None else b.to(self.dev, torch.float32).contiguous()
+            return Lin(None, None, bias, False, packed)
         if name.endswith("ff.ff.0.proj"):
             w, b = interleave_swiglu_rows(w, b)
         w = _pad_cols(w)
@@ -146,7 +163,7 @@ class DiTEngine:
     def _workspace(self, B, L, Tc) -> _Workspace:
         ws = self.ws
         if ws is None or (ws.B, ws.L, ws.Tc) != (B, L, Tc):
-            self.ws = ws = _Workspace(self.cfg, B, L, Tc, self.dev, self.fp8)
+            self.ws = ws = _Workspace(self.cfg, B, L, Tc, self.dev, self.fp8, self.gptq_k)
         N = ws.N
         if self.rope is None or self.rope.shape[0] < N:
             self.rope = ops.rope_table(N, 32, device=self.dev)
@@ -154,6 +171,10 @@ class DiTEngine:
 
     # ------------------------------------------------------------------ helpers
     def _gemm(self, x, lin: Lin, out=None, x_scale=None, **kw):
+        if lin.gptq is not None:
+            g = lin.gptq
+            xp = ops.permute_cols(x, g["perm"], self.ws.xperm[:x.shape[0], :g["k"]])
+            return ops.gptq_gemm(xp, g["qw"], g["sz"], g["n"], out, group_size=g["group_size"], bias=lin.bias, **kw)
         if lin.fp8 and x.dtype != torch.float8_e4m3fn:
             raise RuntimeError("fp8 linear needs a quantized activation")
         return ops.gemm(x, lin.w, out, a_scale=x_scale if lin.fp8 else None, b_scale=lin.scale, bias=lin.bias, **kw)

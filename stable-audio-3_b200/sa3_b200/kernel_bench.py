@@ -12,6 +12,7 @@ Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
   attn_cross differential cross-attention over 128 context tokens
   norm_fp8   RMSNorm + modulate of the fp32 stream: amax pass + e4m3 write pass
   qknorm     qk RMSNorm + RoPE on q, k, q_diff, k_diff in place
+  ff1_gptq   GLU.proj GPTQ int4 GEMM (group 128, act-order gather included separately), M = 16 x 2648
 Each case's operands exceed the 126 MB L2.
 """
 from __future__ import annotations
@@ -25,6 +26,7 @@ from . import _lib, ops
 from .quant import interleave_swiglu_rows, quantize_weight_e4m3
 
 B, L, NM, D, H = 2, 8183, 64, 1536, 24
+N_GPTQ = 2584 + 64
 N = L + NM
 M = B * N
 
@@ -88,6 +90,16 @@ def case(name: str, iters: int) -> dict:
                                    heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=128)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 4.0 * 64 * N * 128 * H * 2 * B / ms / 1e9}
+    if name == "ff1_gptq":
+        from .gptq import random_layer
+        Mg = 16 * N_GPTQ
+        lay = random_layer(12288, 1536, 128, g, dev)
+        a = torch.randn(Mg, 1536, device=dev).bfloat16()
+        out = torch.empty(Mg, 6144, device=dev, dtype=torch.bfloat16)
+        xp = torch.empty_like(a)
+        ms_perm = _time(lambda: ops.permute_cols(a, lay["perm"], xp), iters)
+        ms = _time(lambda: ops.gptq_gemm(xp, lay["qw"], lay["sz"], 12288, out, kind=_lib.EPI_SWIGLU), iters)
+        return {"case": name, "ms": ms, "tflops": 2.0 * Mg * 12288 * 1536 / ms / 1e9, "gather_ms": ms_perm}
     if name == "norm_fp8":
         x = torch.randn(M, D, device=dev)
         gam = torch.ones(D, device=dev)
@@ -113,7 +125,7 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "attn_diff", "attn_cross", "norm_fp8", "qknorm"]
+CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "attn_diff", "attn_cross", "norm_fp8", "qknorm", "ff1_gptq"]
 
 
 def main():

@@ -59,6 +59,35 @@ def _dt(t: torch.Tensor) -> int:
 
 
 # ---------------------------------------------------------------------- GEMM
+def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out) -> Epilogue:
+    epi = Epilogue()
+    epi.kind = kind
+    epi.bias = _ptr(bias)
+    epi.residual = _ptr(residual)
+    epi.ld_residual = _row_stride(residual) if residual is not None else 0
+    epi.gate = _ptr(gate)
+    epi.ld_gate = _row_stride(gate) if gate is not None else 0
+    epi.rows_per_batch = rows_per_batch
+    epi.row_batch = _ptr(row_batch)
+    epi.amax_out = _ptr(amax_out)
+    if seg is not None:
+        epi.seg_in, epi.seg_out, epi.seg_offset = seg
+    epi.c_f32 = 1 if out.dtype == torch.float32 else 0
+    if qk is not None:
+        gams = list(qk["gammas"])
+        _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"))
+        for i, gm in enumerate(gams):
+            epi.qk_gamma[i] = _ptr(gm)
+        epi.qk_group_width = int(qk["group_width"])
+        epi.qk_rope_mask = sum(1 << i for i, r in enumerate(qk.get("rope", [])) if r)
+        epi.qk_eps = float(qk.get("eps", 1e-6))
+        cs = qk.get("cos_sin")
+        epi.cos_sin = _ptr(cs)
+        epi.max_pos = cs.shape[0] if cs is not None else 0
+        epi.row_pos = _ptr(qk.get("row_pos"))
+    return epi
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_scale=None, b_scale=None,
          bias=None, kind: int = _lib.EPI_STORE, residual=None, gate=None, rows_per_batch: int = 0,
          row_batch=None, amax_out=None, seg=None, qk=None) -> torch.Tensor:
@@ -88,31 +117,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     for t, nm in ((a_scale, "a_scale"), (b_scale, "b_scale"), (bias, "bias"), (gate, "gate"), (amax_out, "amax")):
         if t is not None and t.dtype != torch.float32:
             raise RuntimeError(f"{nm} must be float32")
-    epi = Epilogue()
-    epi.kind = kind
-    epi.bias = _ptr(bias)
-    epi.residual = _ptr(residual)
-    epi.ld_residual = _row_stride(residual) if residual is not None else 0
-    epi.gate = _ptr(gate)
-    epi.ld_gate = _row_stride(gate) if gate is not None else 0
-    epi.rows_per_batch = rows_per_batch
-    epi.row_batch = _ptr(row_batch)
-    epi.amax_out = _ptr(amax_out)
-    if seg is not None:
-        epi.seg_in, epi.seg_out, epi.seg_offset = seg
-    epi.c_f32 = 1 if out.dtype == torch.float32 else 0
-    if qk is not None:
-        gams = list(qk["gammas"])
-        _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"))
-        for i, gm in enumerate(gams):
-            epi.qk_gamma[i] = _ptr(gm)
-        epi.qk_group_width = int(qk["group_width"])
-        epi.qk_rope_mask = sum(1 << i for i, r in enumerate(qk.get("rope", [])) if r)
-        epi.qk_eps = float(qk.get("eps", 1e-6))
-        cs = qk.get("cos_sin")
-        epi.cos_sin = _ptr(cs)
-        epi.max_pos = cs.shape[0] if cs is not None else 0
-        epi.row_pos = _ptr(qk.get("row_pos"))
+    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out)
     _count()
     rc = _lib.load().sa3_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _row_stride(a), _row_stride(b),
                               _row_stride(out), _dt(a), _ptr(a_scale), _ptr(b_scale), ctypes.byref(epi), _stream())
@@ -252,4 +257,46 @@ def diff_attn_swa(q_bat: torch.Tensor, k_bat: torch.Tensor, v_bat: torch.Tensor,
     rc = _lib.load().sa3_diff_attn_swa(q_bat.data_ptr(), k_bat.data_ptr(), v_bat.data_ptr(), out.data_ptr(),
                                        _dt(q_bat), B, N, num_heads, d, int(window), _stream())
     _lib.check(rc, "sa3_diff_attn_swa")
+    return out
+
+
+# ---------------------------------------------------------------------- GPTQ
+def gptq_gemm(a: torch.Tensor, qw: torch.Tensor, sz: torch.Tensor, n: int, out: Optional[torch.Tensor] = None, *,
+              group_size: int = 128, bias=None, kind: int = _lib.EPI_STORE, residual=None, gate=None,
+              rows_per_batch: int = 0, row_batch=None, amax_out=None, seg=None, qk=None) -> torch.Tensor:
+    """out = epilogue(a @ W^T) with W in the packed GPTQ layout of sa3_b200.gptq.repack; a must already hold the
+    act-order-permuted input channels."""
+    _need_cuda(a, qw, sz, out, bias, residual, gate, row_batch, amax_out)
+    if a.dtype != torch.bfloat16:
+        raise RuntimeError("GPTQ activations are bf16")
+    M, K = a.shape
+    ncols = n // 2 if kind == _lib.EPI_SWIGLU else n
+    if out is None:
+        out = torch.empty(M, ncols, device=a.device, dtype=torch.bfloat16)
+    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out)
+    _count()
+    rc = _lib.load().sa3_gptq_gemm(a.data_ptr(), qw.data_ptr(), sz.data_ptr(), out.data_ptr(), M, n, K,
+                                   _row_stride(a), _row_stride(out), group_size, ctypes.byref(epi), _stream())
+    _lib.check(rc, "sa3_gptq_gemm")
+    return out
+
+
+def gptq_dequant(qw: torch.Tensor, sz: torch.Tensor, n: int, k: int, group_size: int = 128) -> torch.Tensor:
+    _need_cuda(qw, sz)
+    out = torch.empty(n, k, device=qw.device, dtype=torch.bfloat16)
+    _count()
+    rc = _lib.load().sa3_gptq_dequant(qw.data_ptr(), sz.data_ptr(), out.data_ptr(), n, k, group_size, _stream())
+    _lib.check(rc, "sa3_gptq_dequant")
+    return out
+
+
+def permute_cols(x: torch.Tensor, perm: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need_cuda(x, perm, out)
+    rows, K = x.shape
+    if out is None:
+        out = torch.empty(rows, K, device=x.device, dtype=x.dtype)
+    _count()
+    rc = _lib.load().sa3_permute_cols(x.data_ptr(), perm.data_ptr(), out.data_ptr(), rows, K, _row_stride(x),
+                                      _row_stride(out), _stream())
+    _lib.check(rc, "sa3_permute_cols")
     return out

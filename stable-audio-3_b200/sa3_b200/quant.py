@@ -25,14 +25,18 @@ E4M3_MAX = 448.0
 SWIGLU_BLOCK = 128
 
 
-def interleave_swiglu_rows(w: torch.Tensor, b=None, block: int = SWIGLU_BLOCK):
-    """Reorder GLU.proj rows [x (I rows) ; gate (I rows)] into blocks [x_t (128) ; gate_t (128)] so each
-    256-wide GEMM tile holds matching x and gate columns and the SwiGLU fuses into its epilogue."""
-    two_i = w.shape[0]
+def swiglu_interleave_index(two_i: int, block: int = SWIGLU_BLOCK) -> torch.Tensor:
+    """Row order that turns GLU.proj rows [x (I rows) ; gate (I rows)] into blocks [x_t (128) ; gate_t (128)]."""
     inner = two_i // 2
     if inner % block:
         raise ValueError(f"SwiGLU inner dim {inner} must be a multiple of {block}")
-    idx = torch.arange(two_i).view(2, inner // block, block).permute(1, 0, 2).reshape(-1)
+    return torch.arange(two_i).view(2, inner // block, block).permute(1, 0, 2).reshape(-1)
+
+
+def interleave_swiglu_rows(w: torch.Tensor, b=None, block: int = SWIGLU_BLOCK):
+    """Reorder GLU.proj rows [x (I rows) ; gate (I rows)] into blocks [x_t (128) ; gate_t (128)] so each
+    256-wide GEMM tile holds matching x and gate columns and the SwiGLU fuses into its epilogue."""
+    idx = swiglu_interleave_index(w.shape[0], block)
     w2 = w[idx].contiguous()
     b2 = None if b is None else b[idx].contiguous()
     return w2, b2
