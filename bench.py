@@ -37,6 +37,11 @@ WORKLOADS = {
     "medium_fp8": dict(model="medium", mode="fp8", L=8183, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
     # medium DiT with GPTQ int4 weight-only linears (group 128, act-order), L = 2584, batch 16 (8 CFG pairs)
     "medium_gptq": dict(model="medium", mode="gptq", L=2584, prompts=8, Tc=128, cfg_scale=7.0, apg_scale=1.0),
+    # data-parallel sweep: 256 prompts, lengths ~ U{108..8183}, each with a CFG pair, LPT-sharded over the
+    # ranks and packed variable-length (no padding) in batches of <= 2^18 token rows; one step = one
+    # denoiser step over every prompt
+    "dp_varlen_fp8": dict(model="medium", mode="fp8", dp=True, n_prompts=256, len_lo=108, len_hi=8183, Tc=128,
+                          cfg_scale=7.0, apg_scale=1.0, max_tokens=1 << 18),
     # small DiT in bf16 (24 blocks, dim 1024, L = 2584, CFG pair)
     "small_bf16": dict(model="small", mode="bf16", L=2584, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
 }
@@ -203,6 +208,67 @@ def run_reference(args, wl, world, rank):
 
 
 # ----------------------------------------------------------------------------- our arm
+def run_dp_varlen(args, wl, world, rank, local):
+    """Variable-length data-parallel sweep (no collective in the step; max-over-ranks device time)."""
+    import numpy as np
+
+    from sa3_b200 import dist as sdist
+    from sa3_b200.modules import DiffusionTransformer, init_synthetic_
+
+    dev = torch.device("cuda", local)
+    cfg = model_cfg(wl["model"])
+    model = init_synthetic_(DiffusionTransformer(cfg), seed=0).quantize(wl["mode"])
+    eng = model.engine()
+    rng = np.random.default_rng(0)
+    lengths = [int(x) for x in rng.integers(wl["len_lo"], wl["len_hi"] + 1, size=wl["n_prompts"])]
+    shard = sdist.lpt_shard([sdist.prompt_cost(n) for n in lengths], world)[rank]
+    mbs = sdist.micro_batches(shard, lengths, wl["max_tokens"])
+    g = torch.Generator().manual_seed(1000 + rank)
+    inputs = {}
+    for i in shard:
+        inputs[i] = (torch.randn(cfg.io_channels, lengths[i], generator=g).to(dev),
+                     torch.randn(wl["Tc"], cfg.cond_token_dim, generator=g).to(dev),
+                     torch.randn(cfg.global_cond_dim, generator=g).to(dev))
+    t = torch.full((max(len(mb) for mb in mbs),), 0.5, device=dev)
+
+    def one_step():
+        for mb in mbs:
+            xs = [inputs[i][0] for i in mb]
+            cond = torch.stack([inputs[i][1] for i in mb])
+            gemb = torch.stack([inputs[i][2] for i in mb])
+            eng.forward_varlen(xs, t[:len(mb)], cond, gemb, None, cfg_scale=wl["cfg_scale"], apg_scale=wl["apg_scale"])
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            one_step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            one_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    tokens = 2 * sum(lengths)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8-e4m3 linears / bf16 attention", "data": "synthetic",
+            "config": {"workload": args.workload, "model": f"sa3-{wl['model']} DiT, random init",
+                       "prompts": wl["n_prompts"], "lengths": f"U{{{wl['len_lo']}..{wl['len_hi']}}} seed 0",
+                       "tokens_per_step": tokens, "parallelism": f"dp{world} (LPT, CFG pair per GPU)",
+                       "packing": f"variable-length, <= {wl['max_tokens']} rows per batch",
+                       "micro_batches_rank0": len(mbs)},
+            "clocks": clk,
+        }), flush=True)
+
+
 def run_ours(args, wl, world, rank, local):
     from sa3_b200 import ops, _lib
     from sa3_b200.modules import DiffusionTransformer, init_synthetic_
@@ -361,7 +427,10 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        run_ours(args, wl, world, rank, local)
+        if wl.get("dp"):
+            run_dp_varlen(args, wl, world, rank, local)
+        else:
+            run_ours(args, wl, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -102,6 +102,9 @@ typedef struct {
   const float* cos_sin;
   int max_pos;
   const int* row_pos;
+  /* optional int32 [M]: output (and residual) row of GEMM row m; overrides seg_*. Packs variable-length
+     sequences (project_in, the local-conditioning add) into the token-row stream. */
+  const int* out_row_map;
 } sa3_epilogue;
 
 int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,
@@ -166,10 +169,11 @@ int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, long long ld
 
 /* Element type conversion of a row-major [rows, cols] view: fp32 <-> bf16
  * (round to nearest even). cols must be a multiple of 8, rows 16-byte aligned.
+ * src_rows (optional int32 [rows]): output row r reads input row src_rows[r].
  * Used to hand the fp32 residual stream to a bf16 GEMM operand (project_out,
  * transformer.py:1267). */
 int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype, int rows, int cols, long long ldx,
-                long long ldo, void* stream);
+                long long ldo, const int* src_rows, void* stream);
 
 /* ---------------------------------------------- glue: qk-norm + partial RoPE (a5, a6)
  *

@@ -40,6 +40,7 @@ struct GemmParams {
 };
 
 __device__ __forceinline__ int out_row_of(const sa3_epilogue& e, int m) {
+  if (e.out_row_map) return __ldg(e.out_row_map + m);
   return e.seg_in > 0 ? (m / e.seg_in) * e.seg_out + e.seg_offset + (m % e.seg_in) : m;
 }
 

@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
 struct ConvParams {
   const void* x;
   void* out;
+  const int* src_rows;
   int x_f32, out_f32;
   int rows, cols;
   long long ldx, ldo;
@@ -334,13 +335,14 @@ __global__ void __launch_bounds__(256) convert_kernel(ConvParams p) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / cpr;
     const int c = (int)(i - r * cpr);
+    const long long rs = p.src_rows ? (long long)__ldg(p.src_rows + r) : r;
     float v[8];
     if (p.x_f32) {
-      const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + r * p.ldx + c * 8);
+      const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + rs * p.ldx + c * 8);
       const float4 a = s[0], b = s[1];
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     } else {
-      unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + r * p.ldx + c * 8), v);
+      unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + rs * p.ldx + c * 8), v);
     }
     if (p.out_f32) {
       float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + r * p.ldo + c * 8);
@@ -482,12 +484,12 @@ extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, in
 }
 
 extern "C" int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype, int rows, int cols, long long ldx,
-                           long long ldo, void* stream) {
+                           long long ldo, const int* src_rows, void* stream) {
   if (!x || !out || rows <= 0 || cols <= 0 || (cols % 8) || ldx < cols || ldo < cols) return SA3_ERR_ARG;
   if ((x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32) || (out_dtype != SA3_DT_BF16 && out_dtype != SA3_DT_F32))
     return SA3_ERR_DTYPE;
   if (!aligned16(x) || !aligned16(out) || (ldx % 8) || (ldo % 8)) return SA3_ERR_ALIGN;
-  ConvParams p{x, out, x_dtype == SA3_DT_F32, out_dtype == SA3_DT_F32, rows, cols, ldx, ldo};
+  ConvParams p{x, out, src_rows, x_dtype == SA3_DT_F32, out_dtype == SA3_DT_F32, rows, cols, ldx, ldo};
   convert_kernel<<<grid_for((long long)rows * (cols / 8), 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return launch_status();
 }

@@ -55,6 +55,7 @@ class Epilogue(ctypes.Structure):
         ("cos_sin", c_vp),
         ("max_pos", c_int),
         ("row_pos", c_vp),
+        ("out_row_map", c_vp),
     ]
 
 
@@ -69,7 +70,7 @@ SIGNATURES = {
     "sa3_permute_cols": [c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp],
     "sa3_rmsnorm_modulate": [c_vp, c_int, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                              c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp],
-    "sa3_convert": [c_vp, c_int, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_vp],
+    "sa3_convert": [c_vp, c_int, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_vp, c_vp],
     "sa3_quantize_e4m3": [c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_vp, c_vp, c_vp],
     "sa3_qk_norm_rope": [c_vp, c_int, c_ll, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_vp),
                          ctypes.POINTER(c_int), c_float, c_vp, c_int, c_int, c_vp, c_vp],

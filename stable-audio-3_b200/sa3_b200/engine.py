@@ -29,6 +29,8 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
+
+import numpy as np
 from typing import Dict, Optional
 
 import torch
@@ -68,12 +70,37 @@ class Lin:
 
 
 class _Workspace:
-    def __init__(self, cfg, B: int, L: int, Tc: int, dev, fp8: bool, gptq_k: int = 0):
+    """Device buffers and packing tables for one set of sequence lengths (reused across steps and graph replays).
+
+    Sequences are packed back to back as token rows: sequence b occupies stream rows [cu[b], cu[b+1]),
+    memory tokens first, then its L_b latents. Every per-row table the kernels take is built here once:
+    row_batch (sequence of each row), row_pos (RoPE position), lat_rows (stream row of each latent row)
+    and mem_rows (stream rows of the memory tokens)."""
+
+    def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0):
         D = cfg.embed_dim
-        N = L + cfg.num_memory_tokens
-        M = B * N
+        nm = cfg.num_memory_tokens
+        B = len(lengths)
+        Ns = [L + nm for L in lengths]
+        M = sum(Ns)
+        R = sum(lengths)
         nq = 5 if cfg.differential else 3
-        self.B, self.L, self.N, self.M, self.Tc = B, L, N, M, Tc
+        self.lengths, self.B, self.M, self.R, self.Tc = tuple(lengths), B, M, R, Tc
+        self.max_n = max(Ns)
+        cu = np.zeros(B + 1, dtype=np.int64)
+        cu[1:] = np.cumsum(Ns)
+        self.cu_host = cu
+        row_batch = np.repeat(np.arange(B, dtype=np.int32), Ns)
+        row_pos = np.concatenate([np.arange(n, dtype=np.int32) for n in Ns])
+        lat_rows = np.concatenate([np.arange(cu[b] + nm, cu[b + 1], dtype=np.int32) for b in range(B)])
+        mem_rows = np.concatenate([np.arange(cu[b], cu[b] + nm, dtype=np.int64) for b in range(B)]) if nm else None
+        self.cu = torch.from_numpy(cu.astype(np.int32)).to(dev)
+        self.cu_ctx = torch.arange(0, (B + 1) * Tc, max(Tc, 1), dtype=torch.int32, device=dev)[:B + 1] if Tc else None
+        self.row_batch = torch.from_numpy(row_batch).to(dev)
+        self.row_pos = torch.from_numpy(row_pos).to(dev)
+        self.lat_rows = torch.from_numpy(lat_rows).to(dev)
+        self.lat_off = [int(x) for x in np.concatenate([[0], np.cumsum(lengths)])]
+        self.mem_rows = torch.from_numpy(mem_rows).to(dev) if nm else None
         bf = torch.bfloat16
         self.h = torch.empty(M, D, device=dev, dtype=torch.float32)  # fp32 residual stream
         self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
@@ -84,11 +111,11 @@ class _Workspace:
         self.kv = torch.empty(max(B * Tc, 1), (3 if cfg.differential else 2) * D, device=dev, dtype=bf)
         self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
         self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
-        self.t1 = torch.empty(B * L, D, device=dev, dtype=bf)
-        self.loc = torch.zeros(B * L, 264, device=dev, dtype=bf)
-        self.xin = torch.empty(B * L, cfg.io_channels, device=dev, dtype=bf)
-        self.hb = torch.empty(B * L, D, device=dev, dtype=bf)  # bf16 copy of the stream for project_out
-        self.out = torch.empty(B * L, cfg.io_channels, device=dev, dtype=torch.float32)
+        self.t1 = torch.empty(R, D, device=dev, dtype=bf)
+        self.loc = torch.zeros(R, 264, device=dev, dtype=bf)
+        self.xin = torch.empty(R, cfg.io_channels, device=dev, dtype=bf)
+        self.hb = torch.empty(R, D, device=dev, dtype=bf)  # bf16 copy of the latent rows for project_out
+        self.out = torch.empty(R, cfg.io_channels, device=dev, dtype=torch.float32)
         self.ctx = torch.empty(max(B * Tc, 1), D, device=dev, dtype=bf)
         self.ctx8 = torch.empty(max(B * Tc, 1), D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.nslots = 8 * cfg.depth + 8
@@ -160,13 +187,13 @@ class DiTEngine:
             return Lin(wq.to(self.dev).contiguous(), s.to(self.dev), bias, True)
         return Lin(w.to(self.dev, torch.bfloat16).contiguous(), None, bias, False)
 
-    def _workspace(self, B, L, Tc) -> _Workspace:
+    def _workspace(self, lengths, Tc) -> _Workspace:
         ws = self.ws
-        if ws is None or (ws.B, ws.L, ws.Tc) != (B, L, Tc):
-            self.ws = ws = _Workspace(self.cfg, B, L, Tc, self.dev, self.fp8, self.gptq_k)
-        N = ws.N
-        if self.rope is None or self.rope.shape[0] < N:
-            self.rope = ops.rope_table(N, 32, device=self.dev)
+        if ws is None or (ws.lengths, ws.Tc) != (tuple(lengths), Tc):
+            self.ws = ws = None
+            self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k)
+        if self.rope is None or self.rope.shape[0] < ws.max_n:
+            self.rope = ops.rope_table(ws.max_n, 32, device=self.dev)
         return ws
 
     # ------------------------------------------------------------------ helpers
@@ -182,7 +209,7 @@ class DiTEngine:
     def _norm_to_a(self, ws, x, gamma, slot, mod=None, scale_off=0, shift_off=0):
         """RMSNorm(+modulate) of the stream into ws.a; FP8: two passes (amax, quantize)."""
         cfg = self.cfg
-        kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, rows_per_batch=ws.N)
+        kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, row_batch=ws.row_batch)
         if self.fp8:
             am = ws.amax[slot:slot + 1]
             sc = ws.scale[slot:slot + 1]
@@ -243,13 +270,62 @@ class DiTEngine:
 
     @torch.no_grad()
     def inner(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None):
-        """DiffusionTransformer._forward + ContinuousTransformer.forward on the kernels; returns fp32 [B, C, L]."""
-        cfg = self.cfg
-        D = cfg.embed_dim
+        """DiffusionTransformer._forward + ContinuousTransformer.forward on the kernels for B sequences of one
+        length; returns fp32 [B, C, L]."""
         B, C, L = x.shape
         Tc = cross_attn_cond.shape[1] if cross_attn_cond is not None else 0
-        ws = self._workspace(B, L, Tc)
-        N, M = ws.N, ws.M
+        ws = self._workspace([L] * B, Tc)
+        ws.xin.view(B, L, C).copy_(x.transpose(1, 2))
+        if local_add_cond is not None and self.cfg.local_add_cond_dim > 0:
+            ws.loc.view(B, L, -1)[:, :, :self.cfg.local_add_cond_dim].copy_(local_add_cond.transpose(1, 2))
+        self._trunk(ws, t, cross_attn_cond, global_embed, local_add_cond is not None)
+        return ws.out.view(B, L, C).transpose(1, 2)
+
+    @torch.no_grad()
+    def inner_varlen(self, xs, t, cross_attn_cond=None, global_embed=None, local_add_conds=None):
+        """Variable-length batch: xs = list of [C, L_b] latents (local_add_conds likewise [257, L_b]); t [B],
+        cross_attn_cond [B, Tc, 768], global_embed [B, 768]. The sequences are packed back to back (no
+        padding); returns a list of fp32 [C, L_b]."""
+        lengths = [int(x.shape[-1]) for x in xs]
+        Tc = cross_attn_cond.shape[1] if cross_attn_cond is not None else 0
+        ws = self._workspace(lengths, Tc)
+        dev = self.dev
+        for b, x in enumerate(xs):
+            ws.xin[ws.lat_off[b]:ws.lat_off[b + 1]].copy_(x.to(dev).transpose(0, 1))
+        has_local = local_add_conds is not None and self.cfg.local_add_cond_dim > 0
+        if has_local:
+            for b, lc in enumerate(local_add_conds):
+                ws.loc[ws.lat_off[b]:ws.lat_off[b + 1], :self.cfg.local_add_cond_dim].copy_(lc.transpose(0, 1))
+        self._trunk(ws, t.to(dev), None if cross_attn_cond is None else cross_attn_cond.to(dev),
+                    None if global_embed is None else global_embed.to(dev), has_local)
+        return [ws.out[ws.lat_off[b]:ws.lat_off[b + 1]].transpose(0, 1) for b in range(len(xs))]
+
+    @torch.no_grad()
+    def forward_varlen(self, xs, t, cross_attn_cond, global_embed=None, local_add_conds=None, cfg_scale: float = 1.0,
+                       apg_scale: float = 1.0):
+        """DiffusionTransformer.forward over prompts of different lengths: each prompt's CFG pair runs in one
+        packed batch (cond halves first, then the unconditional halves), then the per-prompt CFG/APG combine."""
+        P = len(xs)
+        dev = self.dev
+        t = t.to(dev, torch.float32)
+        if cfg_scale == 1.0:
+            return self.inner_varlen(xs, t, cross_attn_cond, global_embed, local_add_conds)
+        cc = cross_attn_cond.to(dev)
+        outs = self.inner_varlen(
+            list(xs) + list(xs), torch.cat([t, t]), torch.cat([cc, torch.zeros_like(cc)]),
+            None if global_embed is None else torch.cat([global_embed, global_embed]).to(dev),
+            None if local_add_conds is None else list(local_add_conds) + list(local_add_conds))
+        res = []
+        for i in range(P):
+            pair = torch.stack([outs[i], outs[P + i]])
+            res.append(self.cfg_combine(xs[i].to(dev)[None], t[i:i + 1], pair, cfg_scale, apg_scale)[0])
+        return res
+
+    def _trunk(self, ws: _Workspace, t, cross_attn_cond, global_embed, has_local: bool):
+        """The trunk on packed sequences: reads ws.xin / ws.loc, writes ws.out (fp32 [R, C])."""
+        cfg = self.cfg
+        D = cfg.embed_dim
+        B, Tc = ws.B, ws.Tc
         nm = cfg.num_memory_tokens
         ln = self.lin
         ws.amax.zero_()
@@ -281,21 +357,19 @@ class DiTEngine:
             ops.absmax(ctx, ws.amax[slot:slot + 1])
             ctx_a, ctx_s = self._quant(ws, ctx, ws.ctx8, slot)
 
-        has_local = local_add_cond is not None and cfg.local_add_cond_dim > 0
-        if has_local:
-            ws.loc.view(B, L, -1)[:, :, :cfg.local_add_cond_dim].copy_(local_add_cond.transpose(1, 2))
-
-        # ---- trunk input: project_in (preprocess conv folded) into rows nm.. of each sequence
-        ws.xin.view(B, L, C).copy_(x.transpose(1, 2))
+        # ---- trunk input: project_in (preprocess conv folded) into each sequence's latent rows
         h = ws.h
-        self._gemm(ws.xin, ln["project_in"], h, seg=(L, N, nm))
+        self._gemm(ws.xin, ln["project_in"], h, out_row_map=ws.lat_rows)
         if nm:
-            h.view(B, N, D)[:, :nm].copy_(self.memory)
+            h.index_copy_(0, ws.mem_rows, self.memory.repeat(B, 1))
 
         wl, wr = cfg.sliding_window if cfg.sliding_window is not None else (-1, -1)
         diff = cfg.differential
         qkv, o, qx, kv = ws.qkv, ws.o, ws.qx, ws.kv
         H = cfg.num_heads
+        seq = dict(cu_seqlens_q=ws.cu, cu_seqlens_k=ws.cu, max_seqlen_q=ws.max_n, max_seqlen_k=ws.max_n)
+        xseq = dict(cu_seqlens_q=ws.cu, cu_seqlens_k=ws.cu_ctx, max_seqlen_q=ws.max_n, max_seqlen_k=Tc)
+        rb = ws.row_batch
         for i in range(cfg.depth):
             p = f"transformer.layers.{i}."
             ssi = ss[i]
@@ -306,19 +380,19 @@ class DiTEngine:
             # to_qkv with qk RMSNorm + RoPE fused into the epilogue (groups q | k | v | q_diff | k_diff)
             groups = [gq, gk, None, gq, gk] if diff else [gq, gk, None]
             rope = [True, True, False, True, True] if diff else [True, True, False]
-            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM, rows_per_batch=N,
-                       qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope))
+            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM,
+                       qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
+                               row_pos=ws.row_pos))
             am1 = ws.amax[s0 + 1:s0 + 2] if self.fp8 else None
             if diff:
                 ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
-                              k2=qkv[:, 4 * D:5 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N,
-                              window=(wl, wr), out=o, amax_out=am1)
+                              k2=qkv[:, 4 * D:5 * D], heads=H, window=(wl, wr), out=o, amax_out=am1, **seq)
             else:
-                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, batch=B, max_seqlen_q=N,
-                              max_seqlen_k=N, window=(wl, wr), out=o, amax_out=am1)
+                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, window=(wl, wr), out=o,
+                              amax_out=am1, **seq)
             oa, osc = self._quant(ws, o, ws.o8, s0 + 1)
             self._gemm(oa, ln[p + "self_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
-                       gate=ssi[:, 2 * D:3 * D], rows_per_batch=N)
+                       gate=ssi[:, 2 * D:3 * D], row_batch=rb)
             # -- cross-attention (transformer.py:1031-1035), no adaLN, no RoPE
             if ctx is not None and (p + "cross_attn.to_q") in ln:
                 c, csc = self._norm_to_a(ws, h, self.gam[p + "cross_attend_norm.gamma"], s0 + 2)
@@ -332,29 +406,27 @@ class DiTEngine:
                 am = ws.amax[s0 + 3:s0 + 4] if self.fp8 else None
                 if diff:
                     ops.attention(qx[:, 0:D], kv[:, 0:D], kv[:, 2 * D:3 * D], q2=qx[:, D:2 * D], k2=kv[:, D:2 * D],
-                                  heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc, out=o, amax_out=am)
+                                  heads=H, out=o, amax_out=am, **xseq)
                 else:
-                    ops.attention(qx, kv[:, 0:D], kv[:, D:2 * D], heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=Tc,
-                                  out=o, amax_out=am)
+                    ops.attention(qx, kv[:, 0:D], kv[:, D:2 * D], heads=H, out=o, amax_out=am, **xseq)
                 oa, osc = self._quant(ws, o, ws.o8, s0 + 3)
                 self._gemm(oa, ln[p + "cross_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_RESIDUAL, residual=h)
             # -- local additive conditioning, left-padded over the memory tokens (transformer.py:978-994, 77-88)
             if has_local and (p + "to_local_embed.0") in ln:
                 self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
-                self._gemm(ws.t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h, seg=(L, N, nm))
+                self._gemm(ws.t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h,
+                           out_row_map=ws.lat_rows)
             # -- feed-forward with adaLN (transformer.py:1042-1049)
             f, fsc = self._norm_to_a(ws, h, self.gam[p + "ff_norm.gamma"], s0 + 4, ssi, 3 * D, 4 * D)
             self._gemm(f, ln[p + "ff.ff.0.proj"], ws.u, x_scale=fsc, kind=_lib.EPI_SWIGLU,
                        amax_out=ws.amax[s0 + 5:s0 + 6] if self.fp8 else None)
             ua, usc = self._quant(ws, ws.u, ws.u8, s0 + 5)
             self._gemm(ua, ln[p + "ff.ff.2"], h, x_scale=usc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
-                       gate=ssi[:, 5 * D:6 * D], rows_per_batch=N)
+                       gate=ssi[:, 5 * D:6 * D], row_batch=rb)
 
         # ---- drop memory tokens, project_out (postprocess conv folded) (transformer.py:1265-1267, dit.py:297-304)
-        for b in range(B):
-            ops.convert(h[b * N + nm:(b + 1) * N], ws.hb[b * L:(b + 1) * L])
+        ops.convert(h, ws.hb, src_rows=ws.lat_rows)
         self._gemm(ws.hb, ln["project_out"], ws.out)
-        return ws.out.view(B, L, C).transpose(1, 2)
 
 
 class GraphedStep:

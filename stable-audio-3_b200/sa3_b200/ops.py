@@ -59,7 +59,8 @@ def _dt(t: torch.Tensor) -> int:
 
 
 # ---------------------------------------------------------------------- GEMM
-def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out) -> Epilogue:
+def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out,
+              out_row_map=None) -> Epilogue:
     epi = Epilogue()
     epi.kind = kind
     epi.bias = _ptr(bias)
@@ -73,6 +74,7 @@ def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, s
     if seg is not None:
         epi.seg_in, epi.seg_out, epi.seg_offset = seg
     epi.c_f32 = 1 if out.dtype == torch.float32 else 0
+    epi.out_row_map = _ptr(out_row_map)
     if qk is not None:
         gams = list(qk["gammas"])
         _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"))
@@ -90,7 +92,7 @@ def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, s
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_scale=None, b_scale=None,
          bias=None, kind: int = _lib.EPI_STORE, residual=None, gate=None, rows_per_batch: int = 0,
-         row_batch=None, amax_out=None, seg=None, qk=None) -> torch.Tensor:
+         row_batch=None, amax_out=None, seg=None, qk=None, out_row_map=None) -> torch.Tensor:
     """out = epilogue(a @ b.T * a_scale * b_scale + bias); a [M,K], b [N,K] (K-major), bf16 or e4m3.
 
     qk (for kind EPI_QK_NORM): dict(gammas=[per column group: fp32 [64] or None], group_width=int,
@@ -105,7 +107,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
         raise RuntimeError(f"K mismatch {K} vs {Kb}")
     ncols = N // 2 if kind == _lib.EPI_SWIGLU else N
     if out is None:
-        if seg is not None:
+        if seg is not None or out_row_map is not None:
             raise RuntimeError("row remap needs an explicit out")
         out = torch.empty(M, ncols, device=a.device, dtype=torch.bfloat16)
     if out.dtype not in (torch.bfloat16, torch.float32):
@@ -117,7 +119,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     for t, nm in ((a_scale, "a_scale"), (b_scale, "b_scale"), (bias, "bias"), (gate, "gate"), (amax_out, "amax")):
         if t is not None and t.dtype != torch.float32:
             raise RuntimeError(f"{nm} must be float32")
-    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out)
+    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out, out_row_map)
     _count()
     rc = _lib.load().sa3_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _row_stride(a), _row_stride(b),
                               _row_stride(out), _dt(a), _ptr(a_scale), _ptr(b_scale), ctypes.byref(epi), _stream())
@@ -173,13 +175,13 @@ def absmax(x: torch.Tensor, amax_out: torch.Tensor) -> None:
     _lib.check(rc, "sa3_quantize_e4m3(amax)")
 
 
-def convert(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-    """out = x cast between fp32 and bf16 (2-D row-major views of equal shape)."""
-    _need_cuda(x, out)
-    rows, cols = x.shape
+def convert(x: torch.Tensor, out: torch.Tensor, src_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = x cast between fp32 and bf16; with src_rows (int32), out[r] = x[src_rows[r]]."""
+    _need_cuda(x, out, src_rows)
+    rows, cols = out.shape
     _count()
     rc = _lib.load().sa3_convert(x.data_ptr(), _dt(x), out.data_ptr(), _dt(out), rows, cols, _row_stride(x),
-                                 _row_stride(out), _stream())
+                                 _row_stride(out), _ptr(src_rows), _stream())
     _lib.check(rc, "sa3_convert")
     return out
 
@@ -263,7 +265,8 @@ def diff_attn_swa(q_bat: torch.Tensor, k_bat: torch.Tensor, v_bat: torch.Tensor,
 # ---------------------------------------------------------------------- GPTQ
 def gptq_gemm(a: torch.Tensor, qw: torch.Tensor, sz: torch.Tensor, n: int, out: Optional[torch.Tensor] = None, *,
               group_size: int = 128, bias=None, kind: int = _lib.EPI_STORE, residual=None, gate=None,
-              rows_per_batch: int = 0, row_batch=None, amax_out=None, seg=None, qk=None) -> torch.Tensor:
+              rows_per_batch: int = 0, row_batch=None, amax_out=None, seg=None, qk=None,
+              out_row_map=None) -> torch.Tensor:
     """out = epilogue(a @ W^T) with W in the packed GPTQ layout of sa3_b200.gptq.repack; a must already hold the
     act-order-permuted input channels."""
     _need_cuda(a, qw, sz, out, bias, residual, gate, row_batch, amax_out)
@@ -273,7 +276,7 @@ def gptq_gemm(a: torch.Tensor, qw: torch.Tensor, sz: torch.Tensor, n: int, out: 
     ncols = n // 2 if kind == _lib.EPI_SWIGLU else n
     if out is None:
         out = torch.empty(M, ncols, device=a.device, dtype=torch.bfloat16)
-    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out)
+    epi = _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, seg, qk, out, out_row_map)
     _count()
     rc = _lib.load().sa3_gptq_gemm(a.data_ptr(), qw.data_ptr(), sz.data_ptr(), out.data_ptr(), M, n, K,
                                    _row_stride(a), _row_stride(out), group_size, ctypes.byref(epi), _stream())
