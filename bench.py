@@ -49,6 +49,17 @@ METRIC = "Medium DiT step latency (ms) + latent tokens/s at 1/2/4/8 B200, FP8/GP
 UNIT = "latent tokens/s"
 
 
+def _profiled_traffic(name):
+    """dram__bytes_read + dram__bytes_write of one launch, from the committed ncu summary of that kernel."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name)):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def _peaks():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -373,8 +384,11 @@ def run_ours(args, wl, world, rank, local):
     else:
         peak, peak_src = (peaks["bf16_tflops"], "measured bf16 burst (MEASURED_PEAKS.json)") if peaks else \
             (1590.0, "fallback bf16 1.59 PF")
+    traffic = _profiled_traffic("gemm_fp8_ff1_medium.md") if (lin.fp8 and M == 16494) else None
     roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "peak_source": peak_src, "traffic": None,
+                "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                "traffic_source": "profiles/gemm_fp8_ff1_medium.md (ncu dram read+write bytes, one launch)"
+                if traffic else None,
                 "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
 
     if rank == 0:
