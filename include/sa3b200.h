@@ -147,9 +147,10 @@ int sa3_permute_cols(const void* x, const int* perm, void* out, int rows, int K,
  * (cross_attend_norm, transformer.py:1033); otherwise scale of batch b is
  * mod + b*ld_mod + scale_off and shift is mod + b*ld_mod + shift_off (fp32).
  * gamma: fp32 [D] or NULL.
- * mode SA3_NORM_WRITE writes y as out_dtype (BF16 or E4M3; E4M3 divides by
- *   s = max(*quant_amax, 1e-12) / 448 first and saturates, and, if scale_out
- *   is non-NULL, stores s there for the consuming GEMM's a_scale).
+ * mode SA3_NORM_WRITE writes y as out_dtype (BF16 or E4M3; E4M3 multiplies by
+ *   r = 448 / max(*quant_amax, 1e-12) first and saturates, and, if scale_out
+ *   is non-NULL, stores s = max(*quant_amax, 1e-12) / 448 there for the
+ *   consuming GEMM's a_scale).
  * mode SA3_NORM_AMAX writes nothing and atomically maxes |y| into *amax_out.
  * x is bf16 or fp32 (x_dtype) [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
  */
@@ -161,8 +162,8 @@ int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D,
                          int rows_per_batch, const int* row_batch, int mode, int out_dtype,
                          const float* quant_amax, float* scale_out, float* amax_out, void* stream);
 
-/* Per-tensor dynamic FP8 quantisation: out = e4m3(x / s), s = max(*amax,1e-12)/448,
- * s also stored to *scale_out when non-NULL. If amax_out is non-NULL, the
+/* Per-tensor dynamic FP8 quantisation: out = e4m3(x * r), r = 448/max(*amax,1e-12);
+ * the dequantisation scale s = max(*amax,1e-12)/448 is stored to *scale_out when non-NULL. If amax_out is non-NULL, the
  * kernel only computes max|x| into it (no write). x is bf16. */
 int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, long long ldx, long long ldo,
                       const float* amax, float* scale_out, float* amax_out, void* stream);
@@ -227,7 +228,7 @@ int sa3_attention(const void* q, const void* k, const void* v, const void* q2, c
  * fixed device-memory budget that cannot risk the implicit device
  * synchronisation of cudaMalloc mid-stream.
  *
- * out[M, N] (bf16) = (e4m3(x / s_x) * s_x) . (w * w_scale[n])^T + bias[n], i.e.
+ * out[M, N] (bf16) = (e4m3(x * r_x) * s_x) . (w * w_scale[n])^T + bias[n], i.e.
  * the same FP8 linear as sa3_quantize_e4m3 (max|x| pass, quantise pass) followed
  * by sa3_gemm, but its scratch (max|x|, s_x and the M*K-byte e4m3 copy of x)
  * lives in a file-scope device array of 16 MiB, so the call allocates nothing.

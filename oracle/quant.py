@@ -8,7 +8,8 @@ for FP8, the fake-quantized activation, in fp32.
 
 FP8 (e4m3, OCP "fn" variant, finite max 448):
   weight:     s_w[n] = max(absmax(W[n, :]), 1e-12) / 448 ; Wq = e4m3(W / s_w[n])
-  activation: s_x    = max(absmax(X), 1e-12) / 448 (per tensor, dynamic) ; Xq = e4m3(X / s_x)
+  activation: s_x    = max(absmax(X), 1e-12) / 448 (per tensor, dynamic) ; Xq = e4m3(X * r_x),
+              r_x    = 448 / max(absmax(X), 1e-12)  (a reciprocal computed once, then one multiply per element)
   y = (Xq * s_x) @ (Wq * s_w)^T + bias
   Rounding is round-to-nearest-even with saturation to +-448.
 
@@ -38,6 +39,10 @@ def act_scale(x: torch.Tensor) -> torch.Tensor:
     return torch.clamp(x.abs().max(), min=1e-12) / E4M3_MAX
 
 
+def act_inv_scale(x: torch.Tensor) -> torch.Tensor:
+    return E4M3_MAX / torch.clamp(x.abs().max(), min=1e-12)
+
+
 def quantize_weight_e4m3(w: torch.Tensor):
     """Per-output-channel scale absmax/448 -> (Wq as float8_e4m3fn, s_w fp32 [N])."""
     w = w.float()
@@ -47,8 +52,7 @@ def quantize_weight_e4m3(w: torch.Tensor):
 
 
 def fake_quant_act(x: torch.Tensor) -> torch.Tensor:
-    s = act_scale(x)
-    return e4m3_round(x / s) * s
+    return e4m3_round(x * act_inv_scale(x)) * act_scale(x)
 
 
 def fp8_linear(x: torch.Tensor, wq: torch.Tensor, s_w: torch.Tensor, bias=None) -> torch.Tensor:

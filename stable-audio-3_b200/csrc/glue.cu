@@ -17,7 +17,10 @@ SA3_DEFINE_ERROR_READER(read_error_glue)
 
 constexpr float kE4M3Max = 448.f;
 
+// Dynamic per-tensor FP8 scale: s = max(amax, 1e-12) / 448 dequantises; q = e4m3(x * inv) with
+// inv = 448 / max(amax, 1e-12) quantises (one IEEE division per thread, a multiply per element).
 __device__ __forceinline__ float quant_scale(const float* amax) { return fmaxf(__ldg(amax), 1e-12f) / kE4M3Max; }
+__device__ __forceinline__ float quant_inv_scale(const float* amax) { return kE4M3Max / fmaxf(__ldg(amax), 1e-12f); }
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -36,14 +39,13 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   u.w = pack_bf16x2(v[6], v[7]);
   return u;
 }
-__device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float inv_s_div, float s) {
-  // q = e4m3(v / s): division (not a reciprocal multiply) to match the oracle.
+// q = e4m3(v * inv), saturating round-to-nearest-even (the oracle's definition).
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float inv) {
   uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) lo |= (uint32_t)f32_to_e4m3(v[j] / s) << (8 * j);
+  for (int j = 0; j < 4; ++j) lo |= (uint32_t)f32_to_e4m3(v[j] * inv) << (8 * j);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) hi |= (uint32_t)f32_to_e4m3(v[4 + j] / s) << (8 * j);
-  (void)inv_s_div;
+  for (int j = 0; j < 4; ++j) hi |= (uint32_t)f32_to_e4m3(v[4 + j] * inv) << (8 * j);
   return make_uint2(lo, hi);
 }
 
@@ -129,8 +131,8 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   const int nchunk = p.D / 8;
   float s = 1.f;
   if (p.mode == SA3_NORM_WRITE && p.out_dtype == SA3_DT_E4M3) {
-    s = quant_scale(p.quant_amax);
-    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
+    s = quant_inv_scale(p.quant_amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
   }
   float amax = 0.f;
   const int stride = gridDim.x * (blockDim.x >> 5);
@@ -188,7 +190,7 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
           for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
         } else if (p.out_dtype == SA3_DT_E4M3) {
           uint8_t* o = reinterpret_cast<uint8_t*>(p.out) + (long long)row * p.ldo + c * 8;
-          *reinterpret_cast<uint2*>(o) = pack8_e4m3(y, 0.f, s);
+          *reinterpret_cast<uint2*>(o) = pack8_e4m3(y, s);
         } else {
           __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + c * 8;
           *reinterpret_cast<uint4*>(o) = pack8(y);
@@ -206,6 +208,135 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
 
+// Bulk-copy variant: warp 4 (lane 0) streams whole rows into an NORM_RING-deep shared-memory ring
+// with cp.async.bulk (one mbarrier per slot); warps 0..3 each normalise one row at a time from
+// shared memory. Up to NORM_RING rows per block are in flight independently of the consumers.
+constexpr int NORM_RING = 8;
+constexpr int NORM_BULK_THREADS = 160;
+
+template <int MAXC, bool VEC>
+__global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormParams p, int rowbytes) {
+  extern __shared__ __align__(16) uint8_t nsm[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(nsm + NORM_RING * rowbytes);
+  uint64_t* empty = full + NORM_RING;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NORM_RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunk = p.D / 8;
+  // rows of this block: blockIdx.x + i * gridDim.x
+  const int nrows = p.rows > (int)blockIdx.x ? (p.rows - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NORM_RING; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  float s = 1.f;
+  if (p.mode == SA3_NORM_WRITE && p.out_dtype == SA3_DT_E4M3) {
+    s = quant_inv_scale(p.quant_amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
+  }
+  float amax = 0.f;
+  if (warp == 4) {
+    if (lane == 0) {
+      int li = 0;
+      for (; li < nrows; ++li) {
+        const int slot = li % NORM_RING;
+        if (li >= NORM_RING && !mbar_wait(&empty[slot], ((li / NORM_RING) - 1) & 1, abort_flag, 60)) break;
+        const int row = blockIdx.x + li * gridDim.x;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x) + (long long)row * p.ldx * (p.x_f32 ? 4 : 2);
+        mbar_arrive_expect_tx(&full[slot], rowbytes);
+        bulk_load(nsm + slot * rowbytes, src, rowbytes, &full[slot]);
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        for (int j = (li > NORM_RING ? li - NORM_RING : 0); j < li; ++j)
+          mbar_wait(&full[j % NORM_RING], (j / NORM_RING) & 1, &never, 61);
+      }
+    }
+  } else {
+    for (int li = warp; li < nrows; li += 4) {
+      const int slot = li % NORM_RING;
+      if (!mbar_wait(&full[slot], (li / NORM_RING) & 1, abort_flag, 62)) break;
+      const int row = blockIdx.x + li * gridDim.x;
+      const uint8_t* rb = nsm + slot * rowbytes;
+      float v[MAXC][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = lane + i * 32;
+        if (c < nchunk) {
+          if (p.x_f32) {
+            const float4 a = reinterpret_cast<const float4*>(rb)[2 * c];
+            const float4 b = reinterpret_cast<const float4*>(rb)[2 * c + 1];
+            v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+            v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+          } else {
+            unpack8(reinterpret_cast<const uint4*>(rb)[c], v[i]);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // the row is in registers: the slot may refill
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / (float)p.D + p.eps);
+      const float* msc = nullptr;
+      const float* msh = nullptr;
+      if (p.mod) {
+        const int b = p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch;
+        msc = p.mod + (long long)b * p.ld_mod + p.scale_off;
+        msh = p.mod + (long long)b * p.ld_mod + p.shift_off;
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = lane + i * 32;
+        if (c < nchunk) {
+          float y[8], gm[8], sc[8], sh[8];
+          if (VEC) {
+            if (p.gamma) ld8f(p.gamma + c * 8, gm);
+            if (msc) {
+              ld8f(msc + c * 8, sc);
+              ld8f(msh + c * 8, sh);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              gm[j] = p.gamma ? __ldg(p.gamma + c * 8 + j) : 1.f;
+              sc[j] = msc ? __ldg(msc + c * 8 + j) : 0.f;
+              sh[j] = msh ? __ldg(msh + c * 8 + j) : 0.f;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float t = v[i][j] * r;
+            if (p.gamma) t *= gm[j];
+            if (msc) t = fmaf(t, 1.f + sc[j], sh[j]);
+            y[j] = t;
+          }
+          if (p.mode == SA3_NORM_AMAX) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+          } else if (p.out_dtype == SA3_DT_E4M3) {
+            uint8_t* o = reinterpret_cast<uint8_t*>(p.out) + (long long)row * p.ldo + c * 8;
+            *reinterpret_cast<uint2*>(o) = pack8_e4m3(y, s);
+          } else {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + c * 8;
+            *reinterpret_cast<uint4*>(o) = pack8(y);
+          }
+        }
+      }
+    }
+  }
+  if (p.mode == SA3_NORM_AMAX) {
+    amax = warp_max(amax);
+    if (lane == 0 && warp < 4) atomic_max_nonneg(p.amax_out, amax);
+  }
+}
+
 struct QuantParams {
   const __nv_bfloat16* x;
   uint8_t* out;
@@ -221,20 +352,36 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(QuantParams p) {
   const long long total = (long long)p.rows * cpr;
   float s = 1.f;
   if (!p.amax_out) {
-    s = quant_scale(p.amax);
-    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
+    s = quant_inv_scale(p.amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.amax);
   }
   float amax = 0.f;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / cpr;
-    const int c = (int)(i - r * cpr);
-    float v[8];
-    unpack8(*reinterpret_cast<const uint4*>(p.x + r * p.ldx + c * 8), v);
-    if (p.amax_out) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  // four independent 16-byte loads in flight per thread
+  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+    uint4 u[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
-    } else {
-      *reinterpret_cast<uint2*>(p.out + r * p.ldo + c * 8) = pack8_e4m3(v, 0.f, s);
+    for (int k = 0; k < 4; ++k) {
+      const long long i = i0 + k * stride;
+      if (i < total) {
+        const long long r = i / cpr;
+        u[k] = *reinterpret_cast<const uint4*>(p.x + r * p.ldx + (i - r * cpr) * 8);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const long long i = i0 + k * stride;
+      if (i < total) {
+        float v[8];
+        unpack8(u[k], v);
+        if (p.amax_out) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        } else {
+          const long long r = i / cpr;
+          *reinterpret_cast<uint2*>(p.out + r * p.ldo + (i - r * cpr) * 8) = pack8_e4m3(v, s);
+        }
+      }
     }
   }
   if (p.amax_out) block_amax_commit(amax, p.amax_out);
@@ -416,6 +563,30 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   if (grid > 148 * 3) grid = 148 * 3;  // one wave at 3 blocks per SM
   const bool vec = aligned16(gamma) && (!mod || (aligned16(mod) && ld_mod % 4 == 0 && scale_off % 4 == 0 &&
                                                     shift_off % 4 == 0));
+  const int rowbytes = D * (x_dtype == SA3_DT_F32 ? 4 : 2);
+  if (rowbytes % 16 == 0 && rowbytes * NORM_RING <= 96 * 1024 && nchunk <= 32 * 8) {
+    // bulk-copy pipeline: one row per slot; 3 blocks of 5 warps per SM
+    const int smem = NORM_RING * rowbytes + 2 * NORM_RING * 8 + 16;
+    int gridb = rows < 148 * 3 ? rows : 148 * 3;
+#define SA3_NORM_BULK(C)                                                                             \
+  if (vec) {                                                                                         \
+    if ((rc = ensure_smem(rmsnorm_bulk_kernel<C, true>, 96 * 1024 + 256))) return rc;                \
+    rmsnorm_bulk_kernel<C, true><<<gridb, NORM_BULK_THREADS, smem, st>>>(p, rowbytes);               \
+  } else {                                                                                           \
+    if ((rc = ensure_smem(rmsnorm_bulk_kernel<C, false>, 96 * 1024 + 256))) return rc;               \
+    rmsnorm_bulk_kernel<C, false><<<gridb, NORM_BULK_THREADS, smem, st>>>(p, rowbytes);              \
+  }
+    int rc;
+    if (nchunk <= 32 * 4) {
+      SA3_NORM_BULK(4)
+    } else if (nchunk <= 32 * 6) {
+      SA3_NORM_BULK(6)
+    } else {
+      SA3_NORM_BULK(8)
+    }
+#undef SA3_NORM_BULK
+    return launch_status();
+  }
 #define SA3_NORM_LAUNCH(C)                                      \
   if (vec)                                                      \
     rmsnorm_modulate_kernel<C, true><<<grid, 128, 0, st>>>(p);  \
@@ -447,7 +618,10 @@ extern "C" int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, l
   QuantParams p{reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<uint8_t*>(out), rows, cols, ldx, ldo,
                 amax, scale_out, amax_out};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  quantize_e4m3_kernel<<<grid_for((long long)rows * (cols / 8), 256), 256, 0, st>>>(p);
+  long long qgrid = ((long long)rows * (cols / 8) + 1023) / 1024;
+  if (qgrid > 148 * 8) qgrid = 148 * 8;
+  if (qgrid < 1) qgrid = 1;
+  quantize_e4m3_kernel<<<(int)qgrid, 256, 0, st>>>(p);
   return launch_status();
 }
 
