@@ -6,6 +6,8 @@
 // _sliding_window_additive_mask :118-127), plus the differential combine
 // out - out_diff of Attention.forward (:790-795).
 //
+// Persistent: one CTA per SM walks work items (query tile fastest, so CTAs that
+// run together share K/V tiles in L2); barrier phases run on across items.
 // Work unit = 128 query rows x one head x one softmax stream. A CTA runs two
 // units side by side: the two streams of a differential head (same rows; the
 // combine o1/l1 - o2/l2 happens on chip), or two consecutive query tiles of a
@@ -35,7 +37,7 @@ constexpr int ATT_BN = 128;
 constexpr int ATT_TILE = 128 * 128;  // 128 rows x 64 16-bit elements
 constexpr int ATT_UNIT_TILES = 7;    // Q, K0, K1, V0, V1, P (2 tiles)
 constexpr int ATT_THREADS = 384;
-constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 512;
+constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 512;  // ring + 18 barriers + slots
 constexpr int ATT_TMEM_COLS = 512;
 
 struct AttnParams {
@@ -85,18 +87,22 @@ __device__ __forceinline__ uint32_t pack_2(float lo, float hi, bool f16) {
   return pack_bf16x2(lo, hi);
 }
 
+// Work item = (pair of query tiles or the two streams of one tile, head, sequence), query tile fastest.
+__device__ __forceinline__ void decode_item(const AttnParams& p, int item, int qtiles_per_item, int& b, int& h,
+                                            int& tile0) {
+  const int per_head = qtiles_per_item;
+  const int pair = item % per_head;
+  const int rest = item / per_head;
+  h = rest % p.heads;
+  b = rest / p.heads;
+  tile0 = p.diff ? pair : 2 * pair;
+}
+
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ2,
                         const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2,
-                        AttnParams p) {
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int tile0 = p.diff ? blockIdx.x : 2 * blockIdx.x;
-  Unit U[2];
-  U[0] = make_unit(p, b, tile0);
-  U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
-  if (!U[0].valid) return;  // uniform per CTA, before any barrier / TMEM use
-
+                        AttnParams p, int num_items, int items_per_head) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 #define SQ(u) (smem + ((u) * ATT_UNIT_TILES + 0) * ATT_TILE)
@@ -110,12 +116,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* s_full = bars + 10;     // [2]
   uint64_t* p_full = bars + 12;     // [2]  (4 arrivals: one per softmax warp)
   uint64_t* o_full = bars + 14;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_empty = bars + 16;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < 16; ++i) mbar_init(&bars[i], (i == 12 || i == 13) ? 4 : 1);
+    for (int i = 0; i < 18; ++i) mbar_init(&bars[i], (i == 12 || i == 13) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -135,41 +142,52 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int col = h * 64;
-  const int jmax = max(U[0].ntiles, U[1].ntiles);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int issued[2][2] = {{0, 0}, {0, 0}};
-      int q_issued[2] = {0, 0};
-      for (int u = 0; u < 2; ++u) {
-        if (U[u].ntiles == 0) continue;
-        const CUtensorMap* tq = (p.diff && u) ? &tmQ2 : &tmQ;
-        mbar_arrive_expect_tx(&q_full[u], ATT_TILE);
-        tma_load_2d(SQ(u), tq, &q_full[u], col, U[u].qs + U[u].i0);
-        q_issued[u] = 1;
-      }
-      for (int j = 0; j < jmax && !*abort_flag; ++j) {
+      int gj[2] = {0, 0};       // tiles loaded per unit
+      int qc[2] = {0, 0};       // Q tiles loaded per unit
+      for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
+        int b, h, tile0;
+        decode_item(p, item, items_per_head, b, h, tile0);
+        Unit U[2];
+        U[0] = make_unit(p, b, tile0);
+        U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
+        if (!U[0].valid) continue;
+        const int col = h * 64;
         for (int u = 0; u < 2; ++u) {
-          if (j >= U[u].ntiles) continue;
-          const int s = j & 1;
-          if (j >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((j >> 1) - 1) & 1, abort_flag, 40)) break;
-          const CUtensorMap* tk = (p.diff && u) ? &tmK2 : &tmK;
-          const CUtensorMap* tv = (p.diff && u) ? &tmV2 : &tmV;
-          const int row = U[u].ks + U[u].j_lo + j * ATT_BN;
-          mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
-          tma_load_2d(SK(u, s), tk, &kv_full[u * 2 + s], col, row);
-          tma_load_2d(SV(u, s), tv, &kv_full[u * 2 + s], col, row);
-          issued[u][s]++;
+          if (U[u].ntiles == 0) continue;
+          if (qc[u] > 0 && !mbar_wait(&q_empty[u], (qc[u] - 1) & 1, abort_flag, 40)) break;
+          const CUtensorMap* tq = (p.diff && u) ? &tmQ2 : &tmQ;
+          mbar_arrive_expect_tx(&q_full[u], ATT_TILE);
+          tma_load_2d(SQ(u), tq, &q_full[u], col, U[u].qs + U[u].i0);
+          qc[u]++;
+        }
+        const int jmax = max(U[0].ntiles, U[1].ntiles);
+        for (int j = 0; j < jmax && !*abort_flag; ++j) {
+          for (int u = 0; u < 2; ++u) {
+            if (j >= U[u].ntiles) continue;
+            const int g = gj[u];
+            const int s = g & 1;
+            if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) break;
+            const CUtensorMap* tk = (p.diff && u) ? &tmK2 : &tmK;
+            const CUtensorMap* tv = (p.diff && u) ? &tmV2 : &tmV;
+            const int row = U[u].ks + U[u].j_lo + j * ATT_BN;
+            mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
+            tma_load_2d(SK(u, s), tk, &kv_full[u * 2 + s], col, row);
+            tma_load_2d(SV(u, s), tv, &kv_full[u * 2 + s], col, row);
+            gj[u]++;
+          }
         }
       }
       if (*abort_flag) {
+        // wait (bounded, ignoring the abort flag) for the last loads this thread issued
         volatile int never = 0;
         for (int u = 0; u < 2; ++u) {
-          if (q_issued[u]) mbar_wait(&q_full[u], 0, &never, 41);
-          for (int s = 0; s < 2; ++s)
-            if (issued[u][s]) mbar_wait(&kv_full[u * 2 + s], (issued[u][s] - 1) & 1, &never, 42);
+          if (qc[u]) mbar_wait(&q_full[u], (qc[u] - 1) & 1, &never, 42);
+          for (int k = gj[u] - 2; k < gj[u]; ++k)
+            if (k >= 0) mbar_wait(&kv_full[u * 2 + (k & 1)], (k >> 1) & 1, &never, 43);
         }
       }
     }
@@ -179,49 +197,68 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int fmt = p.f16 ? 0 : 1;
       const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
       const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
+      int gj[2] = {0, 0};
+      int qc[2] = {0, 0};
       bool ok = true;
-      for (int u = 0; u < 2 && ok; ++u) {
-        if (U[u].ntiles == 0) continue;
-        ok = mbar_wait(&q_full[u], 0, abort_flag, 43) && mbar_wait(&kv_full[u * 2], 0, abort_flag, 44);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
-        const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, 0)));
-#pragma unroll
-        for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
-        tc_commit(&s_full[u]);
-      }
-      for (int j = 0; j < jmax && ok; ++j) {
-        for (int u = 0; u < 2; ++u) {
-          if (j >= U[u].ntiles) continue;
-          const int s = j & 1;
-          if (!mbar_wait(&p_full[u], j & 1, abort_flag, 45)) {
-            ok = false;
-            break;
-          }
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+        int b, h, tile0;
+        decode_item(p, item, items_per_head, b, h, tile0);
+        Unit U[2];
+        U[0] = make_unit(p, b, tile0);
+        U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
+        if (!U[0].valid) continue;
+        for (int u = 0; u < 2 && ok; ++u) {
+          if (U[u].ntiles == 0) continue;
+          const int g = gj[u];
+          ok = mbar_wait(&q_full[u], qc[u] & 1, abort_flag, 44) &&
+               mbar_wait(&kv_full[u * 2 + (g & 1)], (g >> 1) & 1, abort_flag, 45);
+          qc[u]++;
+          if (!ok) break;
           tc_fence_after();
+          const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+          const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, g & 1)));
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint64_t pd = sdesc_kmajor_sw128(smem_u32(SP(u) + (k >> 2) * ATT_TILE)) + 2 * (k & 3);
-            const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(SV(u, s)) + k * 2048, ATT_TILE);
-            mma_f16_ss(tmem + 256 + 64 * u, pd, vd, idesc_o, k != 0);
-          }
-          tc_commit(&o_full[u]);
-          tc_commit(&kv_empty[u * 2 + s]);
-          if (j + 1 < U[u].ntiles) {
-            const int s1 = (j + 1) & 1;
-            if (!mbar_wait(&kv_full[u * 2 + s1], ((j + 1) >> 1) & 1, abort_flag, 46)) {
+          for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+          tc_commit(&s_full[u]);
+          if (U[u].ntiles == 1) tc_commit(&q_empty[u]);  // last MMA that reads Q_u of this item
+        }
+        const int jmax = max(U[0].ntiles, U[1].ntiles);
+        for (int j = 0; j < jmax && ok; ++j) {
+          for (int u = 0; u < 2; ++u) {
+            if (j >= U[u].ntiles) continue;
+            const int g = gj[u] + j;
+            const int s = g & 1;
+            if (!mbar_wait(&p_full[u], g & 1, abort_flag, 46)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
-            const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, s1)));
 #pragma unroll
-            for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
-            tc_commit(&s_full[u]);
+            for (int k = 0; k < 8; ++k) {
+              const uint64_t pd = sdesc_kmajor_sw128(smem_u32(SP(u) + (k >> 2) * ATT_TILE)) + 2 * (k & 3);
+              const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(SV(u, s)) + k * 2048, ATT_TILE);
+              mma_f16_ss(tmem + 256 + 64 * u, pd, vd, idesc_o, k != 0);
+            }
+            tc_commit(&o_full[u]);
+            tc_commit(&kv_empty[u * 2 + s]);
+            if (j + 1 < U[u].ntiles) {
+              const int s1 = (g + 1) & 1;
+              if (!mbar_wait(&kv_full[u * 2 + s1], ((g + 1) >> 1) & 1, abort_flag, 47)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+              const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, s1)));
+#pragma unroll
+              for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+              tc_commit(&s_full[u]);
+              if (j + 2 == U[u].ntiles) tc_commit(&q_empty[u]);  // the next Q_u may load behind it
+            }
           }
         }
+        gj[0] += U[0].ntiles;
+        gj[1] += U[1].ntiles;
       }
     }
   } else if (warp >= 4) {
@@ -229,144 +266,154 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int u = (warp - 4) >> 2;
     const int wq = warp & 3;  // TMEM lane quarter
     const int r = wq * 32 + lane;
-    const Unit un = u ? U[1] : U[0];
-    const int i = un.i0 + r;  // query row within its sequence
     const uint32_t t_s = tmem + ((uint32_t)(wq * 32) << 16) + 128 * u;
     const uint32_t t_o = tmem + ((uint32_t)(wq * 32) << 16) + 256 + 64 * u;
-    // visible keys of this row: [lo_j, hi_j) in sequence coordinates
-    const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
-    const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
     const float NEG_INF = -INFINITY;
-    float m_i = NEG_INF, l_i = 0.f;
-    float o[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] = 0.f;
-    bool bad = false;
     uint8_t* prow = SP(u) + r * 128;
-
-    for (int j = 0; j < un.ntiles; ++j) {
-      if (!mbar_wait(&s_full[u], j & 1, abort_flag, 47)) bad = true;
-      tc_fence_after();
-      const int j0 = un.j_lo + j * ATT_BN;
-      const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
-      // Same decision for the whole warp keeps the masked path rare: a tile is "full" for the
-      // warp when every row of the warp sees all 128 columns.
-      const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
-      const unsigned span = (unsigned)max(chi - max(clo, 0), 0);
-      const int cbeg = max(clo, 0);
-      float mx = NEG_INF;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float sv[32];
-        tmem_ld32(t_s + c * 32, sv);
-        if (full) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
-            mx = valid ? fmaxf(mx, sv[e]) : mx;
-          }
-        }
-      }
-      const float m_new = fmaxf(m_i, mx * p.scale_log2);
-      const float alpha = (m_new == NEG_INF) ? 1.f : fast_exp2(m_i - m_new);
-      const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
-      float rowsum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float sv[32];
-        tmem_ld32(t_s + c * 32, sv);
-        float pv[32];
-        if (full) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            pv[e] = fast_exp2(fmaf(sv[e], p.scale_log2, -m_use));
-            rowsum += pv[e];
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
-            pv[e] = valid ? fast_exp2(fmaf(sv[e], p.scale_log2, -m_use)) : 0.f;
-            rowsum += pv[e];
-          }
-        }
-        uint8_t* rb = prow + (c >> 1) * ATT_TILE;
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          const int ch = ((c & 1) * 4 + qd) ^ (r & 7);
-          uint4 w;
-          w.x = pack_2(pv[qd * 8 + 0], pv[qd * 8 + 1], p.f16);
-          w.y = pack_2(pv[qd * 8 + 2], pv[qd * 8 + 3], p.f16);
-          w.z = pack_2(pv[qd * 8 + 4], pv[qd * 8 + 5], p.f16);
-          w.w = pack_2(pv[qd * 8 + 6], pv[qd * 8 + 7], p.f16);
-          *reinterpret_cast<uint4*>(rb + ch * 16) = w;
-        }
-      }
-      l_i = l_i * alpha + rowsum;
-      m_i = m_new;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[u]);
-      if (!mbar_wait(&o_full[u], j & 1, abort_flag, 48)) bad = true;
-      tc_fence_after();
-      {
-        float ov[32];
-        tmem_ld32(t_o, ov);
-#pragma unroll
-        for (int d = 0; d < 32; ++d) o[d] = fmaf(o[d], alpha, ov[d]);
-        tmem_ld32(t_o + 32, ov);
-#pragma unroll
-        for (int d = 0; d < 32; ++d) o[32 + d] = fmaf(o[32 + d], alpha, ov[d]);
-      }
-      tc_fence_before();
-    }
-    const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
-#pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] *= inv_l;
-
-    bool store = i < un.lq && !bad;
-    if (p.diff) {
-      // unit 1 hands o2 / l2 to unit 0 through its (now idle) P buffer, swizzled by 16-byte chunk.
-      float* xrow = reinterpret_cast<float*>(SP(1) + r * 256);
-      if (u == 1) {
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          reinterpret_cast<float4*>(xrow)[c ^ (r & 15)] =
-              make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (u == 0) {
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float4 w = reinterpret_cast<const float4*>(xrow)[c ^ (r & 15)];
-          o[4 * c] -= w.x;
-          o[4 * c + 1] -= w.y;
-          o[4 * c + 2] -= w.z;
-          o[4 * c + 3] -= w.w;
-        }
-      }
-      store = store && u == 0;
-    }
+    int gj = 0;
     float amax = 0.f;
-    if (store && !*abort_flag) {
-      uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
+      int b, h, tile0;
+      decode_item(p, item, items_per_head, b, h, tile0);
+      const Unit u0 = make_unit(p, b, tile0);
+      if (!u0.valid) continue;
+      const Unit un = u ? make_unit(p, b, p.diff ? tile0 : tile0 + 1) : u0;
+      const int col = h * 64;
+      const int i = un.i0 + r;  // query row within its sequence
+      const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
+      const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
+      float m_i = NEG_INF, l_i = 0.f;
+      float o[64];
 #pragma unroll
-      for (int qd = 0; qd < 8; ++qd) {
-        uint4 w;
-        w.x = pack_2(o[qd * 8 + 0], o[qd * 8 + 1], p.f16);
-        w.y = pack_2(o[qd * 8 + 2], o[qd * 8 + 3], p.f16);
-        w.z = pack_2(o[qd * 8 + 4], o[qd * 8 + 5], p.f16);
-        w.w = pack_2(o[qd * 8 + 6], o[qd * 8 + 7], p.f16);
-        reinterpret_cast<uint4*>(dst)[qd] = w;
+      for (int d = 0; d < 64; ++d) o[d] = 0.f;
+      bool bad = false;
+
+      for (int j = 0; j < un.ntiles; ++j) {
+        const int g = gj + j;
+        if (!mbar_wait(&s_full[u], g & 1, abort_flag, 48)) bad = true;
+        tc_fence_after();
+        const int j0 = un.j_lo + j * ATT_BN;
+        const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
+        const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
+        const unsigned span = (unsigned)max(chi - max(clo, 0), 0);
+        const int cbeg = max(clo, 0);
+        float mx = NEG_INF;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float sv[32];
+          tmem_ld32(t_s + c * 32, sv);
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
+              mx = valid ? fmaxf(mx, sv[e]) : mx;
+            }
+          }
+        }
+        const float m_new = fmaxf(m_i, mx * p.scale_log2);
+        const float alpha = (m_new == NEG_INF) ? 1.f : fast_exp2(m_i - m_new);
+        const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
+        float rowsum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float sv[32];
+          tmem_ld32(t_s + c * 32, sv);
+          float pv[32];
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              pv[e] = fast_exp2(fmaf(sv[e], p.scale_log2, -m_use));
+              rowsum += pv[e];
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
+              pv[e] = valid ? fast_exp2(fmaf(sv[e], p.scale_log2, -m_use)) : 0.f;
+              rowsum += pv[e];
+            }
+          }
+          uint8_t* rb = prow + (c >> 1) * ATT_TILE;
+#pragma unroll
+          for (int qd = 0; qd < 4; ++qd) {
+            const int ch = ((c & 1) * 4 + qd) ^ (r & 7);
+            uint4 w;
+            w.x = pack_2(pv[qd * 8 + 0], pv[qd * 8 + 1], p.f16);
+            w.y = pack_2(pv[qd * 8 + 2], pv[qd * 8 + 3], p.f16);
+            w.z = pack_2(pv[qd * 8 + 4], pv[qd * 8 + 5], p.f16);
+            w.w = pack_2(pv[qd * 8 + 6], pv[qd * 8 + 7], p.f16);
+            *reinterpret_cast<uint4*>(rb + ch * 16) = w;
+          }
+        }
+        l_i = l_i * alpha + rowsum;
+        m_i = m_new;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[u]);
+        if (!mbar_wait(&o_full[u], g & 1, abort_flag, 49)) bad = true;
+        tc_fence_after();
+        {
+          float ov[32];
+          tmem_ld32(t_o, ov);
+#pragma unroll
+          for (int d = 0; d < 32; ++d) o[d] = fmaf(o[d], alpha, ov[d]);
+          tmem_ld32(t_o + 32, ov);
+#pragma unroll
+          for (int d = 0; d < 32; ++d) o[32 + d] = fmaf(o[32 + d], alpha, ov[d]);
+        }
+        tc_fence_before();
       }
-      if (p.amax_out) {
+      gj += un.ntiles;
+      const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
 #pragma unroll
-        for (int d = 0; d < 64; ++d)
-          amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o[d])) : __bfloat162float(__float2bfloat16(o[d]))));
+      for (int d = 0; d < 64; ++d) o[d] *= inv_l;
+
+      bool store = i < un.lq && !bad;
+      if (p.diff) {
+        // unit 1 hands o2 / l2 to unit 0 through its (now idle) P buffer, swizzled by 16-byte chunk.
+        float* xrow = reinterpret_cast<float*>(SP(1) + r * 256);
+        if (u == 1) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            reinterpret_cast<float4*>(xrow)[c ^ (r & 15)] =
+                make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (u == 0) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float4 w = reinterpret_cast<const float4*>(xrow)[c ^ (r & 15)];
+            o[4 * c] -= w.x;
+            o[4 * c + 1] -= w.y;
+            o[4 * c + 2] -= w.z;
+            o[4 * c + 3] -= w.w;
+          }
+        }
+        // unit 1 may only overwrite its P buffer (next item) after unit 0 has read the hand-over
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        store = store && u == 0;
+      }
+      if (store && !*abort_flag) {
+        uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
+#pragma unroll
+        for (int qd = 0; qd < 8; ++qd) {
+          uint4 w;
+          w.x = pack_2(o[qd * 8 + 0], o[qd * 8 + 1], p.f16);
+          w.y = pack_2(o[qd * 8 + 2], o[qd * 8 + 3], p.f16);
+          w.z = pack_2(o[qd * 8 + 4], o[qd * 8 + 5], p.f16);
+          w.w = pack_2(o[qd * 8 + 6], o[qd * 8 + 7], p.f16);
+          reinterpret_cast<uint4*>(dst)[qd] = w;
+        }
+        if (p.amax_out) {
+#pragma unroll
+          for (int d = 0; d < 64; ++d)
+            amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o[d]))
+                                           : __bfloat162float(__float2bfloat16(o[d]))));
+        }
       }
     }
     if (p.amax_out) {
@@ -444,10 +491,18 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   p.ldo = ldo;
   p.amax_out = amax_out;
   const int qtiles = (max_seqlen_q + ATT_BM - 1) / ATT_BM;
-  dim3 grid(p.diff ? qtiles : (qtiles + 1) / 2, heads, batch);
+  const int items_per_head = p.diff ? qtiles : (qtiles + 1) / 2;
+  const long long num_items = (long long)items_per_head * heads * batch;
+  if (num_items > (1LL << 30)) return SA3_ERR_UNSUPPORTED;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return SA3_ERR_LAUNCH;
+  const int grid = num_items < sms ? (int)num_items : sms;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
-  attention_tc_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p);
+  attention_tc_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
+                                                            items_per_head);
   return launch_status();
 }
 
