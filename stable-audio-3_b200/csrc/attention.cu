@@ -12,20 +12,23 @@
 // units side by side: the two streams of a differential head (same rows; the
 // combine o1/l1 - o2/l2 happens on chip), or two consecutive query tiles of a
 // plain head. 384 threads, warp-specialised:
-//   warp 0 (lane 0)  TMA: Q once per unit, then K and V tiles, double-buffered.
-//   warp 1 (lane 0)  tcgen05.mma: S_u = Q_u K^T (M=128, N=128, K=64) into TMEM
-//                    columns [128u, 128u+128); O_u = P_u V (M=128, N=64, K=128)
-//                    into [256+64u, 256+64u+64).
+//   warp 0 (lane 0)  TMA: Q per unit (double-buffered across items), then K and
+//                    V tiles through a two-stage ring per unit.
+//   warp 1 (lane 0)  tcgen05.mma: S_u = Q_u K^T (M=128, N=128, K=64, both from
+//                    shared memory) and O_u += P_u V (M=128, N=64, K=128, P from
+//                    TMEM, V MN-major from its TMA tile).
 //   warps 4..7, 8..11  softmax warpgroup of unit 0 / unit 1; thread r owns query
 //                    row r (TMEM lane r). While one warpgroup runs its softmax the
 //                    tensor core works on the other unit's S and P V.
-// The key range of a unit is clipped to the window of its queries, so fully
-// masked key tiles are never loaded or multiplied; tiles that lie entirely
-// inside every row's band skip masking, edge tiles use one range test per
-// element. Online softmax in fp32 (exp2 domain); P is stored as bf16/fp16 in
-// the 128-byte-swizzled K-major layout the MMA reads, V is read MN-major
-// straight from its TMA tile; each O tile is accumulated in registers.
-// Shared memory: per unit Q 16 KB + K 2x16 KB + V 2x16 KB + P 32 KB = 112 KB.
+// TMEM per unit (256 columns): S [0,128) fp32, P [128,192) as packed 16-bit
+// pairs, O [192,256) fp32. O stays in TMEM for the whole key range; the online
+// softmax keeps a reference maximum per row and only moves it (rescaling O and
+// the row sum) when a tile's maximum exceeds it by more than 2^8, which keeps
+// every exp2 argument <= 8 and leaves the result exactly softmax(S) V. The key
+// range of a unit is clipped to the window of its queries, so fully masked key
+// tiles are never loaded or multiplied; tiles that lie entirely inside every
+// row's band skip masking, edge tiles use one range test per element.
+// Shared memory: per unit Q 2x16 KB + K 2x16 KB + V 2x16 KB = 96 KB.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -35,9 +38,10 @@ SA3_DEFINE_ERROR_READER(read_error_attention)
 constexpr int ATT_BM = 128;
 constexpr int ATT_BN = 128;
 constexpr int ATT_TILE = 128 * 128;  // 128 rows x 64 16-bit elements
-constexpr int ATT_UNIT_TILES = 7;    // Q, K0, K1, V0, V1, P (2 tiles)
+constexpr int ATT_UNIT_TILES = 6;    // Q0, Q1, K0, K1, V0, V1
 constexpr int ATT_THREADS = 384;
-constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 512;  // ring + 18 barriers + slots
+constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 1024;  // tiles + barriers, slots, row-sum exchange
+constexpr float ATT_RESCALE_LOG2 = 8.f;  // move the reference maximum only when it grows by more than this
 constexpr int ATT_TMEM_COLS = 512;
 
 struct AttnParams {
@@ -105,24 +109,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         AttnParams p, int num_items, int items_per_head) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-#define SQ(u) (smem + ((u) * ATT_UNIT_TILES + 0) * ATT_TILE)
-#define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + 1 + (s)) * ATT_TILE)
-#define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + 3 + (s)) * ATT_TILE)
-#define SP(u) (smem + ((u) * ATT_UNIT_TILES + 5) * ATT_TILE)
+#define SQ(u, b) (smem + ((u) * ATT_UNIT_TILES + (b)) * ATT_TILE)
+#define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + 2 + (s)) * ATT_TILE)
+#define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + 4 + (s)) * ATT_TILE)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE);
-  uint64_t* q_full = bars;          // [2]
-  uint64_t* kv_full = bars + 2;     // [2][2]  (unit, buffer)
-  uint64_t* kv_empty = bars + 6;    // [2][2]
-  uint64_t* s_full = bars + 10;     // [2]
-  uint64_t* p_full = bars + 12;     // [2]  (4 arrivals: one per softmax warp)
-  uint64_t* o_full = bars + 14;     // [2]
-  uint64_t* q_empty = bars + 16;    // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* q_full = bars;         // [unit][buffer]
+  uint64_t* q_empty = bars + 4;    // [unit][buffer]
+  uint64_t* kv_full = bars + 8;    // [unit][stage]
+  uint64_t* kv_empty = bars + 12;  // [unit][stage]
+  uint64_t* s_full = bars + 16;    // [unit]
+  uint64_t* p_full = bars + 18;    // [unit]  (4 arrivals: one per softmax warp)
+  uint64_t* o_full = bars + 20;    // [unit]  one phase per P V
+  uint64_t* mma_done = bars + 22;  // teardown: every MMA issued has completed
+  constexpr int NBARS = 23;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xl = reinterpret_cast<float*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE + 512);  // [128] 1/l of stream 2
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < 18; ++i) mbar_init(&bars[i], (i == 12 || i == 13) ? 4 : 1);
+    for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], (i == 18 || i == 19) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -146,9 +152,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int gj[2] = {0, 0};       // tiles loaded per unit
-      int qc[2] = {0, 0};       // Q tiles loaded per unit
-      for (int item = blockIdx.x; item < num_items && !*abort_flag; item += gridDim.x) {
+      int gj[2] = {0, 0};  // K/V tiles loaded per unit
+      int qc[2] = {0, 0};  // Q tiles loaded per unit
+      bool ok = true;
+      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
         int b, h, tile0;
         decode_item(p, item, items_per_head, b, h, tile0);
         Unit U[2];
@@ -156,21 +163,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
         if (!U[0].valid) continue;
         const int col = h * 64;
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < 2 && ok; ++u) {
           if (U[u].ntiles == 0) continue;
-          if (qc[u] > 0 && !mbar_wait(&q_empty[u], (qc[u] - 1) & 1, abort_flag, 40)) break;
+          const int c = qc[u], qb = c & 1;
+          if (c >= 2 && !mbar_wait(&q_empty[u * 2 + qb], ((c >> 1) - 1) & 1, abort_flag, 40)) {
+            ok = false;
+            break;
+          }
           const CUtensorMap* tq = (p.diff && u) ? &tmQ2 : &tmQ;
-          mbar_arrive_expect_tx(&q_full[u], ATT_TILE);
-          tma_load_2d(SQ(u), tq, &q_full[u], col, U[u].qs + U[u].i0);
+          mbar_arrive_expect_tx(&q_full[u * 2 + qb], ATT_TILE);
+          tma_load_2d(SQ(u, qb), tq, &q_full[u * 2 + qb], col, U[u].qs + U[u].i0);
           qc[u]++;
         }
         const int jmax = max(U[0].ntiles, U[1].ntiles);
-        for (int j = 0; j < jmax && !*abort_flag; ++j) {
+        for (int j = 0; j < jmax && ok; ++j) {
           for (int u = 0; u < 2; ++u) {
             if (j >= U[u].ntiles) continue;
             const int g = gj[u];
             const int s = g & 1;
-            if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) break;
+            if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) {
+              ok = false;
+              break;
+            }
             const CUtensorMap* tk = (p.diff && u) ? &tmK2 : &tmK;
             const CUtensorMap* tv = (p.diff && u) ? &tmV2 : &tmV;
             const int row = U[u].ks + U[u].j_lo + j * ATT_BN;
@@ -185,7 +199,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         // wait (bounded, ignoring the abort flag) for the last loads this thread issued
         volatile int never = 0;
         for (int u = 0; u < 2; ++u) {
-          if (qc[u]) mbar_wait(&q_full[u], (qc[u] - 1) & 1, &never, 42);
+          for (int c = qc[u] - 2; c < qc[u]; ++c)
+            if (c >= 0) mbar_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, &never, 42);
           for (int k = gj[u] - 2; k < gj[u]; ++k)
             if (k >= 0) mbar_wait(&kv_full[u * 2 + (k & 1)], (k >> 1) & 1, &never, 43);
         }
@@ -209,18 +224,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!U[0].valid) continue;
         for (int u = 0; u < 2 && ok; ++u) {
           if (U[u].ntiles == 0) continue;
-          const int g = gj[u];
-          ok = mbar_wait(&q_full[u], qc[u] & 1, abort_flag, 44) &&
+          const int g = gj[u], c = qc[u], qb = c & 1;
+          ok = mbar_wait(&q_full[u * 2 + qb], (c >> 1) & 1, abort_flag, 44) &&
                mbar_wait(&kv_full[u * 2 + (g & 1)], (g >> 1) & 1, abort_flag, 45);
-          qc[u]++;
           if (!ok) break;
           tc_fence_after();
-          const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+          const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u, qb)));
           const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, g & 1)));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+          for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 256 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
           tc_commit(&s_full[u]);
-          if (U[u].ntiles == 1) tc_commit(&q_empty[u]);  // last MMA that reads Q_u of this item
+          if (U[u].ntiles == 1) tc_commit(&q_empty[u * 2 + qb]);  // last MMA that reads this Q buffer
         }
         const int jmax = max(U[0].ntiles, U[1].ntiles);
         for (int j = 0; j < jmax && ok; ++j) {
@@ -228,16 +242,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             if (j >= U[u].ntiles) continue;
             const int g = gj[u] + j;
             const int s = g & 1;
+            const int qb = qc[u] & 1;
             if (!mbar_wait(&p_full[u], g & 1, abort_flag, 46)) {
               ok = false;
               break;
             }
             tc_fence_after();
+            const uint32_t t_p = tmem + 256 * u + 128;
+            const uint32_t t_o = tmem + 256 * u + 192;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-              const uint64_t pd = sdesc_kmajor_sw128(smem_u32(SP(u) + (k >> 2) * ATT_TILE)) + 2 * (k & 3);
               const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(SV(u, s)) + k * 2048, ATT_TILE);
-              mma_f16_ss(tmem + 256 + 64 * u, pd, vd, idesc_o, k != 0);
+              mma_f16_ts(t_o, t_p + 8 * k, vd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
             }
             tc_commit(&o_full[u]);
             tc_commit(&kv_empty[u * 2 + s]);
@@ -248,30 +264,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 break;
               }
               tc_fence_after();
-              const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u)));
+              const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u, qb)));
               const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, s1)));
 #pragma unroll
-              for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 128 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
+              for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 256 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
               tc_commit(&s_full[u]);
-              if (j + 2 == U[u].ntiles) tc_commit(&q_empty[u]);  // the next Q_u may load behind it
+              if (j + 2 == U[u].ntiles) tc_commit(&q_empty[u * 2 + qb]);
             }
           }
         }
-        gj[0] += U[0].ntiles;
-        gj[1] += U[1].ntiles;
+        for (int u = 0; u < 2; ++u) {
+          if (U[u].ntiles == 0) continue;
+          gj[u] += U[u].ntiles;
+          qc[u]++;
+        }
       }
+      // TMEM is released after the final __syncthreads: make sure no MMA is still running then.
+      tc_commit(mma_done);
+      volatile int never = 0;
+      mbar_wait(mma_done, 0, &never, 39);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ softmax warpgroups
     const int u = (warp - 4) >> 2;
     const int wq = warp & 3;  // TMEM lane quarter
     const int r = wq * 32 + lane;
-    const uint32_t t_s = tmem + ((uint32_t)(wq * 32) << 16) + 128 * u;
-    const uint32_t t_o = tmem + ((uint32_t)(wq * 32) << 16) + 256 + 64 * u;
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + 256 * u;
+    const uint32_t t_p = t_s + 128;
+    const uint32_t t_o = t_s + 192;
     const float NEG_INF = -INFINITY;
-    uint8_t* prow = SP(u) + r * 128;
     int gj = 0;
     float amax = 0.f;
+    bool release_pending = false;  // unit 1 (differential): unit 0 still has to read this unit's O
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       int b, h, tile0;
       decode_item(p, item, items_per_head, b, h, tile0);
@@ -282,10 +307,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int i = un.i0 + r;  // query row within its sequence
       const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
       const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
-      float m_i = NEG_INF, l_i = 0.f;
-      float o[64];
-#pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] = 0.f;
+      float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
       bool bad = false;
 
       for (int j = 0; j < un.ntiles; ++j) {
@@ -300,104 +322,137 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         float mx = NEG_INF;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          float sv[32];
-          tmem_ld32(t_s + c * 32, sv);
+          uint32_t sv[32];
+          tmem_ld32_async(t_s + c * 32, sv);
+          tmem_wait_ld();
           if (full) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, sv[e]);
+            for (int e = 0; e < 32; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
           } else {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
-              mx = valid ? fmaxf(mx, sv[e]) : mx;
+              mx = valid ? fmaxf(mx, __uint_as_float(sv[e])) : mx;
             }
           }
         }
-        const float m_new = fmaxf(m_i, mx * p.scale_log2);
-        const float alpha = (m_new == NEG_INF) ? 1.f : fast_exp2(m_i - m_new);
-        const float m_use = (m_new == NEG_INF) ? 0.f : m_new;
+        const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
+        const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
+        const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
+        l_i *= alpha;
+        // warp-uniform: some row of this warp moves a finite reference maximum
+        const bool rescale = __any_sync(0xffffffffu, move && m_i != NEG_INF) && j > 0;
+        if (rescale) {
+          // rescale O once the previous P V has landed in it
+          if (!mbar_wait(&o_full[u], (g - 1) & 1, abort_flag, 50)) bad = true;
+          tc_fence_after();
+          uint32_t ov[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32_async(t_o + 32 * c, ov);
+            tmem_wait_ld();
+            uint32_t w[16];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(ov[16 * h2 + e]) * alpha);
+              tmem_st16(t_o + 32 * c + 16 * h2, w);
+            }
+          }
+        }
+        if (move) m_i = m_tile;
+        const float m_use = m_i == NEG_INF ? 0.f : m_i;
         float rowsum = 0.f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          float sv[32];
-          tmem_ld32(t_s + c * 32, sv);
-          float pv[32];
+          uint32_t sv[32];
+          tmem_ld32_async(t_s + c * 32, sv);
+          tmem_wait_ld();
+          uint32_t w[16];
           if (full) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              pv[e] = fast_exp2(fmaf(sv[e], p.scale_log2, -m_use));
-              rowsum += pv[e];
+            for (int e = 0; e < 32; e += 2) {
+              const float p0 = fast_exp2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -m_use));
+              const float p1 = fast_exp2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -m_use));
+              rowsum += p0 + p1;
+              w[e >> 1] = pack_2(p0, p1, p.f16);
             }
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
-              pv[e] = valid ? fast_exp2(fmaf(sv[e], p.scale_log2, -m_use)) : 0.f;
-              rowsum += pv[e];
+            for (int e = 0; e < 32; e += 2) {
+              const bool v0 = (unsigned)(c * 32 + e - cbeg) < span;
+              const bool v1 = (unsigned)(c * 32 + e + 1 - cbeg) < span;
+              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -m_use)) : 0.f;
+              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -m_use)) : 0.f;
+              rowsum += p0 + p1;
+              w[e >> 1] = pack_2(p0, p1, p.f16);
             }
           }
-          uint8_t* rb = prow + (c >> 1) * ATT_TILE;
-#pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            const int ch = ((c & 1) * 4 + qd) ^ (r & 7);
-            uint4 w;
-            w.x = pack_2(pv[qd * 8 + 0], pv[qd * 8 + 1], p.f16);
-            w.y = pack_2(pv[qd * 8 + 2], pv[qd * 8 + 3], p.f16);
-            w.z = pack_2(pv[qd * 8 + 4], pv[qd * 8 + 5], p.f16);
-            w.w = pack_2(pv[qd * 8 + 6], pv[qd * 8 + 7], p.f16);
-            *reinterpret_cast<uint4*>(rb + ch * 16) = w;
-          }
+          tmem_st16(t_p + 16 * c, w);
         }
-        l_i = l_i * alpha + rowsum;
-        m_i = m_new;
-        fence_proxy_async_smem();
+        l_i += rowsum;
+        tmem_wait_st();
+        if (release_pending) {
+          // the P V this arrival enables overwrites O of stream 2, which unit 0 must have read
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          tc_fence_after();
+          release_pending = false;
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[u]);
-        if (!mbar_wait(&o_full[u], g & 1, abort_flag, 49)) bad = true;
-        tc_fence_after();
-        {
-          float ov[32];
-          tmem_ld32(t_o, ov);
-#pragma unroll
-          for (int d = 0; d < 32; ++d) o[d] = fmaf(o[d], alpha, ov[d]);
-          tmem_ld32(t_o + 32, ov);
-#pragma unroll
-          for (int d = 0; d < 32; ++d) o[32 + d] = fmaf(o[32 + d], alpha, ov[d]);
-        }
-        tc_fence_before();
       }
       gj += un.ntiles;
+      if (un.ntiles > 0 && !mbar_wait(&o_full[u], (gj - 1) & 1, abort_flag, 49)) bad = true;
       const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
-#pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] *= inv_l;
 
-      bool store = i < un.lq && !bad;
-      if (p.diff) {
-        // unit 1 hands o2 / l2 to unit 0 through its (now idle) P buffer, swizzled by 16-byte chunk.
-        float* xrow = reinterpret_cast<float*>(SP(1) + r * 256);
-        if (u == 1) {
-#pragma unroll
-          for (int c = 0; c < 16; ++c)
-            reinterpret_cast<float4*>(xrow)[c ^ (r & 15)] =
-                make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+      if (p.diff && u == 1) {
+        // hand 1/l2 to unit 0, which reads O of this stream straight from TMEM
+        if (release_pending) {
+          asm volatile("bar.sync 2, 256;" ::: "memory");
+          release_pending = false;
         }
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (u == 0) {
+        xl[r] = inv_l;
+        tc_fence_before();
+        asm volatile("bar.arrive 1, 256;" ::: "memory");
+        release_pending = true;
+        continue;
+      }
+      float o[64];
+      tc_fence_after();
+      if (un.ntiles > 0) {
+        uint32_t ov[32];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const float4 w = reinterpret_cast<const float4*>(xrow)[c ^ (r & 15)];
-            o[4 * c] -= w.x;
-            o[4 * c + 1] -= w.y;
-            o[4 * c + 2] -= w.z;
-            o[4 * c + 3] -= w.w;
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32_async(t_o + 32 * c, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l;
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < 64; ++d) o[d] = 0.f;
+      }
+      if (p.diff) {
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        tc_fence_after();
+        const float inv_l2 = xl[r];
+        if (un.ntiles > 0 && !mbar_wait(&o_full[1], (gj - 1) & 1, abort_flag, 51)) bad = true;
+        tc_fence_after();
+        if (un.ntiles > 0) {
+          uint32_t ov[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32_async(t_o + 256 + 32 * c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[32 * c + d] = fmaf(-__uint_as_float(ov[d]), inv_l2, o[32 * c + d]);
           }
         }
-        // unit 1 may only overwrite its P buffer (next item) after unit 0 has read the hand-over
-        asm volatile("bar.sync 2, 256;" ::: "memory");
-        store = store && u == 0;
+        tc_fence_before();
+        asm volatile("bar.arrive 2, 256;" ::: "memory");
       }
-      if (store && !*abort_flag) {
+      if (i < un.lq && !bad && !*abort_flag) {
         uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
 #pragma unroll
         for (int qd = 0; qd < 8; ++qd) {
@@ -416,6 +471,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
       }
     }
+    if (release_pending) asm volatile("bar.sync 2, 256;" ::: "memory");
     if (p.amax_out) {
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
@@ -429,7 +485,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #undef SQ
 #undef SK
 #undef SV
-#undef SP
 }
 
 }  // namespace sa3

@@ -242,6 +242,32 @@ def test_attention_differential(cuda):
     assert max_rel(hh(out), ref) < 1e-2
 
 
+@pytest.mark.parametrize("w,diff", [(-1, False), (256, False), (256, True)])
+def test_attention_growing_scores(cuda, w, diff):
+    """Key norms grow along the sequence, so a row's maximum score keeps rising across key tiles by far
+    more than 2^8: the kernel has to move its reference maximum and rescale O (in TMEM) mid-row."""
+    from sa3_b200 import ops
+
+    g = _gen(21)
+    B, N, H = 1, 1000, 2
+    D = H * 64
+    ramp = (0.5 + 6.0 * torch.arange(N) / N).view(N, 1)
+    q = torch.randn(B * N, D, generator=g)
+    k = torch.randn(B * N, D, generator=g) * ramp
+    v = torch.randn(B * N, D, generator=g)
+    q2 = torch.randn(B * N, D, generator=g)
+    k2 = torch.randn(B * N, D, generator=g) * ramp
+    q, k, v, q2, k2 = (t.bfloat16().to(cuda) for t in (q, k, v, q2, k2))
+    hh = lambda t: _heads(t, B, N, H)  # noqa: E731
+    if diff:
+        out = ops.attention(q, k, v, q2=q2, k2=k2, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w))
+        ref = orf.differential_attention(hh(q), hh(k), hh(v), hh(q2), hh(k2), w, w)
+    else:
+        out = ops.attention(q, k, v, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w))
+        ref = orf.attention(hh(q), hh(k), hh(v), w, w)
+    assert max_rel(hh(out), ref) < 1e-2
+
+
 def test_attention_cross_full(cuda):
     from sa3_b200 import ops
 
