@@ -43,6 +43,11 @@ constexpr int ATT_THREADS = 384;
 constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 1024;  // tiles + barriers, slots, row-sum exchange
 constexpr float ATT_RESCALE_LOG2 = 8.f;  // move the reference maximum only when it grows by more than this
 constexpr int ATT_TMEM_COLS = 512;
+constexpr int ATT_REGS_LAUNCH = 168;  // per thread at launch: 65536 / 384 rounded down to a multiple of 8
+constexpr int ATT_REGS_LOW = 64;      // TMA / MMA warpgroup after the split
+constexpr int ATT_REGS_HIGH = 216;    // each softmax warpgroup after the split
+static_assert(ATT_REGS_LOW * 128 + ATT_REGS_HIGH * 256 <= ATT_REGS_LAUNCH * ATT_THREADS,
+              "register split exceeds the block's launch allocation");
 
 struct AttnParams {
   int f16;  // 1: fp16 operands / output, 0: bf16
@@ -89,6 +94,60 @@ __device__ __forceinline__ uint32_t pack_2(float lo, float hi, bool f16) {
     return *reinterpret_cast<uint32_t*>(&h);
   }
   return pack_bf16x2(lo, hi);
+}
+
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: one instruction per two lanes of data).
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+constexpr uint32_t NEG_INF_BITS = 0xff800000u;
+
+// Edge tile: scores of columns outside [lo, hi) (chunk-relative) become -inf.
+__device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int lo, int hi) {
+  const int a = min(max(lo, 0), 32), b = min(max(hi, 0), 32);
+  const uint32_t below_b = b >= 32 ? 0xffffffffu : ((1u << b) - 1u);
+  const uint32_t below_a = a >= 32 ? 0xffffffffu : ((1u << a) - 1u);
+  const uint32_t m = below_b & ~below_a;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) s[e] = (m >> e) & 1u ? s[e] : NEG_INF_BITS;
+}
+
+// Running maxima over one chunk, eight independent chains.
+__device__ __forceinline__ void max_chunk(const uint32_t (&s)[32], float (&m)[8]) {
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+    m[t] = fmax3(fmax3(m[t], __uint_as_float(s[4 * t]), __uint_as_float(s[4 * t + 1])),
+                 __uint_as_float(s[4 * t + 2]), __uint_as_float(s[4 * t + 3]));
+}
+
+// P = exp2(s * scale - m) for one chunk as packed 16-bit pairs, row sums into four f32x2 chains.
+__device__ __forceinline__ void exp_chunk(const uint32_t (&s)[32], uint64_t scale2, uint64_t negm2,
+                                          uint64_t (&acc)[4], uint32_t (&w)[16], bool f16) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    const float2 x = f2_split(ffma2(f2(__uint_as_float(s[e]), __uint_as_float(s[e + 1])), scale2, negm2));
+    const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
+    acc[(e >> 1) & 3] = fadd2(acc[(e >> 1) & 3], f2(p0, p1));
+    w[e >> 1] = pack_2(p0, p1, f16);
+  }
 }
 
 // Work item = (pair of query tiles or the two streams of one tile, head, sequence), query tile fastest.
@@ -148,7 +207,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  // Register split: the TMA / MMA warpgroup hands registers to the softmax warpgroups, which hold a
+  // full 128-column score row. ATT_REGS_LOW * 128 + ATT_REGS_HIGH * 256 stays below the launch's
+  // 168 * 384 (static_assert below), so the increase never waits on registers that do not exist.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ATT_REGS_LOW));
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -284,7 +347,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       volatile int never = 0;
       mbar_wait(mma_done, 0, &never, 39);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ATT_REGS_HIGH));
     // ------------------------------------------------------------------ softmax warpgroups
     const int u = (warp - 4) >> 2;
     const int wq = warp & 3;  // TMEM lane quarter
@@ -317,25 +382,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int j0 = un.j_lo + j * ATT_BN;
         const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
         const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
-        const unsigned span = (unsigned)max(chi - max(clo, 0), 0);
-        const int cbeg = max(clo, 0);
-        float mx = NEG_INF;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sv[32];
-          tmem_ld32_async(t_s + c * 32, sv);
-          tmem_wait_ld();
-          if (full) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) mx = fmax3(mx, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const bool valid = (unsigned)(c * 32 + e - cbeg) < span;
-              mx = valid ? fmaxf(mx, __uint_as_float(sv[e])) : mx;
-            }
-          }
+        uint32_t sa[32], sb[32], sc[32], sd[32];
+        tmem_ld32_async(t_s, sa);
+        tmem_ld32_async(t_s + 32, sb);
+        tmem_ld32_async(t_s + 64, sc);
+        tmem_ld32_async(t_s + 96, sd);
+        tmem_wait_ld();
+        if (!full) {
+          mask_chunk(sa, clo, chi);
+          mask_chunk(sb, clo - 32, chi - 32);
+          mask_chunk(sc, clo - 64, chi - 64);
+          mask_chunk(sd, clo - 96, chi - 96);
         }
+        float mxs[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mxs[t] = NEG_INF;
+        max_chunk(sa, mxs);
+        max_chunk(sb, mxs);
+        max_chunk(sc, mxs);
+        max_chunk(sd, mxs);
+        const float mx = fmaxf(fmax3(fmax3(mxs[0], mxs[1], mxs[2]), mxs[3], mxs[4]),
+                               fmax3(mxs[5], mxs[6], mxs[7]));
         const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
         const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
         const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
@@ -362,34 +429,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         if (move) m_i = m_tile;
         const float m_use = m_i == NEG_INF ? 0.f : m_i;
-        float rowsum = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sv[32];
-          tmem_ld32_async(t_s + c * 32, sv);
-          tmem_wait_ld();
+        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
+        uint64_t acc[4] = {0, 0, 0, 0};
+        {
           uint32_t w[16];
-          if (full) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float p0 = fast_exp2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -m_use));
-              const float p1 = fast_exp2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -m_use));
-              rowsum += p0 + p1;
-              w[e >> 1] = pack_2(p0, p1, p.f16);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const bool v0 = (unsigned)(c * 32 + e - cbeg) < span;
-              const bool v1 = (unsigned)(c * 32 + e + 1 - cbeg) < span;
-              const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(sv[e]), p.scale_log2, -m_use)) : 0.f;
-              const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(sv[e + 1]), p.scale_log2, -m_use)) : 0.f;
-              rowsum += p0 + p1;
-              w[e >> 1] = pack_2(p0, p1, p.f16);
-            }
-          }
-          tmem_st16(t_p + 16 * c, w);
+          exp_chunk(sa, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p, w);
+          exp_chunk(sb, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 16, w);
+          exp_chunk(sc, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 32, w);
+          exp_chunk(sd, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 48, w);
         }
+        const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
+        const float rowsum = r01.x + r01.y;
         l_i += rowsum;
         tmem_wait_st();
         if (release_pending) {
