@@ -150,30 +150,70 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&s)[32], uint64_t scal
   }
 }
 
-// Work item = (pair of query tiles or the two streams of one tile, head, sequence), query tile fastest.
-__device__ __forceinline__ void decode_item(const AttnParams& p, int item, int qtiles_per_item, int& b, int& h,
+// tcgen05.mma / commit issued by one elected lane of a converged warp, descriptors given as (low
+// word, shared high word): the issue loop only adds constants to the low word (the start-address
+// field). Running the issue loop on the whole warp keeps its operands warp-uniform, which lets the
+// MMAs go out back to back (from a single lane in a divergent branch the 64-wide P V steps issue at
+// about 60% of the tensor rate).
+__device__ __forceinline__ void mma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+// mbar_wait on every lane of a converged warp; the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, site));
+}
+
+// Work item = (pair of consecutive query tiles, head, sequence), query tile fastest. Unit u of the
+// CTA takes query tile 2 * pair + u; a differential head runs its two streams as two passes.
+__device__ __forceinline__ void decode_item(const AttnParams& p, int item, int pairs_per_head, int& b, int& h,
                                             int& tile0) {
-  const int per_head = qtiles_per_item;
-  const int pair = item % per_head;
-  const int rest = item / per_head;
+  const int pair = item % pairs_per_head;
+  const int rest = item / pairs_per_head;
   h = rest % p.heads;
   b = rest / p.heads;
-  tile0 = p.diff ? pair : 2 * pair;
+  tile0 = 2 * pair;
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ2,
                         const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2,
-                        AttnParams p, int num_items, int items_per_head) {
+                        AttnParams p, int num_items, int pairs_per_head) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 #define SQ(u, b) (smem + ((u) * ATT_UNIT_TILES + (b)) * ATT_TILE)
 #define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + 2 + (s)) * ATT_TILE)
 #define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + 4 + (s)) * ATT_TILE)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE);
-  uint64_t* q_full = bars;         // [unit][buffer]
-  uint64_t* q_empty = bars + 4;    // [unit][buffer]
+  uint64_t* q_full = bars;         // [unit][slot]
+  uint64_t* q_empty = bars + 4;    // [unit][slot]
   uint64_t* kv_full = bars + 8;    // [unit][stage]
   uint64_t* kv_empty = bars + 12;  // [unit][stage]
   uint64_t* s_full = bars + 16;    // [unit]
@@ -183,7 +223,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   constexpr int NBARS = 23;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* xl = reinterpret_cast<float*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE + 512);  // [128] 1/l of stream 2
+  const int npass = p.diff ? 2 : 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -209,145 +249,163 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   // Register split: the TMA / MMA warpgroup hands registers to the softmax warpgroups, which hold a
   // full 128-column score row. ATT_REGS_LOW * 128 + ATT_REGS_HIGH * 256 stays below the launch's
-  // 168 * 384 (static_assert below), so the increase never waits on registers that do not exist.
+  // 168 * 384 (static_assert above), so the increase never waits on registers that do not exist.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ATT_REGS_LOW));
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int gj[2] = {0, 0};  // K/V tiles loaded per unit
-      int qc[2] = {0, 0};  // Q tiles loaded per unit
-      bool ok = true;
-      for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-        int b, h, tile0;
-        decode_item(p, item, items_per_head, b, h, tile0);
-        Unit U[2];
-        U[0] = make_unit(p, b, tile0);
-        U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
-        if (!U[0].valid) continue;
-        const int col = h * 64;
-        for (int u = 0; u < 2 && ok; ++u) {
-          if (U[u].ntiles == 0) continue;
-          const int c = qc[u], qb = c & 1;
-          if (c >= 2 && !mbar_wait(&q_empty[u * 2 + qb], ((c >> 1) - 1) & 1, abort_flag, 40)) {
-            ok = false;
-            break;
-          }
-          const CUtensorMap* tq = (p.diff && u) ? &tmQ2 : &tmQ;
-          mbar_arrive_expect_tx(&q_full[u * 2 + qb], ATT_TILE);
-          tma_load_2d(SQ(u, qb), tq, &q_full[u * 2 + qb], col, U[u].qs + U[u].i0);
-          qc[u]++;
-        }
-        const int jmax = max(U[0].ntiles, U[1].ntiles);
-        for (int j = 0; j < jmax && ok; ++j) {
-          for (int u = 0; u < 2; ++u) {
-            if (j >= U[u].ntiles) continue;
-            const int g = gj[u];
-            const int s = g & 1;
-            if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) {
-              ok = false;
-              break;
+    if (warp == 0) {
+      // ---------------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        int gk[2] = {0, 0};  // K/V tiles loaded per unit
+        int qc[2] = {0, 0};  // Q tiles loaded per unit
+        bool ok = true;
+        for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
+          int b, h, tile0;
+          decode_item(p, item, pairs_per_head, b, h, tile0);
+          const Unit U0 = make_unit(p, b, tile0);
+          if (!U0.valid) continue;
+          const Unit U1 = make_unit(p, b, tile0 + 1);
+          const int nt[2] = {U0.ntiles, U1.valid ? U1.ntiles : 0};
+          const int T0 = npass * nt[0], T1 = npass * nt[1];
+          const int col = h * 64;
+          for (int t = 0; t < max(T0, T1) && ok; ++t) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (t >= (u ? T1 : T0) || !ok) continue;
+              const Unit& un = u ? U1 : U0;
+              const int pass = t >= nt[u];
+              const int j = t - pass * nt[u];
+              if (j == 0) {
+                const int c = qc[u], qs = c & 1;
+                if (c >= 2 && !mbar_wait(&q_empty[u * 2 + qs], ((c >> 1) - 1) & 1, abort_flag, 40)) {
+                  ok = false;
+                  continue;
+                }
+                mbar_arrive_expect_tx(&q_full[u * 2 + qs], ATT_TILE);
+                tma_load_2d(SQ(u, qs), pass ? &tmQ2 : &tmQ, &q_full[u * 2 + qs], col, un.qs + un.i0);
+                qc[u]++;
+              }
+              const int g = gk[u];
+              const int s = g & 1;
+              if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) {
+                ok = false;
+                continue;
+              }
+              const int row = un.ks + un.j_lo + j * ATT_BN;
+              mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
+              tma_load_2d(SK(u, s), pass ? &tmK2 : &tmK, &kv_full[u * 2 + s], col, row);
+              tma_load_2d(SV(u, s), pass ? &tmV2 : &tmV, &kv_full[u * 2 + s], col, row);
+              gk[u]++;
             }
-            const CUtensorMap* tk = (p.diff && u) ? &tmK2 : &tmK;
-            const CUtensorMap* tv = (p.diff && u) ? &tmV2 : &tmV;
-            const int row = U[u].ks + U[u].j_lo + j * ATT_BN;
-            mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
-            tma_load_2d(SK(u, s), tk, &kv_full[u * 2 + s], col, row);
-            tma_load_2d(SV(u, s), tv, &kv_full[u * 2 + s], col, row);
-            gj[u]++;
+          }
+        }
+        if (*abort_flag) {
+          // wait (bounded, ignoring the abort flag) for the last loads this thread issued
+          volatile int never = 0;
+          for (int u = 0; u < 2; ++u) {
+            for (int c = qc[u] - 2; c < qc[u]; ++c)
+              if (c >= 0) mbar_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, &never, 42);
+            for (int k = gk[u] - 2; k < gk[u]; ++k)
+              if (k >= 0) mbar_wait(&kv_full[u * 2 + (k & 1)], (k >> 1) & 1, &never, 43);
           }
         }
       }
-      if (*abort_flag) {
-        // wait (bounded, ignoring the abort flag) for the last loads this thread issued
-        volatile int never = 0;
-        for (int u = 0; u < 2; ++u) {
-          for (int c = qc[u] - 2; c < qc[u]; ++c)
-            if (c >= 0) mbar_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, &never, 42);
-          for (int k = gj[u] - 2; k < gj[u]; ++k)
-            if (k >= 0) mbar_wait(&kv_full[u * 2 + (k & 1)], (k >> 1) & 1, &never, 43);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer (whole warp)
       const int fmt = p.f16 ? 0 : 1;
       const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
       const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
-      int gj[2] = {0, 0};
+      // Descriptors differ only in their start-address field (low word, in 16-byte units), and every
+      // tile of the ring sits at a fixed offset, so each MMA only adds a constant to one 32-bit word.
+      // Both base words address the start of the tile area; each operand adds the 16-byte-unit offset
+      // of its own tile, taken from the same SQ / SK / SV macros that lay the tiles out.
+      const uint32_t base = smem_u32(SQ(0, 0));
+      const uint64_t dq = sdesc_kmajor_sw128(base);
+      const uint64_t dv = sdesc_mnmajor_sw128(base, ATT_TILE);
+      const uint32_t k_hi = (uint32_t)(dq >> 32), k_lo = (uint32_t)dq;
+      const uint32_t v_hi = (uint32_t)(dv >> 32), v_lo = (uint32_t)dv;
+#define OFF16(ptr) ((smem_u32(ptr) - base) >> 4)
+      int gk[2] = {0, 0};
       int qc[2] = {0, 0};
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
         int b, h, tile0;
-        decode_item(p, item, items_per_head, b, h, tile0);
-        Unit U[2];
-        U[0] = make_unit(p, b, tile0);
-        U[1] = make_unit(p, b, p.diff ? tile0 : tile0 + 1);
-        if (!U[0].valid) continue;
-        for (int u = 0; u < 2 && ok; ++u) {
-          if (U[u].ntiles == 0) continue;
-          const int g = gj[u], c = qc[u], qb = c & 1;
-          ok = mbar_wait(&q_full[u * 2 + qb], (c >> 1) & 1, abort_flag, 44) &&
-               mbar_wait(&kv_full[u * 2 + (g & 1)], (g >> 1) & 1, abort_flag, 45);
-          if (!ok) break;
-          tc_fence_after();
-          const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u, qb)));
-          const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, g & 1)));
+        decode_item(p, item, pairs_per_head, b, h, tile0);
+        const Unit U0 = make_unit(p, b, tile0);
+        if (!U0.valid) continue;
+        const Unit U1 = make_unit(p, b, tile0 + 1);
+        const int nt[2] = {U0.ntiles, U1.valid ? U1.ntiles : 0};
+        const int T[2] = {npass * nt[0], npass * nt[1]};
+        // first S of each unit: Q of pass 0, first K tile
 #pragma unroll
-          for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 256 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
-          tc_commit(&s_full[u]);
-          if (U[u].ntiles == 1) tc_commit(&q_empty[u * 2 + qb]);  // last MMA that reads this Q buffer
+        for (int u = 0; u < 2; ++u) {
+          if (T[u] == 0 || !ok) continue;
+          const int g = gk[u], c = qc[u];
+          ok = warp_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, abort_flag, 44) &&
+               warp_wait(&kv_full[u * 2 + (g & 1)], (g >> 1) & 1, abort_flag, 45);
+          if (!ok) continue;
+          tc_fence_after();
+          const uint32_t qlo = k_lo + OFF16(SQ(u, c & 1));
+          const uint32_t klo = k_lo + OFF16(SK(u, g & 1));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_ss_lo(tmem + 256 * u, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
+          commit_elect(&s_full[u]);
+          if (nt[u] == 1) commit_elect(&q_empty[u * 2 + (c & 1)]);  // last MMA that reads this Q slot
         }
-        const int jmax = max(U[0].ntiles, U[1].ntiles);
-        for (int j = 0; j < jmax && ok; ++j) {
+        for (int t = 0; t < max(T[0], T[1]) && ok; ++t) {
+#pragma unroll
           for (int u = 0; u < 2; ++u) {
-            if (j >= U[u].ntiles) continue;
-            const int g = gj[u] + j;
+            if (t >= T[u] || !ok) continue;
+            const int g = gk[u] + t;
             const int s = g & 1;
-            const int qb = qc[u] & 1;
-            if (!mbar_wait(&p_full[u], g & 1, abort_flag, 46)) {
+            const int pass = t >= nt[u];
+            const int j = t - pass * nt[u];
+            if (!warp_wait(&p_full[u], g & 1, abort_flag, 46)) {
               ok = false;
-              break;
+              continue;
             }
             tc_fence_after();
-            const uint32_t t_p = tmem + 256 * u + 128;
-            const uint32_t t_o = tmem + 256 * u + 192;
+            // O_pass (+)= P V: P is the 16-bit copy the softmax wrote over the first 64 columns of S
+            const uint32_t vlo = v_lo + OFF16(SV(u, s));
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const uint64_t vd = sdesc_mnmajor_sw128(smem_u32(SV(u, s)) + k * 2048, ATT_TILE);
-              mma_f16_ts(t_o, t_p + 8 * k, vd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-            }
-            tc_commit(&o_full[u]);
-            tc_commit(&kv_empty[u * 2 + s]);
-            if (j + 1 < U[u].ntiles) {
+            for (int k = 0; k < 8; ++k)
+              mma_ts_lo(tmem + 256 * u + 128 + 64 * pass, tmem + 256 * u + 8 * k, vlo + k * (2048 >> 4), v_hi, idesc_o,
+                        (j > 0 || k > 0) ? 1u : 0u);
+            commit_elect(&o_full[u]);
+            commit_elect(&kv_empty[u * 2 + s]);
+            if (t + 1 < T[u]) {
+              // S of the next tile overwrites the P just read: tcgen05 MMAs execute in issue order
+              const int pass1 = (t + 1) >= nt[u];
+              const int j1 = t + 1 - pass1 * nt[u];
+              const int c = qc[u] + pass1;
               const int s1 = (g + 1) & 1;
-              if (!mbar_wait(&kv_full[u * 2 + s1], ((g + 1) >> 1) & 1, abort_flag, 47)) {
+              if ((j1 == 0 && !warp_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, abort_flag, 47)) ||
+                  !warp_wait(&kv_full[u * 2 + s1], ((g + 1) >> 1) & 1, abort_flag, 48)) {
                 ok = false;
-                break;
+                continue;
               }
               tc_fence_after();
-              const uint64_t qd = sdesc_kmajor_sw128(smem_u32(SQ(u, qb)));
-              const uint64_t kd = sdesc_kmajor_sw128(smem_u32(SK(u, s1)));
+              const uint32_t qlo = k_lo + OFF16(SQ(u, c & 1));
+              const uint32_t klo = k_lo + OFF16(SK(u, s1));
 #pragma unroll
-              for (int k = 0; k < 4; ++k) mma_f16_ss(tmem + 256 * u, qd + 2 * k, kd + 2 * k, idesc_s, k != 0);
-              tc_commit(&s_full[u]);
-              if (j + 2 == U[u].ntiles) tc_commit(&q_empty[u * 2 + qb]);
+              for (int k = 0; k < 4; ++k)
+                mma_ss_lo(tmem + 256 * u, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
+              commit_elect(&s_full[u]);
+              if (j1 == nt[u] - 1) commit_elect(&q_empty[u * 2 + (c & 1)]);
             }
           }
         }
+#pragma unroll
         for (int u = 0; u < 2; ++u) {
-          if (U[u].ntiles == 0) continue;
-          gj[u] += U[u].ntiles;
-          qc[u]++;
+          if (T[u] == 0) continue;
+          gk[u] += T[u];
+          qc[u] += npass;
         }
       }
       // TMEM is released after the final __syncthreads: make sure no MMA is still running then.
-      tc_commit(mma_done);
+      commit_elect(mma_done);
       volatile int never = 0;
-      mbar_wait(mma_done, 0, &never, 39);
+      warp_wait(mma_done, 0, &never, 39);
     }
-  }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ATT_REGS_HIGH));
     // ------------------------------------------------------------------ softmax warpgroups
@@ -355,156 +413,129 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int wq = warp & 3;  // TMEM lane quarter
     const int r = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + 256 * u;
-    const uint32_t t_p = t_s + 128;
-    const uint32_t t_o = t_s + 192;
+    const uint32_t t_s = tmem + lane_off + 256 * u;  // S, then P over its first 64 columns
     const float NEG_INF = -INFINITY;
-    int gj = 0;
+    int gk = 0;
     float amax = 0.f;
-    bool release_pending = false;  // unit 1 (differential): unit 0 still has to read this unit's O
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       int b, h, tile0;
-      decode_item(p, item, items_per_head, b, h, tile0);
-      const Unit u0 = make_unit(p, b, tile0);
-      if (!u0.valid) continue;
-      const Unit un = u ? make_unit(p, b, p.diff ? tile0 : tile0 + 1) : u0;
+      decode_item(p, item, pairs_per_head, b, h, tile0);
+      const Unit un = make_unit(p, b, tile0 + u);
+      if (!un.valid) continue;
       const int col = h * 64;
       const int i = un.i0 + r;  // query row within its sequence
       const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
       const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
-      float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
+      float inv_l[2] = {0.f, 0.f};
       bool bad = false;
 
-      for (int j = 0; j < un.ntiles; ++j) {
-        const int g = gj + j;
-        if (!mbar_wait(&s_full[u], g & 1, abort_flag, 48)) bad = true;
-        tc_fence_after();
-        const int j0 = un.j_lo + j * ATT_BN;
-        const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
-        const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
-        uint32_t sa[32], sb[32], sc[32], sd[32];
-        tmem_ld32_async(t_s, sa);
-        tmem_ld32_async(t_s + 32, sb);
-        tmem_ld32_async(t_s + 64, sc);
-        tmem_ld32_async(t_s + 96, sd);
-        tmem_wait_ld();
-        if (!full) {
-          mask_chunk(sa, clo, chi);
-          mask_chunk(sb, clo - 32, chi - 32);
-          mask_chunk(sc, clo - 64, chi - 64);
-          mask_chunk(sd, clo - 96, chi - 96);
-        }
-        float mxs[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mxs[t] = NEG_INF;
-        max_chunk(sa, mxs);
-        max_chunk(sb, mxs);
-        max_chunk(sc, mxs);
-        max_chunk(sd, mxs);
-        const float mx = fmaxf(fmax3(fmax3(mxs[0], mxs[1], mxs[2]), mxs[3], mxs[4]),
-                               fmax3(mxs[5], mxs[6], mxs[7]));
-        const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
-        const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
-        const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
-        l_i *= alpha;
-        // warp-uniform: some row of this warp moves a finite reference maximum
-        const bool rescale = __any_sync(0xffffffffu, move && m_i != NEG_INF) && j > 0;
-        if (rescale) {
-          // rescale O once the previous P V has landed in it
-          if (!mbar_wait(&o_full[u], (g - 1) & 1, abort_flag, 50)) bad = true;
+      for (int pass = 0; pass < npass; ++pass) {
+        const uint32_t t_o = t_s + 128 + 64 * pass;
+        float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
+        for (int j = 0; j < un.ntiles; ++j) {
+          const int g = gk + pass * un.ntiles + j;
+          if (!mbar_wait(&s_full[u], g & 1, abort_flag, 50)) bad = true;
           tc_fence_after();
-          uint32_t ov[32];
+          const int j0 = un.j_lo + j * ATT_BN;
+          const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
+          const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
+          uint32_t sa[32], sb[32], sc[32], sd[32];
+          tmem_ld32_async(t_s, sa);
+          tmem_ld32_async(t_s + 32, sb);
+          tmem_ld32_async(t_s + 64, sc);
+          tmem_ld32_async(t_s + 96, sd);
+          tmem_wait_ld();
+          if (!full) {
+            mask_chunk(sa, clo, chi);
+            mask_chunk(sb, clo - 32, chi - 32);
+            mask_chunk(sc, clo - 64, chi - 64);
+            mask_chunk(sd, clo - 96, chi - 96);
+          }
+          float mxs[8];
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32_async(t_o + 32 * c, ov);
-            tmem_wait_ld();
-            uint32_t w[16];
+          for (int t = 0; t < 8; ++t) mxs[t] = NEG_INF;
+          max_chunk(sa, mxs);
+          max_chunk(sb, mxs);
+          max_chunk(sc, mxs);
+          max_chunk(sd, mxs);
+          const float mx = fmaxf(fmax3(fmax3(mxs[0], mxs[1], mxs[2]), mxs[3], mxs[4]),
+                                 fmax3(mxs[5], mxs[6], mxs[7]));
+          const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
+          const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
+          const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
+          l_i *= alpha;
+          // warp-uniform: some row of this warp moves a finite reference maximum
+          const bool rescale = __any_sync(0xffffffffu, move && m_i != NEG_INF) && j > 0;
+          if (rescale) {
+            // rescale O once the previous P V has landed in it
+            if (!mbar_wait(&o_full[u], (g - 1) & 1, abort_flag, 51)) bad = true;
+            tc_fence_after();
+            uint32_t ov[32];
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
+            for (int c = 0; c < 2; ++c) {
+              tmem_ld32_async(t_o + 32 * c, ov);
+              tmem_wait_ld();
+              uint32_t w[16];
 #pragma unroll
-              for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(ov[16 * h2 + e]) * alpha);
-              tmem_st16(t_o + 32 * c + 16 * h2, w);
+              for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(ov[16 * h2 + e]) * alpha);
+                tmem_st16(t_o + 32 * c + 16 * h2, w);
+              }
             }
           }
+          if (move) m_i = m_tile;
+          const float m_use = m_i == NEG_INF ? 0.f : m_i;
+          const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
+          uint64_t acc[4] = {0, 0, 0, 0};
+          {
+            uint32_t w[16];
+            exp_chunk(sa, scale2, negm2, acc, w, p.f16);
+            tmem_st16(t_s, w);
+            exp_chunk(sb, scale2, negm2, acc, w, p.f16);
+            tmem_st16(t_s + 16, w);
+            exp_chunk(sc, scale2, negm2, acc, w, p.f16);
+            tmem_st16(t_s + 32, w);
+            exp_chunk(sd, scale2, negm2, acc, w, p.f16);
+            tmem_st16(t_s + 48, w);
+          }
+          const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
+          l_i += r01.x + r01.y;
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[u]);
         }
-        if (move) m_i = m_tile;
-        const float m_use = m_i == NEG_INF ? 0.f : m_i;
-        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
-        uint64_t acc[4] = {0, 0, 0, 0};
-        {
-          uint32_t w[16];
-          exp_chunk(sa, scale2, negm2, acc, w, p.f16);
-          tmem_st16(t_p, w);
-          exp_chunk(sb, scale2, negm2, acc, w, p.f16);
-          tmem_st16(t_p + 16, w);
-          exp_chunk(sc, scale2, negm2, acc, w, p.f16);
-          tmem_st16(t_p + 32, w);
-          exp_chunk(sd, scale2, negm2, acc, w, p.f16);
-          tmem_st16(t_p + 48, w);
-        }
-        const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
-        const float rowsum = r01.x + r01.y;
-        l_i += rowsum;
-        tmem_wait_st();
-        if (release_pending) {
-          // the P V this arrival enables overwrites O of stream 2, which unit 0 must have read
-          asm volatile("bar.sync 2, 256;" ::: "memory");
-          tc_fence_after();
-          release_pending = false;
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[u]);
+        inv_l[pass] = l_i > 0.f ? 1.f / l_i : 0.f;
       }
-      gj += un.ntiles;
-      if (un.ntiles > 0 && !mbar_wait(&o_full[u], (gj - 1) & 1, abort_flag, 49)) bad = true;
-      const float inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
+      gk += npass * un.ntiles;
 
-      if (p.diff && u == 1) {
-        // hand 1/l2 to unit 0, which reads O of this stream straight from TMEM
-        if (release_pending) {
-          asm volatile("bar.sync 2, 256;" ::: "memory");
-          release_pending = false;
-        }
-        xl[r] = inv_l;
-        tc_fence_before();
-        asm volatile("bar.arrive 1, 256;" ::: "memory");
-        release_pending = true;
-        continue;
-      }
       float o[64];
-      tc_fence_after();
       if (un.ntiles > 0) {
+        if (!mbar_wait(&o_full[u], (gk - 1) & 1, abort_flag, 49)) bad = true;
+        tc_fence_after();
         uint32_t ov[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          tmem_ld32_async(t_o + 32 * c, ov);
+          tmem_ld32_async(t_s + 128 + 32 * c, ov);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l;
+          for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l[0];
         }
-      } else {
-#pragma unroll
-        for (int d = 0; d < 64; ++d) o[d] = 0.f;
-      }
-      if (p.diff) {
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        tc_fence_after();
-        const float inv_l2 = xl[r];
-        if (un.ntiles > 0 && !mbar_wait(&o_full[1], (gj - 1) & 1, abort_flag, 51)) bad = true;
-        tc_fence_after();
-        if (un.ntiles > 0) {
-          uint32_t ov[32];
+        if (p.diff) {
+          // differential combine o1 / l1 - o2 / l2 (transformer.py:790-795)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
-            tmem_ld32_async(t_o + 256 + 32 * c, ov);
+            tmem_ld32_async(t_s + 192 + 32 * c, ov);
             tmem_wait_ld();
 #pragma unroll
-            for (int d = 0; d < 32; ++d) o[32 * c + d] = fmaf(-__uint_as_float(ov[d]), inv_l2, o[32 * c + d]);
+            for (int d = 0; d < 32; ++d) o[32 * c + d] = fmaf(-__uint_as_float(ov[d]), inv_l[1], o[32 * c + d]);
           }
         }
         tc_fence_before();
-        asm volatile("bar.arrive 2, 256;" ::: "memory");
+      } else {
+#pragma unroll
+        for (int d = 0; d < 64; ++d) o[d] = 0.f;
       }
       if (i < un.lq && !bad && !*abort_flag) {
         uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
@@ -525,7 +556,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
       }
     }
-    if (release_pending) asm volatile("bar.sync 2, 256;" ::: "memory");
     if (p.amax_out) {
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
@@ -539,6 +569,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #undef SQ
 #undef SK
 #undef SV
+#undef OFF16
 }
 
 }  // namespace sa3
@@ -600,8 +631,8 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   p.ldo = ldo;
   p.amax_out = amax_out;
   const int qtiles = (max_seqlen_q + ATT_BM - 1) / ATT_BM;
-  const int items_per_head = p.diff ? qtiles : (qtiles + 1) / 2;
-  const long long num_items = (long long)items_per_head * heads * batch;
+  const int pairs_per_head = (qtiles + 1) / 2;
+  const long long num_items = (long long)pairs_per_head * heads * batch;
   if (num_items > (1LL << 30)) return SA3_ERR_UNSUPPORTED;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -611,7 +642,7 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
   attention_tc_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
-                                                            items_per_head);
+                                                            pairs_per_head);
   return launch_status();
 }
 
