@@ -6,29 +6,36 @@
 // _sliding_window_additive_mask :118-127), plus the differential combine
 // out - out_diff of Attention.forward (:790-795).
 //
-// Persistent: one CTA per SM walks work items (query tile fastest, so CTAs that
-// run together share K/V tiles in L2); barrier phases run on across items.
-// Work unit = 128 query rows x one head x one softmax stream. A CTA runs two
-// units side by side: the two streams of a differential head (same rows; the
-// combine o1/l1 - o2/l2 happens on chip), or two consecutive query tiles of a
-// plain head. 384 threads, warp-specialised:
-//   warp 0 (lane 0)  TMA: Q per unit (double-buffered across items), then K and
-//                    V tiles through a two-stage ring per unit.
-//   warp 1 (lane 0)  tcgen05.mma: S_u = Q_u K^T (M=128, N=128, K=64, both from
-//                    shared memory) and O_u += P_u V (M=128, N=64, K=128, P from
-//                    TMEM, V MN-major from its TMA tile).
+// Persistent: one CTA per SM walks work items (pairs of query tiles, query tile
+// fastest, so CTAs that run together share K/V tiles in L2); barrier phases run
+// on across items. Unit u of a CTA owns query tile 2 * pair + u (128 rows x one
+// head); a differential head runs its two softmax streams as two passes of the
+// same unit. 384 threads, warp-specialised:
+//   warps 0 / 3 (lane 0)  TMA for unit 0 / 1: Q per pass (two slots), K three
+//                    tiles and V two tiles deep, K one tile ahead of V.
+//   warps 1 / 2      tcgen05.mma for unit 0 / 1, issued by one elected lane of
+//                    the converged warp: S = Q K^T (M=128, N=128, K=64, both
+//                    from shared memory) and O (+)= P V (M=128, N=64, K=128, P
+//                    from TMEM, V MN-major straight from its TMA tile). Each
+//                    unit has its own loader and issuer, so the two units never
+//                    wait on each other.
 //   warps 4..7, 8..11  softmax warpgroup of unit 0 / unit 1; thread r owns query
-//                    row r (TMEM lane r). While one warpgroup runs its softmax the
-//                    tensor core works on the other unit's S and P V.
+//                    row r (TMEM lane r).
 // TMEM per unit (256 columns): S [0,128) fp32, P [128,192) as packed 16-bit
-// pairs, O [192,256) fp32. O stays in TMEM for the whole key range; the online
-// softmax keeps a reference maximum per row and only moves it (rescaling O and
-// the row sum) when a tile's maximum exceeds it by more than 2^8, which keeps
-// every exp2 argument <= 8 and leaves the result exactly softmax(S) V. The key
-// range of a unit is clipped to the window of its queries, so fully masked key
-// tiles are never loaded or multiplied; tiles that lie entirely inside every
-// row's band skip masking, edge tiles use one range test per element.
-// Shared memory: per unit Q 2x16 KB + K 2x16 KB + V 2x16 KB = 96 KB.
+// pairs, O [192,256) fp32. The softmax copies a whole S row into registers and
+// releases the S columns at once, so the tensor core computes S of the next key
+// tile while the exponentials of this one run; P V follows when P is written.
+// O stays in TMEM for the whole key range. The online softmax keeps a
+// reference maximum per row and only moves it (rescaling O and the row sum)
+// when a tile's maximum exceeds it by more than 2^8, which keeps every exp2
+// argument <= 8 and leaves the result exactly softmax(S) V. A differential head
+// normalises stream 1 at the end of its pass and parks it in the output rows as
+// 16-bit values (the rounding the reference applies to each attention output
+// before out - out_diff), then subtracts stream 2's result from it.
+// The key range of a unit is clipped to the window of its queries, so fully
+// masked key tiles are never loaded or multiplied; tiles that lie entirely
+// inside every row's band skip masking, edge tiles mask with a bit mask.
+// Shared memory: per unit Q 2x16 KB + K 3x16 KB + V 2x16 KB = 112 KB.
 #include "common.cuh"
 #include "host_util.h"
 
@@ -38,9 +45,10 @@ SA3_DEFINE_ERROR_READER(read_error_attention)
 constexpr int ATT_BM = 128;
 constexpr int ATT_BN = 128;
 constexpr int ATT_TILE = 128 * 128;  // 128 rows x 64 16-bit elements
-constexpr int ATT_UNIT_TILES = 6;    // Q0, Q1, K0, K1, V0, V1
+constexpr int ATT_QS = 2, ATT_KS = 3, ATT_VS = 2;         // Q slots, K stages, V stages per unit
+constexpr int ATT_UNIT_TILES = ATT_QS + ATT_KS + ATT_VS;  // 7 tiles of 16 KB
 constexpr int ATT_THREADS = 384;
-constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 1024;  // tiles + barriers, slots, row-sum exchange
+constexpr int ATT_SMEM = 2 * ATT_UNIT_TILES * ATT_TILE + 1024 + 1024;  // tiles + alignment slack + barriers
 constexpr float ATT_RESCALE_LOG2 = 8.f;  // move the reference maximum only when it grows by more than this
 constexpr int ATT_TMEM_COLS = 512;
 constexpr int ATT_REGS_LAUNCH = 168;  // per thread at launch: 65536 / 384 rounded down to a multiple of 8
@@ -209,25 +217,29 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 #define SQ(u, b) (smem + ((u) * ATT_UNIT_TILES + (b)) * ATT_TILE)
-#define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + 2 + (s)) * ATT_TILE)
-#define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + 4 + (s)) * ATT_TILE)
+#define SK(u, s) (smem + ((u) * ATT_UNIT_TILES + ATT_QS + (s)) * ATT_TILE)
+#define SV(u, s) (smem + ((u) * ATT_UNIT_TILES + ATT_QS + ATT_KS + (s)) * ATT_TILE)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * ATT_UNIT_TILES * ATT_TILE);
-  uint64_t* q_full = bars;         // [unit][slot]
-  uint64_t* q_empty = bars + 4;    // [unit][slot]
-  uint64_t* kv_full = bars + 8;    // [unit][stage]
-  uint64_t* kv_empty = bars + 12;  // [unit][stage]
-  uint64_t* s_full = bars + 16;    // [unit]
-  uint64_t* p_full = bars + 18;    // [unit]  (4 arrivals: one per softmax warp)
-  uint64_t* o_full = bars + 20;    // [unit]  one phase per P V
-  uint64_t* mma_done = bars + 22;  // teardown: every MMA issued has completed
-  constexpr int NBARS = 23;
+  uint64_t* q_full = bars;          // [unit][ATT_QS]
+  uint64_t* q_empty = bars + 4;     // [unit][ATT_QS]
+  uint64_t* k_full = bars + 8;      // [unit][ATT_KS]
+  uint64_t* k_empty = bars + 14;    // [unit][ATT_KS]
+  uint64_t* v_full = bars + 20;     // [unit][ATT_VS]
+  uint64_t* v_empty = bars + 24;    // [unit][ATT_VS]
+  uint64_t* s_full = bars + 28;     // [unit]  S of a tile is in TMEM
+  uint64_t* s_empty = bars + 30;    // [unit]  the softmax holds it in registers (4 arrivals)
+  uint64_t* p_full = bars + 32;     // [unit]  P of a tile is in TMEM (4 arrivals)
+  uint64_t* o_full = bars + 34;     // [unit]  one phase per P V
+  uint64_t* mma_done = bars + 36;   // [unit] teardown: every MMA issued has completed
+  uint64_t* turn_bar = bars + 38;   // [unit][sub-partition] exponential turn of a softmax warp
+  constexpr int NBARS = 46;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int npass = p.diff ? 2 : 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], (i == 18 || i == 19) ? 4 : 1);
+    for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], (i >= 30 && i < 34) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -252,70 +264,75 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   // 168 * 384 (static_assert above), so the increase never waits on registers that do not exist.
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(ATT_REGS_LOW));
-    if (warp == 0) {
-      // ---------------------------------------------------------------- TMA producer
+    if (warp == 0 || warp == 3) {
+      // ---------------------------------------------------------------- TMA producer of unit u
+      const int u = warp == 3;
       if (lane == 0) {
-        int gk[2] = {0, 0};  // K/V tiles loaded per unit
-        int qc[2] = {0, 0};  // Q tiles loaded per unit
+        int gk = 0, gv = 0, qc = 0;  // K, V and Q tiles loaded
         bool ok = true;
         for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
           int b, h, tile0;
           decode_item(p, item, pairs_per_head, b, h, tile0);
-          const Unit U0 = make_unit(p, b, tile0);
-          if (!U0.valid) continue;
-          const Unit U1 = make_unit(p, b, tile0 + 1);
-          const int nt[2] = {U0.ntiles, U1.valid ? U1.ntiles : 0};
-          const int T0 = npass * nt[0], T1 = npass * nt[1];
+          const Unit un = make_unit(p, b, tile0 + u);
+          if (!un.valid) continue;
+          const int nt = un.ntiles, T = npass * nt;
           const int col = h * 64;
-          for (int t = 0; t < max(T0, T1) && ok; ++t) {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              if (t >= (u ? T1 : T0) || !ok) continue;
-              const Unit& un = u ? U1 : U0;
-              const int pass = t >= nt[u];
-              const int j = t - pass * nt[u];
+          // step n loads K of tile n and V of tile n - 1 (K runs one tile ahead of V)
+          for (int n = 0; n <= T && T > 0 && ok; ++n) {
+            if (n < T) {
+              const int pass = n >= nt;
+              const int j = n - pass * nt;
               if (j == 0) {
-                const int c = qc[u], qs = c & 1;
-                if (c >= 2 && !mbar_wait(&q_empty[u * 2 + qs], ((c >> 1) - 1) & 1, abort_flag, 40)) {
+                const int qs = qc % ATT_QS;
+                if (qc >= ATT_QS && !mbar_wait(&q_empty[u * ATT_QS + qs], ((qc / ATT_QS) - 1) & 1, abort_flag, 40)) {
                   ok = false;
-                  continue;
+                  break;
                 }
-                mbar_arrive_expect_tx(&q_full[u * 2 + qs], ATT_TILE);
-                tma_load_2d(SQ(u, qs), pass ? &tmQ2 : &tmQ, &q_full[u * 2 + qs], col, un.qs + un.i0);
-                qc[u]++;
+                mbar_arrive_expect_tx(&q_full[u * ATT_QS + qs], ATT_TILE);
+                tma_load_2d(SQ(u, qs), pass ? &tmQ2 : &tmQ, &q_full[u * ATT_QS + qs], col, un.qs + un.i0);
+                qc++;
               }
-              const int g = gk[u];
-              const int s = g & 1;
-              if (g >= 2 && !mbar_wait(&kv_empty[u * 2 + s], ((g >> 1) - 1) & 1, abort_flag, 41)) {
+              const int ks = gk % ATT_KS;
+              if (gk >= ATT_KS && !mbar_wait(&k_empty[u * ATT_KS + ks], ((gk / ATT_KS) - 1) & 1, abort_flag, 41)) {
                 ok = false;
-                continue;
+                break;
               }
-              const int row = un.ks + un.j_lo + j * ATT_BN;
-              mbar_arrive_expect_tx(&kv_full[u * 2 + s], 2 * ATT_TILE);
-              tma_load_2d(SK(u, s), pass ? &tmK2 : &tmK, &kv_full[u * 2 + s], col, row);
-              tma_load_2d(SV(u, s), pass ? &tmV2 : &tmV, &kv_full[u * 2 + s], col, row);
-              gk[u]++;
+              mbar_arrive_expect_tx(&k_full[u * ATT_KS + ks], ATT_TILE);
+              tma_load_2d(SK(u, ks), pass ? &tmK2 : &tmK, &k_full[u * ATT_KS + ks], col, un.ks + un.j_lo + j * ATT_BN);
+              gk++;
+            }
+            if (n >= 1) {
+              const int t = n - 1;
+              const int pass = t >= nt;
+              const int j = t - pass * nt;
+              const int vs = gv % ATT_VS;
+              if (gv >= ATT_VS && !mbar_wait(&v_empty[u * ATT_VS + vs], ((gv / ATT_VS) - 1) & 1, abort_flag, 42)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&v_full[u * ATT_VS + vs], ATT_TILE);
+              tma_load_2d(SV(u, vs), pass ? &tmV2 : &tmV, &v_full[u * ATT_VS + vs], col, un.ks + un.j_lo + j * ATT_BN);
+              gv++;
             }
           }
         }
         if (*abort_flag) {
           // wait (bounded, ignoring the abort flag) for the last loads this thread issued
           volatile int never = 0;
-          for (int u = 0; u < 2; ++u) {
-            for (int c = qc[u] - 2; c < qc[u]; ++c)
-              if (c >= 0) mbar_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, &never, 42);
-            for (int k = gk[u] - 2; k < gk[u]; ++k)
-              if (k >= 0) mbar_wait(&kv_full[u * 2 + (k & 1)], (k >> 1) & 1, &never, 43);
-          }
+          for (int c = max(qc - ATT_QS, 0); c < qc; ++c)
+            mbar_wait(&q_full[u * ATT_QS + c % ATT_QS], (c / ATT_QS) & 1, &never, 43);
+          for (int k = max(gk - ATT_KS, 0); k < gk; ++k)
+            mbar_wait(&k_full[u * ATT_KS + k % ATT_KS], (k / ATT_KS) & 1, &never, 43);
+          for (int k = max(gv - ATT_VS, 0); k < gv; ++k)
+            mbar_wait(&v_full[u * ATT_VS + k % ATT_VS], (k / ATT_VS) & 1, &never, 43);
         }
       }
-    } else if (warp == 1) {
-      // ---------------------------------------------------------------- MMA issuer (whole warp)
+    } else {
+      // ---------------------------------------------------------------- MMA issuer of unit u (whole warp)
+      const int u = warp - 1;
       const int fmt = p.f16 ? 0 : 1;
       const uint32_t idesc_s = make_idesc(128, 128, fmt, fmt, 0, 0);
       const uint32_t idesc_o = make_idesc(128, 64, fmt, fmt, 0, 1);
-      // Descriptors differ only in their start-address field (low word, in 16-byte units), and every
-      // tile of the ring sits at a fixed offset, so each MMA only adds a constant to one 32-bit word.
       // Both base words address the start of the tile area; each operand adds the 16-byte-unit offset
       // of its own tile, taken from the same SQ / SK / SV macros that lay the tiles out.
       const uint32_t base = smem_u32(SQ(0, 0));
@@ -324,221 +341,276 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const uint32_t k_hi = (uint32_t)(dq >> 32), k_lo = (uint32_t)dq;
       const uint32_t v_hi = (uint32_t)(dv >> 32), v_lo = (uint32_t)dv;
 #define OFF16(ptr) ((smem_u32(ptr) - base) >> 4)
-      int gk[2] = {0, 0};
-      int qc[2] = {0, 0};
+      const uint32_t t_s = tmem + 256 * u, t_p = t_s + 128, t_o = t_s + 192;
+      int gt = 0, qc = 0;  // tiles and Q tiles consumed
       bool ok = true;
       for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
         int b, h, tile0;
         decode_item(p, item, pairs_per_head, b, h, tile0);
-        const Unit U0 = make_unit(p, b, tile0);
-        if (!U0.valid) continue;
-        const Unit U1 = make_unit(p, b, tile0 + 1);
-        const int nt[2] = {U0.ntiles, U1.valid ? U1.ntiles : 0};
-        const int T[2] = {npass * nt[0], npass * nt[1]};
-        // first S of each unit: Q of pass 0, first K tile
+        const Unit un = make_unit(p, b, tile0 + u);
+        if (!un.valid) continue;
+        const int nt = un.ntiles, T = npass * nt;
+        if (T == 0) continue;
+        // S of tile 0: the S columns must have been released by the last tile of the previous item
+        ok = (gt == 0 || warp_wait(&s_empty[u], (gt - 1) & 1, abort_flag, 44)) &&
+             warp_wait(&q_full[u * ATT_QS + qc % ATT_QS], (qc / ATT_QS) & 1, abort_flag, 44) &&
+             warp_wait(&k_full[u * ATT_KS + gt % ATT_KS], (gt / ATT_KS) & 1, abort_flag, 45);
+        if (!ok) break;
+        tc_fence_after();
+        {
+          const uint32_t qlo = k_lo + OFF16(SQ(u, qc % ATT_QS));
+          const uint32_t klo = k_lo + OFF16(SK(u, gt % ATT_KS));
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          if (T[u] == 0 || !ok) continue;
-          const int g = gk[u], c = qc[u];
-          ok = warp_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, abort_flag, 44) &&
-               warp_wait(&kv_full[u * 2 + (g & 1)], (g >> 1) & 1, abort_flag, 45);
-          if (!ok) continue;
-          tc_fence_after();
-          const uint32_t qlo = k_lo + OFF16(SQ(u, c & 1));
-          const uint32_t klo = k_lo + OFF16(SK(u, g & 1));
-#pragma unroll
-          for (int k = 0; k < 4; ++k) mma_ss_lo(tmem + 256 * u, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
+          for (int k = 0; k < 4; ++k) mma_ss_lo(t_s, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
           commit_elect(&s_full[u]);
-          if (nt[u] == 1) commit_elect(&q_empty[u * 2 + (c & 1)]);  // last MMA that reads this Q slot
+          commit_elect(&k_empty[u * ATT_KS + gt % ATT_KS]);
+          if (nt == 1) commit_elect(&q_empty[u * ATT_QS + qc % ATT_QS]);  // last MMA that reads this Q slot
         }
-        for (int t = 0; t < max(T[0], T[1]) && ok; ++t) {
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            if (t >= T[u] || !ok) continue;
-            const int g = gk[u] + t;
-            const int s = g & 1;
-            const int pass = t >= nt[u];
-            const int j = t - pass * nt[u];
-            if (!warp_wait(&p_full[u], g & 1, abort_flag, 46)) {
-              ok = false;
-              continue;
-            }
+        for (int t = 0; t < T && ok; ++t) {
+          const int g = gt + t;
+          if (t + 1 < T) {
+            // S of tile t + 1 as soon as the softmax holds tile t in registers
+            const int pass1 = (t + 1) >= nt;
+            const int j1 = t + 1 - pass1 * nt;
+            const int c = qc + pass1;
+            ok = warp_wait(&s_empty[u], g & 1, abort_flag, 46) &&
+                 (j1 != 0 || warp_wait(&q_full[u * ATT_QS + c % ATT_QS], (c / ATT_QS) & 1, abort_flag, 46)) &&
+                 warp_wait(&k_full[u * ATT_KS + (g + 1) % ATT_KS], ((g + 1) / ATT_KS) & 1, abort_flag, 47);
+            if (!ok) break;
             tc_fence_after();
-            // O_pass (+)= P V: P is the 16-bit copy the softmax wrote over the first 64 columns of S
-            const uint32_t vlo = v_lo + OFF16(SV(u, s));
+            const uint32_t qlo = k_lo + OFF16(SQ(u, c % ATT_QS));
+            const uint32_t klo = k_lo + OFF16(SK(u, (g + 1) % ATT_KS));
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              mma_ts_lo(tmem + 256 * u + 128 + 64 * pass, tmem + 256 * u + 8 * k, vlo + k * (2048 >> 4), v_hi, idesc_o,
-                        (j > 0 || k > 0) ? 1u : 0u);
-            commit_elect(&o_full[u]);
-            commit_elect(&kv_empty[u * 2 + s]);
-            if (t + 1 < T[u]) {
-              // S of the next tile overwrites the P just read: tcgen05 MMAs execute in issue order
-              const int pass1 = (t + 1) >= nt[u];
-              const int j1 = t + 1 - pass1 * nt[u];
-              const int c = qc[u] + pass1;
-              const int s1 = (g + 1) & 1;
-              if ((j1 == 0 && !warp_wait(&q_full[u * 2 + (c & 1)], (c >> 1) & 1, abort_flag, 47)) ||
-                  !warp_wait(&kv_full[u * 2 + s1], ((g + 1) >> 1) & 1, abort_flag, 48)) {
-                ok = false;
-                continue;
-              }
-              tc_fence_after();
-              const uint32_t qlo = k_lo + OFF16(SQ(u, c & 1));
-              const uint32_t klo = k_lo + OFF16(SK(u, s1));
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                mma_ss_lo(tmem + 256 * u, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
-              commit_elect(&s_full[u]);
-              if (j1 == nt[u] - 1) commit_elect(&q_empty[u * 2 + (c & 1)]);
-            }
+            for (int k = 0; k < 4; ++k) mma_ss_lo(t_s, qlo + 2 * k, klo + 2 * k, k_hi, idesc_s, k != 0);
+            commit_elect(&s_full[u]);
+            commit_elect(&k_empty[u * ATT_KS + (g + 1) % ATT_KS]);
+            if (j1 == nt - 1) commit_elect(&q_empty[u * ATT_QS + c % ATT_QS]);
           }
-        }
+          // P V of tile t once its P is written
+          const int pass = t >= nt;
+          const int j = t - pass * nt;
+          ok = warp_wait(&p_full[u], g & 1, abort_flag, 48) &&
+               warp_wait(&v_full[u * ATT_VS + g % ATT_VS], (g / ATT_VS) & 1, abort_flag, 48);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vlo = v_lo + OFF16(SV(u, g % ATT_VS));
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          if (T[u] == 0) continue;
-          gk[u] += T[u];
-          qc[u] += npass;
+          for (int k = 0; k < 8; ++k)
+            mma_ts_lo(t_o, t_p + 8 * k, vlo + k * (2048 >> 4), v_hi, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          commit_elect(&o_full[u]);
+          commit_elect(&v_empty[u * ATT_VS + g % ATT_VS]);
         }
+        gt += T;
+        qc += npass;
       }
-      // TMEM is released after the final __syncthreads: make sure no MMA is still running then.
-      commit_elect(mma_done);
+#undef OFF16
+      // TMEM is released after the final __syncthreads: make sure no MMA of this warp is still running.
+      commit_elect(&mma_done[u]);
       volatile int never = 0;
-      warp_wait(mma_done, 0, &never, 39);
+      warp_wait(&mma_done[u], 0, &never, 39);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(ATT_REGS_HIGH));
     // ------------------------------------------------------------------ softmax warpgroups
     const int u = (warp - 4) >> 2;
-    const int wq = warp & 3;  // TMEM lane quarter
+    const int wq = warp & 3;  // TMEM lane quarter = SM sub-partition of this warp
     const int r = wq * 32 + lane;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_s = tmem + lane_off + 256 * u;  // S, then P over its first 64 columns
+    const uint32_t t_s = tmem + lane_off + 256 * u;
+    const uint32_t t_p = t_s + 128;
+    const uint32_t t_o = t_s + 192;
     const float NEG_INF = -INFINITY;
-    int gk = 0;
+    // Exponential turns: warp wq of unit 0 and warp wq of unit 1 share one sub-partition and its
+    // MUFU; they take turns on the exp2 phase, so one warp's loads, maxima and waits run while
+    // the other's exponentials keep the MUFU busy. my_turn / next_turn of this warp.
+    uint64_t* my_turn = &turn_bar[u * 4 + wq];
+    uint64_t* next_turn = &turn_bar[(1 - u) * 4 + wq];
+    int turns = 0;
+    bool bad_turn = false;
+    auto take_turn = [&]() {
+      if (u == 1 || turns > 0) {
+        const int phase = u == 1 ? turns : turns - 1;
+        if (!mbar_wait(my_turn, phase & 1, abort_flag, 53)) bad_turn = true;
+      }
+    };
+    auto pass_turn = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(next_turn);
+      turns++;
+    };
+    int gt = 0;
     float amax = 0.f;
     for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
       int b, h, tile0;
       decode_item(p, item, pairs_per_head, b, h, tile0);
       const Unit un = make_unit(p, b, tile0 + u);
-      if (!un.valid) continue;
+      const Unit uo = make_unit(p, b, tile0 + 1 - u);
+      if (!un.valid && !uo.valid) continue;
+      const int nt = un.valid ? un.ntiles : 0;
+      const int T = npass * nt, To = npass * (uo.valid ? uo.ntiles : 0);
       const int col = h * 64;
       const int i = un.i0 + r;  // query row within its sequence
+      const bool row_ok = un.valid && i < un.lq;
+      uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
       const int lo_j = p.wl < 0 ? 0 : max(0, i + un.dlt - p.wl);
       const int hi_j = p.wr < 0 ? un.lk : min(un.lk, i + un.dlt + p.wr + 1);
-      float inv_l[2] = {0.f, 0.f};
       bool bad = false;
+      float inv_l = 0.f;
+      float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
 
-      for (int pass = 0; pass < npass; ++pass) {
-        const uint32_t t_o = t_s + 128 + 64 * pass;
-        float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
-        for (int j = 0; j < un.ntiles; ++j) {
-          const int g = gk + pass * un.ntiles + j;
-          if (!mbar_wait(&s_full[u], g & 1, abort_flag, 50)) bad = true;
-          tc_fence_after();
-          const int j0 = un.j_lo + j * ATT_BN;
-          const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
-          const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
-          uint32_t sa[32], sb[32], sc[32], sd[32];
-          tmem_ld32_async(t_s, sa);
-          tmem_ld32_async(t_s + 32, sb);
-          tmem_ld32_async(t_s + 64, sc);
-          tmem_ld32_async(t_s + 96, sd);
-          tmem_wait_ld();
-          if (!full) {
-            mask_chunk(sa, clo, chi);
-            mask_chunk(sb, clo - 32, chi - 32);
-            mask_chunk(sc, clo - 64, chi - 64);
-            mask_chunk(sd, clo - 96, chi - 96);
-          }
-          float mxs[8];
+      for (int t = 0; t < max(T, To); ++t) {
+        if (t >= T) {
+          // the other unit has more tiles in this item: keep the turn sequence in step
+          take_turn();
+          pass_turn();
+          continue;
+        }
+        const int pass = t >= nt;
+        const int j = t - pass * nt;
+        if (j == 0) {
+          m_i = NEG_INF;
+          l_i = 0.f;
+        }
+        const int g = gt + t;
+        if (!mbar_wait(&s_full[u], g & 1, abort_flag, 50)) bad = true;
+        tc_fence_after();
+        const int j0 = un.j_lo + j * ATT_BN;
+        const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
+        const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
+        uint32_t sa[32], sb[32], sc[32], sd[32];
+        tmem_ld32_async(t_s, sa);
+        tmem_ld32_async(t_s + 32, sb);
+        tmem_ld32_async(t_s + 64, sc);
+        tmem_ld32_async(t_s + 96, sd);
+        tmem_wait_ld();
+        // the S columns are free for the next tile's Q K^T
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[u]);
+        if (!full) {
+          mask_chunk(sa, clo, chi);
+          mask_chunk(sb, clo - 32, chi - 32);
+          mask_chunk(sc, clo - 64, chi - 64);
+          mask_chunk(sd, clo - 96, chi - 96);
+        }
+        float mxs[8];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) mxs[t] = NEG_INF;
-          max_chunk(sa, mxs);
-          max_chunk(sb, mxs);
-          max_chunk(sc, mxs);
-          max_chunk(sd, mxs);
-          const float mx = fmaxf(fmax3(fmax3(mxs[0], mxs[1], mxs[2]), mxs[3], mxs[4]),
-                                 fmax3(mxs[5], mxs[6], mxs[7]));
-          const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
-          const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
-          const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
-          l_i *= alpha;
-          // warp-uniform: some row of this warp moves a finite reference maximum
-          const bool rescale = __any_sync(0xffffffffu, move && m_i != NEG_INF) && j > 0;
-          if (rescale) {
-            // rescale O once the previous P V has landed in it
-            if (!mbar_wait(&o_full[u], (g - 1) & 1, abort_flag, 51)) bad = true;
-            tc_fence_after();
-            uint32_t ov[32];
+        for (int e = 0; e < 8; ++e) mxs[e] = NEG_INF;
+        max_chunk(sa, mxs);
+        max_chunk(sb, mxs);
+        max_chunk(sc, mxs);
+        max_chunk(sd, mxs);
+        const float mx = fmaxf(fmax3(fmax3(mxs[0], mxs[1], mxs[2]), mxs[3], mxs[4]),
+                               fmax3(mxs[5], mxs[6], mxs[7]));
+        const float m_tile = mx * p.scale_log2;  // -inf when no visible key in this tile
+        const bool move = m_tile > m_i + ATT_RESCALE_LOG2;
+        const float alpha = move ? fast_exp2(m_i - m_tile) : 1.f;  // 0 while m_i = -inf (O row still 0)
+        l_i *= alpha;
+        // P and O of the previous tile: P V must be done before P is overwritten or O is touched
+        if (g > 0 && !mbar_wait(&o_full[u], (g - 1) & 1, abort_flag, 51)) bad = true;
+        tc_fence_after();
+        // warp-uniform: some row of this warp moves a finite reference maximum
+        const bool rescale = __any_sync(0xffffffffu, move && m_i != NEG_INF) && j > 0;
+        if (move) m_i = m_tile;
+        const float m_use = m_i == NEG_INF ? 0.f : m_i;
+        const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
+        uint64_t acc[4] = {0, 0, 0, 0};
+        take_turn();
+        {
+          uint32_t w[16];
+          exp_chunk(sa, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p, w);
+          exp_chunk(sb, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 16, w);
+          exp_chunk(sc, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 32, w);
+          exp_chunk(sd, scale2, negm2, acc, w, p.f16);
+          tmem_st16(t_p + 48, w);
+        }
+        pass_turn();
+        const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
+        l_i += r01.x + r01.y;
+        // O work once the score registers are dead, before this tile's P V is released
+        if (pass == 1 && j == 0) {
+          // end of stream 1: normalise it and park it in the output rows (16-bit, as the
+          // reference's first attention output) until stream 2 is done
+          uint32_t ov[32];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              tmem_ld32_async(t_o + 32 * c, ov);
-              tmem_wait_ld();
-              uint32_t w[16];
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32_async(t_o + 32 * c, ov);
+            tmem_wait_ld();
+            if (row_ok && !bad) {
 #pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(ov[16 * h2 + e]) * alpha);
-                tmem_st16(t_o + 32 * c + 16 * h2, w);
+              for (int qd = 0; qd < 4; ++qd) {
+                uint4 w;
+                w.x = pack_2(__uint_as_float(ov[qd * 8 + 0]) * inv_l, __uint_as_float(ov[qd * 8 + 1]) * inv_l, p.f16);
+                w.y = pack_2(__uint_as_float(ov[qd * 8 + 2]) * inv_l, __uint_as_float(ov[qd * 8 + 3]) * inv_l, p.f16);
+                w.z = pack_2(__uint_as_float(ov[qd * 8 + 4]) * inv_l, __uint_as_float(ov[qd * 8 + 5]) * inv_l, p.f16);
+                w.w = pack_2(__uint_as_float(ov[qd * 8 + 6]) * inv_l, __uint_as_float(ov[qd * 8 + 7]) * inv_l, p.f16);
+                reinterpret_cast<uint4*>(dst)[c * 4 + qd] = w;
               }
             }
           }
-          if (move) m_i = m_tile;
-          const float m_use = m_i == NEG_INF ? 0.f : m_i;
-          const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
-          uint64_t acc[4] = {0, 0, 0, 0};
-          {
-            uint32_t w[16];
-            exp_chunk(sa, scale2, negm2, acc, w, p.f16);
-            tmem_st16(t_s, w);
-            exp_chunk(sb, scale2, negm2, acc, w, p.f16);
-            tmem_st16(t_s + 16, w);
-            exp_chunk(sc, scale2, negm2, acc, w, p.f16);
-            tmem_st16(t_s + 32, w);
-            exp_chunk(sd, scale2, negm2, acc, w, p.f16);
-            tmem_st16(t_s + 48, w);
-          }
-          const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
-          l_i += r01.x + r01.y;
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[u]);
         }
-        inv_l[pass] = l_i > 0.f ? 1.f / l_i : 0.f;
+        if (rescale) {
+          uint32_t ov[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32_async(t_o + 32 * c, ov);
+            tmem_wait_ld();
+            uint32_t w[16];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) w[e] = __float_as_uint(__uint_as_float(ov[16 * h2 + e]) * alpha);
+              tmem_st16(t_o + 32 * c + 16 * h2, w);
+            }
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[u]);
+        if (j == nt - 1) inv_l = l_i > 0.f ? 1.f / l_i : 0.f;
       }
-      gk += npass * un.ntiles;
+      gt += T;
+      if (!un.valid) continue;
 
       float o[64];
-      if (un.ntiles > 0) {
-        if (!mbar_wait(&o_full[u], (gk - 1) & 1, abort_flag, 49)) bad = true;
+      if (nt > 0) {
+        if (!mbar_wait(&o_full[u], (gt - 1) & 1, abort_flag, 52)) bad = true;
         tc_fence_after();
         uint32_t ov[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          tmem_ld32_async(t_s + 128 + 32 * c, ov);
+          tmem_ld32_async(t_o + 32 * c, ov);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l[0];
-        }
-        if (p.diff) {
-          // differential combine o1 / l1 - o2 / l2 (transformer.py:790-795)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32_async(t_s + 192 + 32 * c, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int d = 0; d < 32; ++d) o[32 * c + d] = fmaf(-__uint_as_float(ov[d]), inv_l[1], o[32 * c + d]);
-          }
+          for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l;
         }
         tc_fence_before();
+        if (p.diff && row_ok && !bad) {
+          // differential combine out - out_diff (transformer.py:790-795), stream 1 parked in dst
+#pragma unroll
+          for (int qd = 0; qd < 8; ++qd) {
+            const uint4 w = reinterpret_cast<const uint4*>(dst)[qd];
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float lo = p.f16 ? __half2float(__ushort_as_half((unsigned short)(ws[e] & 0xffffu)))
+                                     : __uint_as_float(ws[e] << 16);
+              const float hi = p.f16 ? __half2float(__ushort_as_half((unsigned short)(ws[e] >> 16)))
+                                     : __uint_as_float(ws[e] & 0xffff0000u);
+              o[qd * 8 + 2 * e] = lo - o[qd * 8 + 2 * e];
+              o[qd * 8 + 2 * e + 1] = hi - o[qd * 8 + 2 * e + 1];
+            }
+          }
+        }
       } else {
 #pragma unroll
         for (int d = 0; d < 64; ++d) o[d] = 0.f;
       }
-      if (i < un.lq && !bad && !*abort_flag) {
-        uint16_t* dst = reinterpret_cast<uint16_t*>(p.out) + (long long)(un.qs + i) * p.ldo + col;
+      if (row_ok && !bad && !bad_turn && !*abort_flag) {
 #pragma unroll
         for (int qd = 0; qd < 8; ++qd) {
           uint4 w;
@@ -569,7 +641,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #undef SQ
 #undef SK
 #undef SV
-#undef OFF16
 }
 
 }  // namespace sa3
