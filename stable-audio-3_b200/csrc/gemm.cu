@@ -336,7 +336,10 @@ __global__ void __launch_bounds__(128, 1)
 constexpr int PG_THREADS = 320;
 constexpr int PG_EPI_WARPS = 8;
 constexpr int PG_TMEM_COLS = 512;
-constexpr int PG_SMEM = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 + 256;
+// ring | barriers (256 B) | epilogue transpose scratch (8 warps x 32 x 33 floats); + 1 KB alignment slack
+constexpr int PG_SCRATCH_OFFSET = GEMM_STAGES * GEMM_STAGE_BYTES + 256;
+constexpr int PG_SMEM = PG_SCRATCH_OFFSET + PG_EPI_WARPS * 32 * 33 * 4 + 1024;
+static_assert(PG_SMEM <= 232448, "persistent GEMM exceeds the 227 KB shared-memory limit");
 
 __device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
@@ -462,13 +465,95 @@ __device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int
   }
 }
 
+// Residual epilogues into the fp32 stream, transposed through a per-warp shared-memory scratch of
+// 32 x 33 floats. TMEM hands each thread one row. In the write-back pass 8 threads cover one row's
+// 32 columns with float4 accesses, so each warp instruction moves 4 full 128-byte row segments
+// instead of 32 rows x 16 bytes. Thread t handles rows (t / 8) + 4k, k = 0..7, columns 4 (t % 8) ..
+// +3; with the 33-float pitch both the row writes and these reads are free of bank conflicts. The
+// output-row map and CFG batch of a row are computed once per tile by the lane that owns the row
+// and handed out by shuffles. C may alias the residual: each element is read before the same
+// thread writes it. Needs 16-byte aligned residual / C rows (the caller checks).
+template <int KIND>
+__device__ __forceinline__ void pg_residual_tile_t(const GemmParams& p, uint32_t tmem_tile, int m0, int n0, int q,
+                                                   int half, float sa, float& amax, float* scratch) {
+  const sa3_epilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+  const uint32_t trow = tmem_tile + ((uint32_t)(q * 32) << 16);
+  const int row0 = m0 + q * 32;
+  const int nrows = min(32, p.M - row0);  // warp-uniform
+  const float* res = reinterpret_cast<const float*>(e.residual);
+  float* out = reinterpret_cast<float*>(p.C);
+  const bool my_ok = lane < nrows;
+  const int my_orow = my_ok ? out_row_of(e, row0 + lane) : 0;
+  int my_batch = 0;
+  if (KIND == SA3_EPI_GATED_RESIDUAL && my_ok)
+    my_batch = e.row_batch ? __ldg(e.row_batch + row0 + lane) : (row0 + lane) / e.rows_per_batch;
+  const int rsub = lane >> 3, c4 = 4 * (lane & 7);
+  long long roff[8], ooff[8];
+  int bk[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int orow = __shfl_sync(0xffffffffu, my_orow, rsub + 4 * k);
+    roff[k] = (long long)orow * e.ld_residual;
+    ooff[k] = (long long)orow * p.ldc;
+    bk[k] = __shfl_sync(0xffffffffu, my_batch, rsub + 4 * k);
+  }
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    const int col = half * 128 + c * 32;
+    const int nc = n0 + col;
+    if (nc >= p.N) break;  // uniform per warp
+    float v[32];
+    tmem_ld32(trow + col, v);
+    scale_bias32(v, nc, sa, p.b_scale, e.bias);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) scratch[lane * 33 + i] = v[i];
+    __syncwarp();
+    float4 r[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (rsub + 4 * k < nrows) r[k] = *reinterpret_cast<const float4*>(res + roff[k] + nc + c4);  // may alias C
+    int cur_b = -1;
+    float4 gs = make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int rr = rsub + 4 * k;
+      if (rr < nrows) {
+        const float* sp = scratch + rr * 33 + c4;
+        float4 val = make_float4(sp[0], sp[1], sp[2], sp[3]);
+        if (KIND == SA3_EPI_GATED_RESIDUAL) {
+          if (bk[k] != cur_b) {
+            cur_b = bk[k];
+            const float4 g = __ldg(reinterpret_cast<const float4*>(e.gate + (long long)cur_b * e.ld_gate + nc + c4));
+            gs = make_float4(fast_sigmoid(1.f - g.x), fast_sigmoid(1.f - g.y), fast_sigmoid(1.f - g.z),
+                             fast_sigmoid(1.f - g.w));
+          }
+          val = make_float4(fmaf(val.x, gs.x, r[k].x), fmaf(val.y, gs.y, r[k].y), fmaf(val.z, gs.z, r[k].z),
+                            fmaf(val.w, gs.w, r[k].w));
+        } else {
+          val = make_float4(val.x + r[k].x, val.y + r[k].y, val.z + r[k].z, val.w + r[k].w);
+        }
+        *reinterpret_cast<float4*>(out + ooff[k] + nc + c4) = val;
+        if (e.amax_out) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(val.x), fabsf(val.y)), fmaxf(fabsf(val.z), fabsf(val.w))));
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // Epilogue of one 128 x 256 accumulator tile for the 32 rows of TMEM lane quarter q and column
 // half `half` (tmem_tile = the tile's first TMEM column). Shared by the FP8/bf16 and GPTQ kernels.
 template <int KIND>
 __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t tmem_tile, int m0, int n0, int q,
-                                                 int half, float sa, float& amax) {
+                                                 int half, float sa, float& amax, float* scratch = nullptr) {
   const sa3_epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
+  if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && scratch && e.c_f32 &&
+      ((reinterpret_cast<uintptr_t>(e.residual) | reinterpret_cast<uintptr_t>(p.C)) & 15) == 0 &&
+      ((e.ld_residual | p.ldc) & 3) == 0 && (KIND != SA3_EPI_GATED_RESIDUAL || ((reinterpret_cast<uintptr_t>(e.gate) & 15) == 0 && (e.ld_gate & 3) == 0))) {
+    pg_residual_tile_t<KIND>(p, tmem_tile, m0, n0, q, half, sa, amax, scratch);
+    return;
+  }
       const int m = m0 + q * 32 + lane;
       const int orow = out_row_of(e, m < p.M ? m : p.M - 1);
       int batch = 0;
@@ -619,6 +704,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // ---------------- epilogue warps
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;  // column half of the tile
+    float* epi_scratch = reinterpret_cast<float*>(smem + PG_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
     float amax = 0.f;
@@ -629,7 +715,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       tc_fence_after();
       const int m0 = (t / tiles_n) * GEMM_BM;
       const int n0 = (t % tiles_n) * GEMM_BN;
-      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax);
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);

@@ -75,6 +75,28 @@ def case(name: str, iters: int) -> dict:
                                   residual=h, gate=gate, rows_per_batch=N)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 2.0 * M * n * k / ms / 1e9}
+    if name in ("out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16"):
+        # epilogue cost: the same M x 1536 x 1536 shapes with a plain bf16 store vs the fp32 residual
+        k = 264 if name == "local1_bf16" else 1536
+        n = 1536
+        if name == "out_fp8_store":
+            a = torch.randn(M, k, device=dev).to(torch.float8_e4m3fn)
+            wq, s = _fp8_weight(n, k, dev, g)
+            wq, s = wq.to(dev), s.to(dev)
+            out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s)  # noqa: E731
+        else:
+            a = torch.randn(M, k, device=dev).bfloat16()
+            w = (torch.randn(n, k, generator=g) * 0.02).bfloat16().to(dev)
+            if name == "local2_bf16":
+                h = torch.randn(M, n, device=dev)
+                fn = lambda: ops.gemm(a, w, h, kind=_lib.EPI_RESIDUAL, residual=h)  # noqa: E731
+            else:
+                out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+                kind = _lib.EPI_SILU if name == "local1_bf16" else _lib.EPI_STORE
+                fn = lambda: ops.gemm(a, w, out, kind=kind)  # noqa: E731
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "tflops": 2.0 * M * n * k / ms / 1e9}
     if name == "attn_diff":
         qkv = torch.randn(M, 5 * D, device=dev).bfloat16()
         q, k, v, q2, k2 = (qkv[:, i * D:(i + 1) * D] for i in range(5))
@@ -125,7 +147,7 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "attn_diff", "attn_cross", "norm_fp8", "qknorm", "ff1_gptq"]
+CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "qknorm", "ff1_gptq"]
 
 
 def main():
