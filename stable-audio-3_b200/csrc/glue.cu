@@ -122,6 +122,13 @@ __device__ __forceinline__ void norm_load_row(const NormParams& p, int row, floa
   }
 }
 
+// Row visiting order. The fp32 stream was just written by a GEMM that walks its row tiles upwards,
+// so the max|y| pass visits rows from the top down (the most recently written rows are still in
+// L2), and the write pass that follows goes upwards again (the rows the max|y| pass read last).
+__device__ __forceinline__ int norm_row(const NormParams& p, int i) {
+  return p.mode == SA3_NORM_AMAX ? p.rows - 1 - i : i;
+}
+
 // One warp per row; each lane owns chunks of 8 columns at lane*8 + i*256. Warps are persistent and
 // load row r + stride before normalising row r, so two rows of every warp are in flight. VEC: gamma
 // and the modulation rows are 16-byte aligned and come in as float4 loads.
@@ -136,13 +143,14 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   }
   float amax = 0.f;
   const int stride = gridDim.x * (blockDim.x >> 5);
-  int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  int li = blockIdx.x * (blockDim.x >> 5) + warp;
   float v[MAXC][8];
-  if (row < p.rows) norm_load_row<MAXC>(p, row, v);
-  while (row < p.rows) {
-    const int nrow = row + stride;
+  if (li < p.rows) norm_load_row<MAXC>(p, norm_row(p, li), v);
+  while (li < p.rows) {
+    const int row = norm_row(p, li);
+    const int nli = li + stride;
     float nv[MAXC][8];
-    if (nrow < p.rows) norm_load_row<MAXC>(p, nrow, nv);
+    if (nli < p.rows) norm_load_row<MAXC>(p, norm_row(p, nli), nv);
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i)
@@ -197,13 +205,13 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
         }
       }
     }
-    if (nrow < p.rows) {
+    if (nli < p.rows) {
 #pragma unroll
       for (int i = 0; i < MAXC; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = nv[i][j];
     }
-    row = nrow;
+    li = nli;
   }
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
       for (; li < nrows; ++li) {
         const int slot = li % NORM_RING;
         if (li >= NORM_RING && !mbar_wait(&empty[slot], ((li / NORM_RING) - 1) & 1, abort_flag, 60)) break;
-        const int row = blockIdx.x + li * gridDim.x;
+        const int row = norm_row(p, blockIdx.x + li * gridDim.x);
         const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x) + (long long)row * p.ldx * (p.x_f32 ? 4 : 2);
         mbar_arrive_expect_tx(&full[slot], rowbytes);
         bulk_load(nsm + slot * rowbytes, src, rowbytes, &full[slot]);
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
     for (int li = warp; li < nrows; li += 4) {
       const int slot = li % NORM_RING;
       if (!mbar_wait(&full[slot], (li / NORM_RING) & 1, abort_flag, 62)) break;
-      const int row = blockIdx.x + li * gridDim.x;
+      const int row = norm_row(p, blockIdx.x + li * gridDim.x);
       const uint8_t* rb = nsm + slot * rowbytes;
       float v[MAXC][8];
       float ss = 0.f;
@@ -357,21 +365,23 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(QuantParams p) {
   }
   float amax = 0.f;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  // four independent 16-byte loads in flight per thread
-  for (long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
+  // Chunks are visited from the last row down: the producer of x (a GEMM walking its row tiles
+  // upwards, or the attention kernel) wrote the last rows last, so those are the ones still in L2.
+  // Four independent 16-byte loads in flight per thread.
+  for (long long j0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; j0 < total; j0 += 4 * stride) {
     uint4 u[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const long long i = i0 + k * stride;
-      if (i < total) {
+      const long long i = total - 1 - (j0 + k * stride);
+      if (i >= 0) {
         const long long r = i / cpr;
         u[k] = *reinterpret_cast<const uint4*>(p.x + r * p.ldx + (i - r * cpr) * 8);
       }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const long long i = i0 + k * stride;
-      if (i < total) {
+      const long long i = total - 1 - (j0 + k * stride);
+      if (i >= 0) {
         float v[8];
         unpack8(u[k], v);
         if (p.amax_out) {
