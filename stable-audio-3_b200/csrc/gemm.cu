@@ -732,6 +732,275 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, PG_TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- 2-SM persistent GEMM
+// A cluster of two CTAs (one per SM) computes 256 x 256 output tiles with tcgen05.mma.cta_group::2:
+// CTA rank r holds A rows [m0 + 128 r, +128) and B rows [n0 + 128 r, +128) of every K slice, the
+// leader (rank 0) issues M=256 N=256 MMAs that read both CTAs' shared memory, and each CTA's TMEM
+// receives its own 128 x 256 accumulator. Per SM and K slice that is half the B bytes of the
+// single-SM 128 x 256 tile, which is what lets the FP8 MMA run near its rate without exceeding the
+// shared-memory bandwidth.
+//   warp 0 (lane 0)  TMA of this CTA's A and B halves; both CTAs' copies complete on the leader's
+//                    full barrier (the leader expects the bytes of both).
+//   warp 1           leader: MMA issue (elected lane of the converged warp); commits signal the
+//                    empty / acc_full barriers of both CTAs. Both CTAs: 2-SM TMEM allocation.
+//   warps 2..9       epilogue of this CTA's 128 rows; the peer's warps report a drained
+//                    accumulator on the leader's acc_empty barrier.
+// All cluster-wide waits are bounded mbarrier waits except the two cluster barriers (after set-up
+// and before exit), which every thread of both CTAs reaches on every path.
+constexpr int P2_STAGES = 6;
+constexpr int SA3_PAIR_MIN_ROWS = 512;  // below this the single-SM kernel has enough tiles to fill the GPU
+constexpr int P2_A_BYTES = 128 * 128;  // 128 rows x 128-byte K slice
+constexpr int P2_B_BYTES = 128 * 128;  // this CTA's half of the 256 B rows
+constexpr int P2_STAGE_BYTES = P2_A_BYTES + P2_B_BYTES;
+constexpr int P2_SCRATCH_OFFSET = P2_STAGES * P2_STAGE_BYTES + 256;
+constexpr int P2_SMEM = P2_SCRATCH_OFFSET + PG_EPI_WARPS * 32 * 33 * 4 + 1024;
+static_assert(P2_SMEM <= 232448, "2-SM GEMM exceeds the 227 KB shared-memory limit");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on a barrier of the CTA
+// pair (cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+template <bool FP8>
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  if (FP8)
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on the barrier at this offset in both CTAs once the pair MMAs issued so far are done.
+__device__ __forceinline__ void commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t.reg .b16 m;\n\t"
+      "mov.b16 m, 3;\n\t"
+      "elect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ bool warp_wait_g(uint64_t* bar, uint32_t parity, volatile int* abort, int site) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, site));
+}
+
+template <bool FP8, int KIND>
+__global__ void __launch_bounds__(PG_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p,
+                     int tiles_n, int num_tiles) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P2_STAGES * P2_STAGE_BYTES);
+  uint64_t* empty = full + P2_STAGES;
+  uint64_t* acc_full = empty + P2_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2], leader only: 2 x PG_EPI_WARPS arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  constexpr int BK = FP8 ? 128 : 64;
+  const int nkb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P2_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * PG_EPI_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(PG_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+        const int m0 = (t / tiles_n) * 256 + 128 * (int)rank;
+        const int n0 = (t % tiles_n) * 256 + 128 * (int)rank;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % P2_STAGES;
+          if (it >= (uint32_t)P2_STAGES && !mbar_wait(&empty[s], ((it / P2_STAGES) - 1) & 1, abort_flag, 71)) break;
+          uint8_t* st = smem + s * P2_STAGE_BYTES;
+          const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * P2_STAGE_BYTES);
+          tma_load_2d_pair(st, &tmA, fbar, kb * BK, m0);
+          tma_load_2d_pair(st + P2_A_BYTES, &tmB, fbar, kb * BK, n0);
+        }
+      }
+      if (*abort_flag && rank == 0) {
+        // both CTAs' copies complete on the leader's barriers: wait (bounded) for the last ones
+        volatile int never = 0;
+        const uint32_t first = it > (uint32_t)P2_STAGES ? it - P2_STAGES : 0;
+        for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % P2_STAGES], (j / P2_STAGES) & 1, &never, 72);
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // the instruction descriptor takes M = 256 for the pair
+      const uint32_t idesc = make_idesc(256, 256, FP8 ? 0 : 1, FP8 ? 0 : 1, 0, 0);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++lt) {
+        const uint32_t a = lt & 1;
+        if (lt >= 2 && !warp_wait_g(&acc_empty[a], ((lt >> 1) - 1) & 1, abort_flag, 73)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + a * GEMM_BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % P2_STAGES;
+          if (!warp_wait_g(&full[s], (it / P2_STAGES) & 1, abort_flag, 74)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * P2_STAGE_BYTES);
+          const uint64_t ad = sdesc_kmajor_sw128(a_addr);
+          const uint64_t bd = sdesc_kmajor_sw128(a_addr + P2_A_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_pair<FP8>(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          commit_pair_both(&empty[s]);
+        }
+        commit_pair_both(&acc_full[a]);
+      }
+      // TMEM is released after the final cluster barrier: no MMA may still be running then
+      volatile int never = 0;
+      commit_pair_both(&acc_full[lt & 1]);
+      warp_wait_g(&acc_full[lt & 1], (lt >> 1) & 1, &never, 75);
+    }
+  } else {
+    // ---------------- epilogue warps
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    float* epi_scratch = reinterpret_cast<float*>(smem + P2_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
+    const sa3_epilogue& e = p.epi;
+    const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
+    float amax = 0.f;
+    uint32_t lt = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++lt) {
+      const uint32_t a = lt & 1;
+      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 76)) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * 256 + 128 * (int)rank;
+      const int n0 = (t % tiles_n) * 256;
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&acc_empty[a]);
+        else
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
+      }
+    }
+    if (e.amax_out) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) atomic_max_nonneg(e.amax_out, amax);
+    }
+  }
+
+  __syncwarp();  // reconverge the single-lane roles before the aligned cluster barrier
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while the other may still touch its barriers or memory
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PG_TMEM_COLS) : "memory");
+  }
+}
+
+template <bool FP8>
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int kind,
+                       cudaStream_t st) {
+  const int tiles_n = (p.N + 255) / 256;
+  const int tiles_m = (p.M + 255) / 256;
+  const int num_tiles = tiles_n * tiles_m;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 2)
+    return SA3_ERR_LAUNCH;
+  const int npairs = num_tiles < sms / 2 ? num_tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * npairs, 1, 1);
+  cfg.blockDim = dim3(PG_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P2_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int rc;
+#define SA3_P2_CASE(K)                                                                               \
+  case K:                                                                                            \
+    if ((rc = ensure_smem(gemm_pair_kernel<FP8, K>, P2_SMEM))) return rc;                            \
+    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, p, tiles_n, num_tiles) != cudaSuccess) \
+      return SA3_ERR_LAUNCH;                                                                         \
+    break;
+  switch (kind) {
+    SA3_P2_CASE(SA3_EPI_STORE)
+    SA3_P2_CASE(SA3_EPI_SILU)
+    SA3_P2_CASE(SA3_EPI_SWIGLU)
+    SA3_P2_CASE(SA3_EPI_GATED_RESIDUAL)
+    SA3_P2_CASE(SA3_EPI_RESIDUAL)
+    SA3_P2_CASE(SA3_EPI_QK_NORM)
+    default:
+      return SA3_ERR_ARG;
+  }
+#undef SA3_P2_CASE
+  return launch_status();
+}
+
 template <bool FP8>
 static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int kind,
                              cudaStream_t st) {
@@ -1068,6 +1337,12 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (res_kind) fast = fast && aligned16(e.residual) && ((e.ld_residual * celt) % 16 == 0);
   if (e.kind == SA3_EPI_GATED_RESIDUAL) fast = fast && aligned16(e.gate) && (e.ld_gate % 4 == 0);
   if (!fast && e.kind == SA3_EPI_QK_NORM) return SA3_ERR_UNSUPPORTED;  // only the persistent kernel fuses it
+  if (fast && fp8 && M >= SA3_PAIR_MIN_ROWS) {
+    // FP8 with enough rows for 256-row tiles: the 2-SM kernel. Its A and B boxes are 128 rows.
+    CUtensorMap tmB2;
+    if ((rc = make_tmap_2d(&tmB2, B, dt, esz, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, bk, 128))) return rc;
+    return launch_pair<true>(tmA, tmB2, p, e.kind, st);
+  }
   if (fast) return fp8 ? launch_persistent<true>(tmA, tmB, p, e.kind, st) : launch_persistent<false>(tmA, tmB, p, e.kind, st);
 
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);

@@ -74,6 +74,53 @@ def test_gemm_fp8_matches_quantized_definition(cuda, M, N, K):
     assert rel_fro(out, ref) < 5e-3
 
 
+@pytest.mark.parametrize("M", [600, 777, 1030])
+@pytest.mark.parametrize("kind", ["store", "swiglu", "gated_residual_f32", "residual_f32"])
+def test_gemm_fp8_pair_epilogues(cuda, M, kind):
+    """FP8 GEMMs with M >= 512 run on the 2-SM (CTA pair, 256 x 256 tile) kernel. Every epilogue kind
+    against the FP8 definition, with M leaving the last pair tile partly or wholly empty for one CTA."""
+    from sa3_b200 import ops, _lib
+
+    g = _gen(M + len(kind))
+    B, N, K = 2, 512, 384
+    x = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g) * 0.1
+    wq, sw = oq.quantize_weight_e4m3(w)
+    xd = x.to(cuda)
+    amax = torch.zeros(1, device=cuda)
+    ops.absmax(xd.bfloat16(), amax)
+    s = torch.zeros(1, device=cuda)
+    # fp32 definition of the linear on the same bf16-rounded activation the device quantises
+    h = oq.fp8_linear(x.bfloat16().float(), wq, sw, bias)
+    xq = ops.quantize_e4m3(xd.bfloat16(), amax, scale_out=s)
+    wd, swd, bd = wq.to(cuda), sw.to(cuda), bias.to(cuda)
+    rows_per_batch = (M + 1) // 2
+    if kind == "store":
+        out = ops.gemm(xq, wd, a_scale=s, b_scale=swd, bias=bd)
+        ref = h
+    elif kind == "swiglu":
+        out = ops.gemm(xq, wd, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_SWIGLU)
+        # rows are [x | gate] per 256-row block (the interleave the model applies to GLU.proj)
+        hb = h.view(M, N // 256, 2, 128)
+        ref = (hb[:, :, 0] * torch.nn.functional.silu(hb[:, :, 1])).reshape(M, N // 2)
+    else:
+        res = torch.randn(M, N, generator=g)
+        gate = torch.randn(B, N, generator=g)
+        out = res.clone().to(cuda)
+        if kind == "gated_residual_f32":
+            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_GATED_RESIDUAL, residual=out,
+                     gate=gate.to(cuda), rows_per_batch=rows_per_batch)
+            bidx = torch.arange(M) // rows_per_batch
+            ref = res + h * torch.sigmoid(1 - gate[bidx])
+        else:
+            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_RESIDUAL, residual=out)
+            ref = res + h
+    torch.cuda.synchronize()
+    assert rel_fro(out, ref) < 5e-3
+    assert _lib.device_error() == 0
+
+
 def test_gemm_epilogues(cuda):
     from sa3_b200 import ops, _lib
 
