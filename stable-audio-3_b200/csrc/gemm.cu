@@ -37,7 +37,60 @@ struct GemmParams {
   const float* a_scale;
   const float* b_scale;
   sa3_epilogue epi;
+  int tma_store;  // bf16 output through shared memory and TMA stores (no output-row remap)
 };
+
+// bf16 output chunks of 32 rows x 32 columns go out through a per-warp double buffer in shared
+// memory and one TMA store each. The buffers use the 64-byte swizzle of the output tensor map, so
+// the row writes below are free of bank conflicts; a buffer is reused only after the TMA store
+// that last read it has finished reading (bulk-group wait).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all_but_one() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct StoreStage {
+  const CUtensorMap* tm;  // output map: box 32 x 32 bf16, 64-byte swizzle
+  uint8_t* buf;           // this warp's 2 x 2 KB, 512-byte aligned
+  int next;               // buffer to fill next
+};
+
+// This thread's row of the chunk (v, columns col..col+31 of output row row0 + lane) -> bf16 -> TMA.
+__device__ __forceinline__ void stage_store32(StoreStage& st, int col, int row0, int M, const float (&v)[32],
+                                              float& amax, bool want_amax) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* b = st.buf + st.next * 2048;
+  if (lane == 0) bulk_wait_read_all_but_one();  // the store issued two chunks ago has read this buffer
+  __syncwarp();
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  if (want_amax && row0 + lane < M) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ ((lane >> 1) & 3)) * 16)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && row0 < M) {  // rows past M are clipped by the tensor map; a box wholly past M is skipped
+    tma_store_2d(st.tm, b, col, row0);
+    bulk_commit_group();
+  }
+  st.next ^= 1;
+}
 
 __device__ __forceinline__ int out_row_of(const sa3_epilogue& e, int m) {
   if (e.out_row_map) return __ldg(e.out_row_map + m);
@@ -545,7 +598,8 @@ __device__ __forceinline__ void pg_residual_tile_t(const GemmParams& p, uint32_t
 // half `half` (tmem_tile = the tile's first TMEM column). Shared by the FP8/bf16 and GPTQ kernels.
 template <int KIND>
 __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t tmem_tile, int m0, int n0, int q,
-                                                 int half, float sa, float& amax, float* scratch = nullptr) {
+                                                 int half, float sa, float& amax, float* scratch = nullptr,
+                                                 StoreStage* stg = nullptr) {
   const sa3_epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && scratch && e.c_f32 &&
@@ -571,7 +625,10 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           scale_bias32(g, n0 + 128 + col, sa, p.b_scale, e.bias);
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = x[i] * g[i] * fast_sigmoid(g[i]);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
+          if (stg)
+            stage_store32(*stg, n0 / 2 + col, m0 + q * 32, p.M, x, amax, e.amax_out != nullptr);
+          else
+            pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, n0 / 2 + col, x, amax);
         }
       } else if (KIND == SA3_EPI_QK_NORM) {
 #pragma unroll 1
@@ -585,8 +642,13 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           scale_bias32(v, nc, sa, p.b_scale, e.bias);
           scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
           qk_norm_rope64(e, m, nc, v, w);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc, v, amax);
-          pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc + 32, w, amax);
+          if (stg) {
+            stage_store32(*stg, nc, m0 + q * 32, p.M, v, amax, e.amax_out != nullptr);
+            stage_store32(*stg, nc + 32, m0 + q * 32, p.M, w, amax, e.amax_out != nullptr);
+          } else {
+            pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc, v, amax);
+            pg_store_chunk<SA3_EPI_STORE>(p, m, orow, 0, nc + 32, w, amax);
+          }
         }
       } else {
 #pragma unroll 1
@@ -597,7 +659,15 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           float v[32];
           tmem_ld32(trow + col, v);
           scale_bias32(v, nc, sa, p.b_scale, e.bias);
-          pg_store_chunk<KIND>(p, m, orow, batch, nc, v, amax);
+          if ((KIND == SA3_EPI_STORE || KIND == SA3_EPI_SILU) && stg) {
+            if (KIND == SA3_EPI_SILU) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = v[i] * fast_sigmoid(v[i]);
+            }
+            stage_store32(*stg, nc, m0 + q * 32, p.M, v, amax, e.amax_out != nullptr);
+          } else {
+            pg_store_chunk<KIND>(p, m, orow, batch, nc, v, amax);
+          }
         }
       }
 }
@@ -605,7 +675,7 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           GemmParams p, int tiles_n, int num_tiles) {
+                           const __grid_constant__ CUtensorMap tmC, GemmParams p, int tiles_n, int num_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
@@ -705,6 +775,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;  // column half of the tile
     float* epi_scratch = reinterpret_cast<float*>(smem + PG_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
+    // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
+    StoreStage stg{&tmC, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096, 0};
+    StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
     float amax = 0.f;
@@ -715,11 +788,12 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       tc_fence_after();
       const int m0 = (t / tiles_n) * GEMM_BM;
       const int n0 = (t % tiles_n) * GEMM_BN;
-      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch);
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch, stgp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
+    if (stgp && lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before the CTA exits
     if (e.amax_out) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -818,8 +892,8 @@ __device__ __forceinline__ bool warp_wait_g(uint64_t* bar, uint32_t parity, vola
 
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p,
-                     int tiles_n, int num_tiles) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, GemmParams p, int tiles_n, int num_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P2_STAGES * P2_STAGE_BYTES);
@@ -921,6 +995,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     float* epi_scratch = reinterpret_cast<float*>(smem + P2_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
+    // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
+    StoreStage stg{&tmC, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096, 0};
+    StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
     float amax = 0.f;
@@ -931,7 +1008,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       tc_fence_after();
       const int m0 = (t / tiles_n) * 256 + 128 * (int)rank;
       const int n0 = (t % tiles_n) * 256;
-      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch);
+      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch, stgp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -941,6 +1018,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
           mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
       }
     }
+    if (stgp && lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before the CTA exits
     if (e.amax_out) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -958,8 +1036,8 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
 }
 
 template <bool FP8>
-static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int kind,
-                       cudaStream_t st) {
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const GemmParams& p,
+                       int kind, cudaStream_t st) {
   const int tiles_n = (p.N + 255) / 256;
   const int tiles_m = (p.M + 255) / 256;
   const int num_tiles = tiles_n * tiles_m;
@@ -984,7 +1062,7 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
 #define SA3_P2_CASE(K)                                                                               \
   case K:                                                                                            \
     if ((rc = ensure_smem(gemm_pair_kernel<FP8, K>, P2_SMEM))) return rc;                            \
-    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, p, tiles_n, num_tiles) != cudaSuccess) \
+    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, tmC, p, tiles_n, num_tiles) != cudaSuccess) \
       return SA3_ERR_LAUNCH;                                                                         \
     break;
   switch (kind) {
@@ -1002,8 +1080,8 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
 }
 
 template <bool FP8>
-static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p, int kind,
-                             cudaStream_t st) {
+static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                             const GemmParams& p, int kind, cudaStream_t st) {
   const int tiles_n = (p.N + GEMM_BN - 1) / GEMM_BN;
   const int tiles_m = (p.M + GEMM_BM - 1) / GEMM_BM;
   const int num_tiles = tiles_n * tiles_m;
@@ -1019,7 +1097,7 @@ static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, con
 #define SA3_PG_CASE(K)                                                                                   \
   case K:                                                                                                \
     if ((rc = ensure_smem(gemm_persistent_kernel<FP8, K>, PG_SMEM))) return rc;                          \
-    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, p, tiles_n, num_tiles); \
+    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, tmC, p, tiles_n, num_tiles); \
     break;
   switch (kind) {
     SA3_PG_CASE(SA3_EPI_STORE)
@@ -1337,13 +1415,25 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (res_kind) fast = fast && aligned16(e.residual) && ((e.ld_residual * celt) % 16 == 0);
   if (e.kind == SA3_EPI_GATED_RESIDUAL) fast = fast && aligned16(e.gate) && (e.ld_gate % 4 == 0);
   if (!fast && e.kind == SA3_EPI_QK_NORM) return SA3_ERR_UNSUPPORTED;  // only the persistent kernel fuses it
+  // bf16 outputs without a row remap leave through TMA stores (tmC); otherwise tmC is unused
+  CUtensorMap tmC = tmA;
+  p.tma_store = 0;
+  if (fast && !e.c_f32 && !e.out_row_map && e.seg_in == 0 &&
+      (e.kind == SA3_EPI_STORE || e.kind == SA3_EPI_SILU || e.kind == SA3_EPI_SWIGLU || e.kind == SA3_EPI_QK_NORM)) {
+    const uint64_t ccols = e.kind == SA3_EPI_SWIGLU ? (uint64_t)N / 2 : (uint64_t)N;
+    if ((rc = make_tmap_2d(&tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ccols, (uint64_t)M, (uint64_t)ldc, 32, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+    p.tma_store = 1;
+  }
   if (fast && fp8 && M >= SA3_PAIR_MIN_ROWS) {
     // FP8 with enough rows for 256-row tiles: the 2-SM kernel. Its A and B boxes are 128 rows.
     CUtensorMap tmB2;
     if ((rc = make_tmap_2d(&tmB2, B, dt, esz, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, bk, 128))) return rc;
-    return launch_pair<true>(tmA, tmB2, p, e.kind, st);
+    return launch_pair<true>(tmA, tmB2, tmC, p, e.kind, st);
   }
-  if (fast) return fp8 ? launch_persistent<true>(tmA, tmB, p, e.kind, st) : launch_persistent<false>(tmA, tmB, p, e.kind, st);
+  if (fast)
+    return fp8 ? launch_persistent<true>(tmA, tmB, tmC, p, e.kind, st) : launch_persistent<false>(tmA, tmB, tmC, p, e.kind, st);
 
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);
   if (grid.y > 65535) return SA3_ERR_UNSUPPORTED;
@@ -1401,6 +1491,7 @@ extern "C" int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, voi
   p.a_scale = nullptr;
   p.b_scale = nullptr;
   p.epi = e;
+  p.tma_store = 0;
   const int tiles_n = N / GEMM_BN;
   const int num_tiles = tiles_n * ((M + GEMM_BM - 1) / GEMM_BM);
   int sms = 0, dev = 0;
