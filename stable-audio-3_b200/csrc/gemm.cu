@@ -57,9 +57,14 @@ __device__ __forceinline__ void bulk_wait_read_all_but_one() {
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 struct StoreStage {
-  const CUtensorMap* tm;  // output map: box 32 x 32 bf16, 64-byte swizzle
-  uint8_t* buf;           // this warp's 2 x 2 KB, 512-byte aligned
-  int next;               // buffer to fill next
+  const CUtensorMap* tm;   // output map: box 32 x 32 bf16, or 16 x 32 fp32 (residual kinds); 64-byte swizzle
+  const CUtensorMap* tmr;  // residual map (fp32 residual kinds): box 16 x 32 fp32, 64-byte swizzle
+  uint8_t* buf;            // this warp's 2 x 2 KB, 512-byte aligned
+  uint64_t* rbar;          // this warp's 2 residual-load barriers
+  volatile int* abort;
+  int next;                // bf16: buffer to fill next
+  int uses;                // residual: chunks loaded so far (barrier phase)
+  int pending;             // residual: loads issued and not yet consumed
 };
 
 // This thread's row of the chunk (v, columns col..col+31 of output row row0 + lane) -> bf16 -> TMA.
@@ -518,6 +523,81 @@ __device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int
   }
 }
 
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// sigmoid(x) = (1 + tanh(x / 2)) / 2 with one MUFU operation.
+__device__ __forceinline__ float sigmoid_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
+
+// Residual kinds into the fp32 stream through TMA: the residual of this warp's 32 rows x 32 columns
+// comes in as two 32 x 16 boxes (one per 2 KB buffer), is combined in place with the accumulator
+// chunk v (this thread's row) and leaves as two TMA stores. rb = this row's CFG batch.
+// Loads of one chunk's residual (lane 0). The first chunk of a tile is issued before the tile's
+// accumulator is ready, so its latency hides behind the main loop.
+__device__ __forceinline__ void residual_tma_issue(StoreStage& st, int M, int nc, int row0) {
+  if (row0 >= M) return;  // warp-uniform
+  st.pending = 1;
+  if ((threadIdx.x & 31) != 0) return;
+  bulk_wait_read_all();  // the stores of the previous chunk have read both buffers
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mbar_arrive_expect_tx(&st.rbar[h], 2048);
+    tma_load_2d(st.buf + h * 2048, st.tmr, &st.rbar[h], nc + 16 * h, row0);
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void residual_tma_chunk(StoreStage& st, const GemmParams& p, int nc, int row0, int rb,
+                                                   const float (&v)[32], float& amax) {
+  const sa3_epilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+  if (row0 >= p.M) return;  // warp-uniform: no valid row
+  __syncwarp();
+  const bool row_ok = row0 + lane < p.M;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mbar_wait(&st.rbar[h], st.uses & 1, st.abort, 77);
+    if (h == 1) st.pending = 0;
+    uint8_t* rowp = st.buf + h * 2048 + lane * 64;
+    float4 g4[4];
+    if (KIND == SA3_EPI_GATED_RESIDUAL) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        g4[c] = __ldg(reinterpret_cast<const float4*>(e.gate + (long long)rb * e.ld_gate + nc + 16 * h + 4 * c));
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float4* q = reinterpret_cast<float4*>(rowp + ((c ^ sw) * 16));
+      float4 r = *q;
+      const float* vv = v + 16 * h + 4 * c;
+      if (KIND == SA3_EPI_GATED_RESIDUAL) {
+        r.x = fmaf(vv[0], sigmoid_tanh(1.f - g4[c].x), r.x);
+        r.y = fmaf(vv[1], sigmoid_tanh(1.f - g4[c].y), r.y);
+        r.z = fmaf(vv[2], sigmoid_tanh(1.f - g4[c].z), r.z);
+        r.w = fmaf(vv[3], sigmoid_tanh(1.f - g4[c].w), r.w);
+      } else {
+        r.x += vv[0];
+        r.y += vv[1];
+        r.z += vv[2];
+        r.w += vv[3];
+      }
+      *q = r;
+      if (e.amax_out && row_ok) amax = fmaxf(amax, fmaxf(fmaxf(fabsf(r.x), fabsf(r.y)), fmaxf(fabsf(r.z), fabsf(r.w))));
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(st.tm, st.buf + h * 2048, nc + 16 * h, row0);
+      bulk_commit_group();
+    }
+  }
+  st.uses++;
+}
+
 // Residual epilogues into the fp32 stream, transposed through a per-warp shared-memory scratch of
 // 32 x 33 floats. TMEM hands each thread one row. In the write-back pass 8 threads cover one row's
 // 32 columns with float4 accesses, so each warp instruction moves 4 full 128-byte row segments
@@ -602,6 +682,23 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
                                                  StoreStage* stg = nullptr) {
   const sa3_epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
+  if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && stg && stg->tmr) {
+    const uint32_t trow = tmem_tile + ((uint32_t)(q * 32) << 16);
+    const int m = m0 + q * 32 + lane;
+    int rb = 0;
+    if (KIND == SA3_EPI_GATED_RESIDUAL && m < p.M) rb = e.row_batch ? __ldg(e.row_batch + m) : m / e.rows_per_batch;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      const int nc = n0 + half * 128 + c * 32;
+      if (nc >= p.N) break;  // uniform per warp
+      if (c > 0) residual_tma_issue(*stg, p.M, nc, m0 + q * 32);  // chunk 0 was issued by the caller
+      float v[32];
+      tmem_ld32(trow + half * 128 + c * 32, v);
+      scale_bias32(v, nc, sa, p.b_scale, e.bias);
+      residual_tma_chunk<KIND>(*stg, p, nc, m0 + q * 32, rb, v, amax);
+    }
+    return;
+  }
   if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && scratch && e.c_f32 &&
       ((reinterpret_cast<uintptr_t>(e.residual) | reinterpret_cast<uintptr_t>(p.C)) & 15) == 0 &&
       ((e.ld_residual | p.ldc) & 3) == 0 && (KIND != SA3_EPI_GATED_RESIDUAL || ((reinterpret_cast<uintptr_t>(e.gate) & 15) == 0 && (e.ld_gate & 3) == 0))) {
@@ -675,7 +772,8 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           const __grid_constant__ CUtensorMap tmC, GemmParams p, int tiles_n, int num_tiles) {
+                           const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                           GemmParams p, int tiles_n, int num_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_STAGES * GEMM_STAGE_BYTES);
@@ -700,6 +798,10 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       mbar_init(&acc_empty[a], PG_EPI_WARPS);
     }
     *abort_flag = 0;
+    {
+      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+      for (int i = 0; i < 2 * PG_EPI_WARPS; ++i) mbar_init(&rb[i], 1);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -776,7 +878,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int half = (warp - 2) >> 2;  // column half of the tile
     float* epi_scratch = reinterpret_cast<float*>(smem + PG_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
-    StoreStage stg{&tmC, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096, 0};
+    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+    StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -784,14 +888,21 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
       const uint32_t a = lt & 1;
-      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 35)) break;
-      tc_fence_after();
       const int m0 = (t / tiles_n) * GEMM_BM;
       const int n0 = (t % tiles_n) * GEMM_BN;
+      if (stgp && stgp->tmr && n0 + half * 128 < p.N) residual_tma_issue(stg, p.M, n0 + half * 128, m0 + q * 32);
+      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 35)) break;
+      tc_fence_after();
       pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch, stgp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+    if (stgp && stg.pending) {
+      // a residual load issued before an aborted accumulator wait: let it land before the CTA exits
+      volatile int never = 0;
+      mbar_wait(&stg.rbar[0], stg.uses & 1, &never, 78);
+      mbar_wait(&stg.rbar[1], stg.uses & 1, &never, 78);
     }
     if (stgp && lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before the CTA exits
     if (e.amax_out) {
@@ -893,7 +1004,8 @@ __device__ __forceinline__ bool warp_wait_g(uint64_t* bar, uint32_t parity, vola
 template <bool FP8, int KIND>
 __global__ void __launch_bounds__(PG_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, GemmParams p, int tiles_n, int num_tiles) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+                     GemmParams p, int tiles_n, int num_tiles) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + P2_STAGES * P2_STAGE_BYTES);
@@ -920,6 +1032,10 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       mbar_init(&acc_empty[a], 2 * PG_EPI_WARPS);
     }
     *abort_flag = 0;
+    {
+      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+      for (int i = 0; i < 2 * PG_EPI_WARPS; ++i) mbar_init(&rb[i], 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -996,7 +1112,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int half = (warp - 2) >> 2;
     float* epi_scratch = reinterpret_cast<float*>(smem + P2_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
-    StoreStage stg{&tmC, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096, 0};
+    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+    StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -1004,10 +1122,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     uint32_t lt = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++lt) {
       const uint32_t a = lt & 1;
-      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 76)) break;
-      tc_fence_after();
       const int m0 = (t / tiles_n) * 256 + 128 * (int)rank;
       const int n0 = (t % tiles_n) * 256;
+      if (stgp && stgp->tmr && n0 + half * 128 < p.N) residual_tma_issue(stg, p.M, n0 + half * 128, m0 + q * 32);
+      if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 76)) break;
+      tc_fence_after();
       pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch, stgp);
       tc_fence_before();
       __syncwarp();
@@ -1017,6 +1136,12 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         else
           mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
       }
+    }
+    if (stgp && stg.pending) {
+      // a residual load issued before an aborted accumulator wait: let it land before the CTA exits
+      volatile int never = 0;
+      mbar_wait(&stg.rbar[0], stg.uses & 1, &never, 78);
+      mbar_wait(&stg.rbar[1], stg.uses & 1, &never, 78);
     }
     if (stgp && lane == 0) bulk_wait_all();  // this warp's TMA stores are complete before the CTA exits
     if (e.amax_out) {
@@ -1036,8 +1161,8 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
 }
 
 template <bool FP8>
-static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const GemmParams& p,
-                       int kind, cudaStream_t st) {
+static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                       const CUtensorMap& tmR, const GemmParams& p, int kind, cudaStream_t st) {
   const int tiles_n = (p.N + 255) / 256;
   const int tiles_m = (p.M + 255) / 256;
   const int num_tiles = tiles_n * tiles_m;
@@ -1062,7 +1187,7 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUt
 #define SA3_P2_CASE(K)                                                                               \
   case K:                                                                                            \
     if ((rc = ensure_smem(gemm_pair_kernel<FP8, K>, P2_SMEM))) return rc;                            \
-    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, tmC, p, tiles_n, num_tiles) != cudaSuccess) \
+    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, tmC, tmR, p, tiles_n, num_tiles) != cudaSuccess) \
       return SA3_ERR_LAUNCH;                                                                         \
     break;
   switch (kind) {
@@ -1081,7 +1206,7 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUt
 
 template <bool FP8>
 static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
-                             const GemmParams& p, int kind, cudaStream_t st) {
+                             const CUtensorMap& tmR, const GemmParams& p, int kind, cudaStream_t st) {
   const int tiles_n = (p.N + GEMM_BN - 1) / GEMM_BN;
   const int tiles_m = (p.M + GEMM_BM - 1) / GEMM_BM;
   const int num_tiles = tiles_n * tiles_m;
@@ -1097,7 +1222,7 @@ static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, con
 #define SA3_PG_CASE(K)                                                                                   \
   case K:                                                                                                \
     if ((rc = ensure_smem(gemm_persistent_kernel<FP8, K>, PG_SMEM))) return rc;                          \
-    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, tmC, p, tiles_n, num_tiles); \
+    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, tmC, tmR, p, tiles_n, num_tiles); \
     break;
   switch (kind) {
     SA3_PG_CASE(SA3_EPI_STORE)
@@ -1426,14 +1551,27 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
       return rc;
     p.tma_store = 1;
   }
+  // fp32 residual kinds without a row remap: residual in and result out through TMA (tma_store = 2)
+  CUtensorMap tmR = tmA;
+  if (fast && e.c_f32 && !e.out_row_map && e.seg_in == 0 &&
+      (e.kind == SA3_EPI_GATED_RESIDUAL || e.kind == SA3_EPI_RESIDUAL) && (e.kind != SA3_EPI_GATED_RESIDUAL || e.ld_gate % 4 == 0)) {
+    if ((rc = make_tmap_2d(&tmC, C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 16, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+    if ((rc = make_tmap_2d(&tmR, e.residual, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)M,
+                           (uint64_t)e.ld_residual, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+    p.tma_store = 2;
+  }
   if (fast && fp8 && M >= SA3_PAIR_MIN_ROWS) {
     // FP8 with enough rows for 256-row tiles: the 2-SM kernel. Its A and B boxes are 128 rows.
     CUtensorMap tmB2;
     if ((rc = make_tmap_2d(&tmB2, B, dt, esz, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, bk, 128))) return rc;
-    return launch_pair<true>(tmA, tmB2, tmC, p, e.kind, st);
+    return launch_pair<true>(tmA, tmB2, tmC, tmR, p, e.kind, st);
   }
   if (fast)
-    return fp8 ? launch_persistent<true>(tmA, tmB, tmC, p, e.kind, st) : launch_persistent<false>(tmA, tmB, tmC, p, e.kind, st);
+    return fp8 ? launch_persistent<true>(tmA, tmB, tmC, tmR, p, e.kind, st)
+               : launch_persistent<false>(tmA, tmB, tmC, tmR, p, e.kind, st);
 
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);
   if (grid.y > 65535) return SA3_ERR_UNSUPPORTED;
