@@ -40,12 +40,16 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return u;
 }
 // q = e4m3(v * inv), saturating round-to-nearest-even (the oracle's definition).
+// Two fp32 -> two e4m3 (round to nearest even, saturating to +-448) in one instruction; the
+// first operand lands in the high byte, so (b, a) puts a in the lower byte.
+__device__ __forceinline__ uint32_t e4m3x2(float a, float b) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(b), "f"(a));
+  return d;
+}
 __device__ __forceinline__ uint2 pack8_e4m3(const float (&v)[8], float inv) {
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) lo |= (uint32_t)f32_to_e4m3(v[j] * inv) << (8 * j);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) hi |= (uint32_t)f32_to_e4m3(v[4 + j] * inv) << (8 * j);
+  const uint32_t lo = e4m3x2(v[0] * inv, v[1] * inv) | (e4m3x2(v[2] * inv, v[3] * inv) << 16);
+  const uint32_t hi = e4m3x2(v[4] * inv, v[5] * inv) | (e4m3x2(v[6] * inv, v[7] * inv) << 16);
   return make_uint2(lo, hi);
 }
 
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
       const int row = norm_row(p, blockIdx.x + li * gridDim.x);
       const uint8_t* rb = nsm + slot * rowbytes;
       float v[MAXC][8];
-      float ss = 0.f;
+      float ss4[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = lane + i * 32;
@@ -285,9 +289,10 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
             unpack8(reinterpret_cast<const uint4*>(rb)[c], v[i]);
           }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+          for (int j = 0; j < 8; ++j) ss4[j & 3] = fmaf(v[i][j], v[i][j], ss4[j & 3]);
         }
       }
+      float ss = (ss4[0] + ss4[1]) + (ss4[2] + ss4[3]);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // the row is in registers: the slot may refill
       ss = warp_sum(ss);
@@ -355,7 +360,11 @@ struct QuantParams {
   float* amax_out;
 };
 
-__global__ void __launch_bounds__(256) quantize_e4m3_kernel(QuantParams p) {
+// Eight independent 16-byte loads per thread and three 256-thread blocks per SM keep ~96 KB per SM
+// in flight, which the HBM latency needs. A thread walks its chunks with a fixed stride, so its
+// (row, chunk) position advances by a precomputed (row, chunk) step instead of a division.
+constexpr int QUANT_INFLIGHT = 8;
+__global__ void __launch_bounds__(256, 3) quantize_e4m3_kernel(QuantParams p) {
   const int cpr = p.cols / 8;  // 8-element chunks per row
   const long long total = (long long)p.rows * cpr;
   float s = 1.f;
@@ -365,34 +374,45 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(QuantParams p) {
   }
   float amax = 0.f;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  // Chunks are visited from the last row down: the producer of x (a GEMM walking its row tiles
-  // upwards, or the attention kernel) wrote the last rows last, so those are the ones still in L2.
-  // Four independent 16-byte loads in flight per thread.
-  for (long long j0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; j0 < total; j0 += 4 * stride) {
-    uint4 u[4];
+  const int dr = (int)(stride / cpr), dc = (int)(stride % cpr);
+  long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  int r0 = (int)(i0 / cpr), c0 = (int)(i0 % cpr);
+  for (; i0 < total; i0 += QUANT_INFLIGHT * stride) {
+    uint4 u[QUANT_INFLIGHT];
+    int r = r0, c = c0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const long long i = total - 1 - (j0 + k * stride);
-      if (i >= 0) {
-        const long long r = i / cpr;
-        u[k] = *reinterpret_cast<const uint4*>(p.x + r * p.ldx + (i - r * cpr) * 8);
+    for (int k = 0; k < QUANT_INFLIGHT; ++k) {
+      if (r < p.rows) u[k] = *reinterpret_cast<const uint4*>(p.x + (long long)r * p.ldx + c * 8);
+      r += dr;
+      c += dc;
+      if (c >= cpr) {
+        c -= cpr;
+        ++r;
       }
     }
+    r = r0;
+    c = c0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const long long i = total - 1 - (j0 + k * stride);
-      if (i >= 0) {
+    for (int k = 0; k < QUANT_INFLIGHT; ++k) {
+      if (r < p.rows) {
         float v[8];
         unpack8(u[k], v);
         if (p.amax_out) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
         } else {
-          const long long r = i / cpr;
-          *reinterpret_cast<uint2*>(p.out + r * p.ldo + (i - r * cpr) * 8) = pack8_e4m3(v, s);
+          *reinterpret_cast<uint2*>(p.out + (long long)r * p.ldo + c * 8) = pack8_e4m3(v, s);
         }
       }
+      r += dr;
+      c += dc;
+      if (c >= cpr) {
+        c -= cpr;
+        ++r;
+      }
     }
+    r0 = r;
+    c0 = c;
   }
   if (p.amax_out) block_amax_commit(amax, p.amax_out);
 }
@@ -629,7 +649,7 @@ extern "C" int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, l
                 amax, scale_out, amax_out};
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   long long qgrid = ((long long)rows * (cols / 8) + 1023) / 1024;
-  if (qgrid > 148 * 8) qgrid = 148 * 8;
+  if (qgrid > 148 * 3) qgrid = 148 * 3;
   if (qgrid < 1) qgrid = 1;
   quantize_e4m3_kernel<<<(int)qgrid, 256, 0, st>>>(p);
   return launch_status();

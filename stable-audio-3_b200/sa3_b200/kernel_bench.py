@@ -136,6 +136,17 @@ def case(name: str, iters: int) -> dict:
                                  quant_amax=am, scale_out=sc)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "GBps": (2 * M * D * 4 + M * D) / ms / 1e6}
+    if name in ("quant_attn", "quant_ff"):
+        # activation quantisation with the scale from a producer's max|x|: M x 1536 (attention output) and
+        # M x 6144 (FF hidden)
+        c = D if name == "quant_attn" else 4 * D
+        x = torch.randn(M, c, device=dev).bfloat16()
+        am = x.float().abs().max().reshape(1)
+        sc = torch.zeros(1, device=dev)
+        out = torch.empty(M, c, device=dev, dtype=torch.float8_e4m3fn)
+        fn = lambda: ops.quantize_e4m3(x, am, out=out, scale_out=sc)  # noqa: E731
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "GBps": 3 * M * c / ms / 1e6}
     if name == "qknorm":
         qkv = torch.randn(M, 5 * D, device=dev).bfloat16()
         gam = torch.ones(64, device=dev)
@@ -147,7 +158,7 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "qknorm", "ff1_gptq"]
+CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq"]
 
 
 def main():
