@@ -223,11 +223,11 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
 // Bulk-copy variant: warp 4 (lane 0) streams whole rows into an NORM_RING-deep shared-memory ring
 // with cp.async.bulk (one mbarrier per slot); warps 0..3 each normalise one row at a time from
 // shared memory. Up to NORM_RING rows per block are in flight independently of the consumers.
-constexpr int NORM_RING = 8;
+constexpr int NORM_RING = 12;
 constexpr int NORM_BULK_THREADS = 160;
 
 template <int MAXC, bool VEC>
-__global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormParams p, int rowbytes) {
+__global__ void __launch_bounds__(NORM_BULK_THREADS, 2) rmsnorm_bulk_kernel(NormParams p, int rowbytes) {
   extern __shared__ __align__(16) uint8_t nsm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(nsm + NORM_RING * rowbytes);
   uint64_t* empty = full + NORM_RING;
@@ -269,6 +269,8 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
       }
     }
   } else {
+    int cur_b = -1;  // CFG batch whose coefficients ca hold (VEC)
+    float ca[MAXC][8];
     for (int li = warp; li < nrows; li += 4) {
       const int slot = li % NORM_RING;
       if (!mbar_wait(&full[slot], (li / NORM_RING) & 1, abort_flag, 62)) break;
@@ -297,38 +299,52 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS) rmsnorm_bulk_kernel(NormPar
       if (lane == 0) mbar_arrive(&empty[slot]);  // the row is in registers: the slot may refill
       ss = warp_sum(ss);
       const float r = rsqrtf(ss / (float)p.D + p.eps);
-      const float* msc = nullptr;
-      const float* msh = nullptr;
-      if (p.mod) {
-        const int b = p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch;
-        msc = p.mod + (long long)b * p.ld_mod + p.scale_off;
-        msh = p.mod + (long long)b * p.ld_mod + p.shift_off;
+      const int b = p.mod ? (p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch) : 0;
+      if (VEC && b != cur_b) {
+        // warp-uniform (one row per warp): y = x * r * a + shift with a = gamma * (1 + scale) held in
+        // registers across rows of the same CFG batch; the shift row is read per row
+        cur_b = b;
+        const float* msc = p.mod ? p.mod + (long long)b * p.ld_mod + p.scale_off : nullptr;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+          const int c = lane + i * 32;
+          if (c < nchunk) {
+            float gm[8], sc[8];
+            if (p.gamma) ld8f(p.gamma + c * 8, gm);
+            if (msc) ld8f(msc + c * 8, sc);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float g = p.gamma ? gm[j] : 1.f;
+              ca[i][j] = msc ? g * (1.f + sc[j]) : g;
+            }
+          }
+        }
       }
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = lane + i * 32;
         if (c < nchunk) {
-          float y[8], gm[8], sc[8], sh[8];
+          float y[8];
           if (VEC) {
-            if (p.gamma) ld8f(p.gamma + c * 8, gm);
-            if (msc) {
-              ld8f(msc + c * 8, sc);
-              ld8f(msh + c * 8, sh);
+            float sh[8];
+            if (p.mod) {
+              ld8f(p.mod + (long long)b * p.ld_mod + p.shift_off + c * 8, sh);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) sh[j] = 0.f;
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = fmaf(v[i][j] * r, ca[i][j], sh[j]);
           } else {
+            const float* msc = p.mod ? p.mod + (long long)b * p.ld_mod + p.scale_off : nullptr;
+            const float* msh = p.mod ? p.mod + (long long)b * p.ld_mod + p.shift_off : nullptr;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              gm[j] = p.gamma ? __ldg(p.gamma + c * 8 + j) : 1.f;
-              sc[j] = msc ? __ldg(msc + c * 8 + j) : 0.f;
-              sh[j] = msh ? __ldg(msh + c * 8 + j) : 0.f;
+              float t = v[i][j] * r;
+              if (p.gamma) t *= __ldg(p.gamma + c * 8 + j);
+              if (msc) t = fmaf(t, 1.f + __ldg(msc + c * 8 + j), __ldg(msh + c * 8 + j));
+              y[j] = t;
             }
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float t = v[i][j] * r;
-            if (p.gamma) t *= gm[j];
-            if (msc) t = fmaf(t, 1.f + sc[j], sh[j]);
-            y[j] = t;
           }
           if (p.mode == SA3_NORM_AMAX) {
 #pragma unroll
@@ -595,9 +611,10 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
                                                     shift_off % 4 == 0));
   const int rowbytes = D * (x_dtype == SA3_DT_F32 ? 4 : 2);
   if (rowbytes % 16 == 0 && rowbytes * NORM_RING <= 96 * 1024 && nchunk <= 32 * 8) {
-    // bulk-copy pipeline: one row per slot; 3 blocks of 5 warps per SM
+    // bulk-copy pipeline: one row per slot; 2 blocks of 5 warps per SM (the consumers hold a row and
+    // its modulation coefficients in registers), 2 x NORM_RING rows in flight per SM
     const int smem = NORM_RING * rowbytes + 2 * NORM_RING * 8 + 16;
-    int gridb = rows < 148 * 3 ? rows : 148 * 3;
+    int gridb = rows < 148 * 2 ? rows : 148 * 2;
 #define SA3_NORM_BULK(C)                                                                             \
   if (vec) {                                                                                         \
     if ((rc = ensure_smem(rmsnorm_bulk_kernel<C, true>, 96 * 1024 + 256))) return rc;                \
