@@ -220,6 +220,86 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
 
+// Direct-load variant for the fp32 stream: 8 warps per block, 3 blocks per SM, one row per warp in
+// flight (24 x 6 KB per SM at D = 1536). Lane l owns the float4s l + 32 k of the row, so every warp
+// load is 512 contiguous bytes. The modulation coefficients a = gamma * (1 + scale) and shift of up
+// to two CFG batches sit in a shared-memory table built at block start; rows of other batches
+// (packed variable-length inputs) read them from global memory.
+constexpr int NORM_D_THREADS = 256;
+template <int NV>  // float4s per lane: D = 128 * NV
+__global__ void __launch_bounds__(NORM_D_THREADS, 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int idx = threadIdx.x; idx < tab_batches * p.D; idx += blockDim.x) {
+    const int b = idx / p.D, j = idx - b * p.D;
+    const float g = p.gamma ? __ldg(p.gamma + j) : 1.f;
+    if (p.mod) {
+      ntab[(2 * b) * p.D + j] = g * (1.f + __ldg(p.mod + (long long)b * p.ld_mod + p.scale_off + j));
+      ntab[(2 * b + 1) * p.D + j] = __ldg(p.mod + (long long)b * p.ld_mod + p.shift_off + j);
+    } else {
+      ntab[(2 * b) * p.D + j] = g;
+      ntab[(2 * b + 1) * p.D + j] = 0.f;
+    }
+  }
+  __syncthreads();
+  float s = 1.f;
+  if (p.mode == SA3_NORM_WRITE && p.out_dtype == SA3_DT_E4M3) {
+    s = quant_inv_scale(p.quant_amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
+  }
+  float amax = 0.f;
+  const int nw = gridDim.x * (NORM_D_THREADS / 32);
+  for (int li = blockIdx.x * (NORM_D_THREADS / 32) + warp; li < p.rows; li += nw) {
+    const int row = norm_row(p, li);
+    const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (long long)row * p.ldx);
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) v[k] = xr[lane + 32 * k];
+    float ss4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      ss4[0] = fmaf(v[k].x, v[k].x, ss4[0]);
+      ss4[1] = fmaf(v[k].y, v[k].y, ss4[1]);
+      ss4[2] = fmaf(v[k].z, v[k].z, ss4[2]);
+      ss4[3] = fmaf(v[k].w, v[k].w, ss4[3]);
+    }
+    const float r = rsqrtf(warp_sum((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / (float)p.D + p.eps);
+    const int b = p.mod ? (p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch) : 0;
+    const bool in_tab = b < tab_batches;  // warp-uniform
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int e = 4 * (lane + 32 * k);  // first element of this float4
+      float4 a, sh;
+      if (in_tab) {
+        a = *reinterpret_cast<const float4*>(ntab + (2 * b) * p.D + e);
+        sh = *reinterpret_cast<const float4*>(ntab + (2 * b + 1) * p.D + e);
+      } else {
+        const float4 g = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + e)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        if (p.mod) {
+          const float4 sc = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.scale_off + e));
+          sh = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.shift_off + e));
+          a = make_float4(g.x * (1.f + sc.x), g.y * (1.f + sc.y), g.z * (1.f + sc.z), g.w * (1.f + sc.w));
+        } else {
+          a = g;
+          sh = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      const float y0 = fmaf(v[k].x * r, a.x, sh.x), y1 = fmaf(v[k].y * r, a.y, sh.y);
+      const float y2 = fmaf(v[k].z * r, a.z, sh.z), y3 = fmaf(v[k].w * r, a.w, sh.w);
+      if (p.mode == SA3_NORM_AMAX) {
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
+      } else if (p.out_dtype == SA3_DT_E4M3) {
+        *reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(p.out) + (long long)row * p.ldo + e) =
+            e4m3x2(y0 * s, y1 * s) | (e4m3x2(y2 * s, y3 * s) << 16);
+      } else {
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + e) =
+            make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+      }
+    }
+  }
+  if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
+}
+
 // Bulk-copy variant: warp 4 (lane 0) streams whole rows into an NORM_RING-deep shared-memory ring
 // with cp.async.bulk (one mbarrier per slot); warps 0..3 each normalise one row at a time from
 // shared memory. Up to NORM_RING rows per block are in flight independently of the consumers.
@@ -610,6 +690,32 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   const bool vec = aligned16(gamma) && (!mod || (aligned16(mod) && ld_mod % 4 == 0 && scale_off % 4 == 0 &&
                                                     shift_off % 4 == 0));
   const int rowbytes = D * (x_dtype == SA3_DT_F32 ? 4 : 2);
+  if (vec && x_dtype == SA3_DT_F32 && D % 128 == 0 && D <= 4096 && ldx % 4 == 0 &&
+      (mode == SA3_NORM_AMAX || out_dtype == SA3_DT_BF16 ? (ldo % 4 == 0) : (ldo % 4 == 0))) {
+    int tab_batches = 1;
+    if (mod) tab_batches = (!row_batch && rows_per_batch > 0 && (rows + rows_per_batch - 1) / rows_per_batch <= 2)
+                               ? (rows + rows_per_batch - 1) / rows_per_batch
+                               : 0;
+    const int smem = tab_batches * 2 * D * 4;
+    int gridd = (rows + 7) / 8;
+    if (gridd > 148 * 3) gridd = 148 * 3;
+    int rc;
+#define SA3_NORM_DIRECT(V)                                                               \
+  case V:                                                                                \
+    if ((rc = ensure_smem(rmsnorm_direct_kernel<V>, 2 * 2 * 4096 * 4))) return rc;       \
+    rmsnorm_direct_kernel<V><<<gridd, NORM_D_THREADS, smem, st>>>(p, tab_batches);        \
+    break;
+    switch (D / 128) {
+      SA3_NORM_DIRECT(8)
+      SA3_NORM_DIRECT(12)
+      SA3_NORM_DIRECT(16)
+      default:
+        goto bulk_path;
+    }
+#undef SA3_NORM_DIRECT
+    return launch_status();
+  }
+bulk_path:
   if (rowbytes % 16 == 0 && rowbytes * NORM_RING <= 96 * 1024 && nchunk <= 32 * 8) {
     // bulk-copy pipeline: one row per slot; 2 blocks of 5 warps per SM (the consumers hold a row and
     // its modulation coefficients in registers), 2 x NORM_RING rows in flight per SM
