@@ -1563,11 +1563,12 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
       return rc;
     p.tma_store = 2;
   }
-  if (fast && fp8 && M >= SA3_PAIR_MIN_ROWS) {
-    // FP8 with enough rows for 256-row tiles: the 2-SM kernel. Its A and B boxes are 128 rows.
+  if (fast && M >= SA3_PAIR_MIN_ROWS) {
+    // enough rows for 256-row tiles: the 2-SM kernel (FP8 or bf16). Its A and B boxes are 128 rows.
     CUtensorMap tmB2;
     if ((rc = make_tmap_2d(&tmB2, B, dt, esz, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, bk, 128))) return rc;
-    return launch_pair<true>(tmA, tmB2, tmC, tmR, p, e.kind, st);
+    return fp8 ? launch_pair<true>(tmA, tmB2, tmC, tmR, p, e.kind, st)
+               : launch_pair<false>(tmA, tmB2, tmC, tmR, p, e.kind, st);
   }
   if (fast)
     return fp8 ? launch_persistent<true>(tmA, tmB, tmC, tmR, p, e.kind, st)
