@@ -360,8 +360,9 @@ def run_ours(args, wl, world, rank, local):
     else:
         scale = ws.scale[4:5]
         run_k = lambda: eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)  # noqa: E731
-        kname = ("gemm_persistent_kernel<fp8, SwiGLU>" if lin.fp8 else "gemm_persistent_kernel<bf16, SwiGLU>") + \
-            " (FF GLU.proj)"
+        # M >= 512 runs on the 2-SM (CTA pair) kernel, smaller M on the single-SM one
+        kern = "gemm_pair_kernel" if M >= 512 else "gemm_persistent_kernel"
+        kname = f"{kern}<{'fp8' if lin.fp8 else 'bf16'}, SwiGLU> (FF GLU.proj)"
     reps = 20
     with torch.inference_mode():
         for _ in range(3):

@@ -232,6 +232,44 @@ def test_rmsnorm_modulate(cuda):
     assert max_rel(out, orf.rms_norm(x.float(), gamma, 1e-5)) < 1e-2
 
 
+@pytest.mark.parametrize("layout", ["two_batches", "three_batches", "row_batch", "no_mod"])
+def test_rmsnorm_modulate_fp32_stream(cuda, layout):
+    """RMSNorm + modulate of the fp32 residual stream (the direct-load kernel): the per-block coefficient table
+    (<= 2 CFG batches), the per-row global path (3 batches, or a row -> batch table as in packed variable-length
+    batches) and plain RMSNorm; max|y| pass, e4m3 and bf16 outputs vs the oracle."""
+    from sa3_b200 import ops
+
+    g = _gen(41)
+    D = 1536
+    lens = {"two_batches": [333, 333], "three_batches": [200, 200, 200], "row_batch": [120, 301, 77],
+            "no_mod": [250]}[layout]
+    B, M = len(lens), sum(lens)
+    x = torch.randn(M, D, generator=g) * 3
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    mod = torch.randn(B, 6 * D, generator=g) * 0.3
+    bidx = torch.repeat_interleave(torch.arange(B), torch.tensor(lens))
+    kw = {}
+    if layout == "no_mod":
+        ref = orf.rms_norm(x, gamma, 1e-5)
+    else:
+        ref = orf.modulate(orf.rms_norm(x, gamma, 1e-5), mod[bidx, 0:D], mod[bidx, D:2 * D])
+        kw = dict(mod=mod.to(cuda), scale_off=0, shift_off=D)
+        if layout == "row_batch":
+            kw["row_batch"] = bidx.to(torch.int32).to(cuda)
+        else:
+            kw["rows_per_batch"] = lens[0]
+    xd, gd = x.to(cuda), gamma.to(cuda)
+    out = ops.rmsnorm_modulate(xd, gd, 1e-5, **kw)
+    assert max_rel(out, ref) < 1e-2
+    amax = torch.zeros(1, device=cuda)
+    ops.rmsnorm_modulate(xd, gd, 1e-5, amax_only=amax, **kw)
+    torch.cuda.synchronize()
+    assert abs(amax.item() - ref.abs().max().item()) / ref.abs().max().item() < 1e-5
+    s = torch.zeros(1, device=cuda)
+    q = ops.rmsnorm_modulate(xd, gd, 1e-5, out_dtype=torch.float8_e4m3fn, quant_amax=amax, scale_out=s, **kw)
+    assert rel_fro(q.float().cpu() * s.cpu(), oq.fake_quant_act(ref)) < 2e-2
+
+
 def test_qk_norm_rope(cuda):
     from sa3_b200 import ops
 
