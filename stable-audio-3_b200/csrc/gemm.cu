@@ -399,7 +399,13 @@ constexpr int PG_SCRATCH_OFFSET = GEMM_STAGES * GEMM_STAGE_BYTES + 256;
 constexpr int PG_SMEM = PG_SCRATCH_OFFSET + PG_EPI_WARPS * 32 * 33 * 4 + 1024;
 static_assert(PG_SMEM <= 232448, "persistent GEMM exceeds the 227 KB shared-memory limit");
 
-__device__ __forceinline__ float fast_sigmoid(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+// sigmoid(x) = (1 + tanh(x / 2)) / 2: one MUFU operation (tanh.approx, relative error ~2^-11) instead of an
+// exponential and a reciprocal; the epilogues that use it write bf16 or feed an fp32 residual update.
+__device__ __forceinline__ float fast_sigmoid(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
 
 __device__ __forceinline__ void ldg_f32x32(const float* p, float (&v)[32]) {
   const float4* q = reinterpret_cast<const float4*>(p);
@@ -525,13 +531,6 @@ __device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int
 
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
-// sigmoid(x) = (1 + tanh(x / 2)) / 2 with one MUFU operation.
-__device__ __forceinline__ float sigmoid_tanh(float x) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
-  return fmaf(0.5f, t, 0.5f);
-}
-
 // Residual kinds into the fp32 stream through TMA: the residual of this warp's 32 rows x 32 columns
 // comes in as two 32 x 16 boxes (one per 2 KB buffer), is combined in place with the accumulator
 // chunk v (this thread's row) and leaves as two TMA stores. rb = this row's CFG batch.
@@ -575,10 +574,10 @@ __device__ __forceinline__ void residual_tma_chunk(StoreStage& st, const GemmPar
       float4 r = *q;
       const float* vv = v + 16 * h + 4 * c;
       if (KIND == SA3_EPI_GATED_RESIDUAL) {
-        r.x = fmaf(vv[0], sigmoid_tanh(1.f - g4[c].x), r.x);
-        r.y = fmaf(vv[1], sigmoid_tanh(1.f - g4[c].y), r.y);
-        r.z = fmaf(vv[2], sigmoid_tanh(1.f - g4[c].z), r.z);
-        r.w = fmaf(vv[3], sigmoid_tanh(1.f - g4[c].w), r.w);
+        r.x = fmaf(vv[0], fast_sigmoid(1.f - g4[c].x), r.x);
+        r.y = fmaf(vv[1], fast_sigmoid(1.f - g4[c].y), r.y);
+        r.z = fmaf(vv[2], fast_sigmoid(1.f - g4[c].z), r.z);
+        r.w = fmaf(vv[3], fast_sigmoid(1.f - g4[c].w), r.w);
       } else {
         r.x += vv[0];
         r.y += vv[1];
