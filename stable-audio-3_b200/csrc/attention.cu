@@ -259,6 +259,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the set-up above may run while the previous kernel on the stream retires
   // Register split: the TMA / MMA warpgroup hands registers to the softmax warpgroups, which hold a
   // full 128-column score row. ATT_REGS_LOW * 128 + ATT_REGS_HIGH * 256 stays below the launch's
   // 168 * 384 (static_assert above), so the increase never waits on registers that do not exist.
@@ -712,7 +713,7 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
   const int grid = num_items < sms ? (int)num_items : sms;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
-  attention_tc_kernel<<<grid, ATT_THREADS, ATT_SMEM, st>>>(mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
+  launch_ex(attention_tc_kernel, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, st, 1, mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
                                                             pairs_per_head);
   return launch_status();
 }

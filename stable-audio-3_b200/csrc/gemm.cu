@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the set-up above may run while the previous kernel on the stream retires
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
@@ -495,7 +496,20 @@ __device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int o
 
 // RMSNorm over one 64-column head (v = dims 0..31, w = dims 32..63) with its group's gamma, then
 // rotate_half RoPE on dims 0..31 (pairs i, i+16) at this row's position; fp32 throughout.
-__device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int nc, float (&v)[32], float (&w)[32]) {
+// RoPE cos/sin row of output row m (clamped into [0, M) for the padding rows of the last tile) for the
+// 64-column head at nc, loaded before the tile's accumulator is ready. Leaves cs untouched when the
+// head's group has no rotary embedding.
+__device__ __forceinline__ void qk_rope_prefetch(const sa3_epilogue& e, int m, int M, int nc, int N, float (&cs)[32]) {
+  if (nc >= N || !((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u)) return;
+  m = m < M ? m : M - 1;
+  int pos = e.row_pos ? __ldg(e.row_pos + m) : (e.rows_per_batch > 0 ? m % e.rows_per_batch : 0);
+  if (pos >= e.max_pos) pos = e.max_pos - 1;
+  if (pos < 0) pos = 0;
+  ldg_f32x32(e.cos_sin + (long long)pos * 32, cs);  // cos[0..15], sin[0..15]
+}
+
+// qk RMSNorm (gamma of the head's group) of one 64-column head held as v = dims 0..31, w = dims 32..63.
+__device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (&v)[32], float (&w)[32]) {
   const int g = nc / e.qk_group_width;
   const float* gam = nullptr;
 #pragma unroll
@@ -514,12 +528,12 @@ __device__ __forceinline__ void qk_norm_rope64(const sa3_epilogue& e, int m, int
 #pragma unroll
     for (int i = 0; i < 32; ++i) w[i] *= r * gv[i];
   }
-  if ((e.qk_rope_mask >> g) & 1u) {
-    int pos = e.row_pos ? __ldg(e.row_pos + (m < 0 ? 0 : m)) : (e.rows_per_batch > 0 ? m % e.rows_per_batch : 0);
-    if (pos >= e.max_pos) pos = e.max_pos - 1;
-    if (pos < 0) pos = 0;
-    float cs[32];
-    ldg_f32x32(e.cos_sin + (long long)pos * 32, cs);  // cos[0..15], sin[0..15]
+}
+
+// Rotary embedding of dims 0..31 of the head (pairs i, i + 16) with the cos/sin row cs, when the
+// head's group has one.
+__device__ __forceinline__ void qk_rope64(const sa3_epilogue& e, int nc, const float (&cs)[32], float (&v)[32]) {
+  if ((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float a = v[i], b = v[i + 16];
@@ -675,10 +689,13 @@ __device__ __forceinline__ void pg_residual_tile_t(const GemmParams& p, uint32_t
 
 // Epilogue of one 128 x 256 accumulator tile for the 32 rows of TMEM lane quarter q and column
 // half `half` (tmem_tile = the tile's first TMEM column). Shared by the FP8/bf16 and GPTQ kernels.
-template <int KIND>
+// CS_PRE: for the qk-norm kind, *cs_pre is the cos/sin row of this thread's row, prefetched by
+// qk_rope_prefetch for column n0 + half * 128 (all heads of a half belong to one group); otherwise it
+// is loaded here per head.
+template <int KIND, bool CS_PRE = false>
 __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t tmem_tile, int m0, int n0, int q,
                                                  int half, float sa, float& amax, float* scratch = nullptr,
-                                                 StoreStage* stg = nullptr) {
+                                                 StoreStage* stg = nullptr, const float (*cs_pre)[32] = nullptr) {
   const sa3_epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
   if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && stg && stg->tmr) {
@@ -737,7 +754,14 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           tmem_ld32(trow + col + 32, w);
           scale_bias32(v, nc, sa, p.b_scale, e.bias);
           scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
-          qk_norm_rope64(e, m, nc, v, w);
+          qk_norm64(e, nc, v, w);
+          if (CS_PRE) {
+            qk_rope64(e, nc, *cs_pre, v);
+          } else if ((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u) {
+            float cs[32];  // the kernels with fewer registers per thread load it per head
+            qk_rope_prefetch(e, m, p.M, nc, p.N, cs);
+            qk_rope64(e, nc, cs, v);
+          }
           if (stg) {
             stage_store32(*stg, nc, m0 + q * 32, p.M, v, amax, e.amax_out != nullptr);
             stage_store32(*stg, nc + 32, m0 + q * 32, p.M, w, amax, e.amax_out != nullptr);
@@ -813,6 +837,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the set-up above may run while the previous kernel on the stream retires
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1049,6 +1074,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the set-up above may run while the previous kernel on the stream retires
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1124,9 +1150,12 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
       const int m0 = (t / tiles_n) * 256 + 128 * (int)rank;
       const int n0 = (t % tiles_n) * 256;
       if (stgp && stgp->tmr && n0 + half * 128 < p.N) residual_tma_issue(stg, p.M, n0 + half * 128, m0 + q * 32);
+      float cs[32];
+      if (KIND == SA3_EPI_QK_NORM) qk_rope_prefetch(e, m0 + q * 32 + lane, p.M, n0 + half * 128, p.N, cs);
       if (!mbar_wait(&acc_full[a], (lt >> 1) & 1, abort_flag, 76)) break;
       tc_fence_after();
-      pg_epilogue_tile<KIND>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch, stgp);
+      pg_epilogue_tile<KIND, KIND == SA3_EPI_QK_NORM>(p, tmem + a * GEMM_BN, m0, n0, q, half, sa, amax, epi_scratch,
+                                                       stgp, &cs);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -1170,24 +1199,13 @@ static int launch_pair(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUt
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 2)
     return SA3_ERR_LAUNCH;
   const int npairs = num_tiles < sms / 2 ? num_tiles : sms / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * npairs, 1, 1);
-  cfg.blockDim = dim3(PG_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = P2_SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   int rc;
 #define SA3_P2_CASE(K)                                                                               \
   case K:                                                                                            \
     if ((rc = ensure_smem(gemm_pair_kernel<FP8, K>, P2_SMEM))) return rc;                            \
-    if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8, K>, tmA, tmB, tmC, tmR, p, tiles_n, num_tiles) != cudaSuccess) \
-      return SA3_ERR_LAUNCH;                                                                         \
+    if ((rc = launch_ex(gemm_pair_kernel<FP8, K>, dim3(2 * npairs), dim3(PG_THREADS), P2_SMEM, st, 2, tmA, tmB, \
+                        tmC, tmR, p, tiles_n, num_tiles)))                                                  \
+      return rc;                                                                                     \
     break;
   switch (kind) {
     SA3_P2_CASE(SA3_EPI_STORE)
@@ -1221,7 +1239,7 @@ static int launch_persistent(const CUtensorMap& tmA, const CUtensorMap& tmB, con
 #define SA3_PG_CASE(K)                                                                                   \
   case K:                                                                                                \
     if ((rc = ensure_smem(gemm_persistent_kernel<FP8, K>, PG_SMEM))) return rc;                          \
-    gemm_persistent_kernel<FP8, K><<<grid, PG_THREADS, PG_SMEM, st>>>(tmA, tmB, tmC, tmR, p, tiles_n, num_tiles); \
+    launch_ex(gemm_persistent_kernel<FP8, K>, dim3(grid), dim3(PG_THREADS), PG_SMEM, st, 1, tmA, tmB, tmC, tmR, p, tiles_n, num_tiles); \
     break;
   switch (kind) {
     SA3_PG_CASE(SA3_EPI_STORE)
@@ -1317,6 +1335,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the set-up above may run while the previous kernel on the stream retires
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1426,6 +1445,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1)
 
 __global__ void __launch_bounds__(256) gptq_dequant_kernel(const uint32_t* qw, const float* sz, __nv_bfloat16* out,
                                                            int N, int K, int group_size) {
+  grid_dep_wait();
   const long long words = (long long)N * (K / 8);
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += (long long)gridDim.x * blockDim.x) {
     const int n = (int)(i / (K / 8));
@@ -1439,6 +1459,7 @@ __global__ void __launch_bounds__(256) gptq_dequant_kernel(const uint32_t* qw, c
 // out[r, j] = x[r, perm[j]] (bf16); one row staged in shared memory per iteration.
 __global__ void __launch_bounds__(256) permute_cols_kernel(const __nv_bfloat16* x, const int* perm, __nv_bfloat16* out,
                                                            int rows, int K, long long ldx, long long ldo) {
+  grid_dep_wait();
   extern __shared__ __align__(16) uint8_t prow_raw[];
   __nv_bfloat16* rowbuf = reinterpret_cast<__nv_bfloat16*>(prow_raw);
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -1577,10 +1598,10 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (grid.y > 65535) return SA3_ERR_UNSUPPORTED;
   if (fp8) {
     if ((rc = ensure_smem(gemm_tc_kernel<true>, GEMM_SMEM))) return rc;
-    gemm_tc_kernel<true><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
+    launch_ex(gemm_tc_kernel<true>, dim3(grid), dim3(128), GEMM_SMEM, st, 1, tmA, tmB, p);
   } else {
     if ((rc = ensure_smem(gemm_tc_kernel<false>, GEMM_SMEM))) return rc;
-    gemm_tc_kernel<false><<<grid, 128, GEMM_SMEM, st>>>(tmA, tmB, p);
+    launch_ex(gemm_tc_kernel<false>, dim3(grid), dim3(128), GEMM_SMEM, st, 1, tmA, tmB, p);
   }
   return launch_status();
 }
@@ -1641,7 +1662,7 @@ extern "C" int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, voi
 #define SA3_GQ_CASE(K_)                                                                                        \
   case K_:                                                                                                     \
     if ((rc = ensure_smem(gemm_gptq_kernel<K_>, GQ_SMEM))) return rc;                                          \
-    gemm_gptq_kernel<K_><<<grid, GQ_THREADS, GQ_SMEM, st>>>(tmA, tmW, tmSZ, p, tiles_n, num_tiles, group_size); \
+    launch_ex(gemm_gptq_kernel<K_>, dim3(grid), dim3(GQ_THREADS), GQ_SMEM, st, 1, tmA, tmW, tmSZ, p, tiles_n, num_tiles, group_size); \
     break;
   switch (e.kind) {
     SA3_GQ_CASE(SA3_EPI_STORE)
@@ -1664,7 +1685,7 @@ extern "C" int sa3_gptq_dequant(const void* qw, const float* sz, void* out, int 
   const long long words = (long long)N * (K / 8);
   long long grid = (words + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
-  gptq_dequant_kernel<<<(int)grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_ex(gptq_dequant_kernel, dim3((int)grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       reinterpret_cast<const uint32_t*>(qw), sz, reinterpret_cast<__nv_bfloat16*>(out), N, K, group_size);
   return launch_status();
 }
@@ -1679,7 +1700,7 @@ extern "C" int sa3_permute_cols(const void* x, const int* perm, void* out, int r
   // the attribute is set once per device, so set it to the largest row this kernel accepts
   if ((rc = ensure_smem(permute_cols_kernel, 96 * 1024))) return rc;
   const int grid = rows < 148 * 8 ? rows : 148 * 8;
-  permute_cols_kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_ex(permute_cols_kernel, dim3(grid), dim3(256), smem, reinterpret_cast<cudaStream_t>(stream), 1, 
       reinterpret_cast<const __nv_bfloat16*>(x), perm, reinterpret_cast<__nv_bfloat16*>(out), rows, K, ldx, ldo);
   return launch_status();
 }

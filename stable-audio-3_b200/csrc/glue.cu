@@ -138,6 +138,7 @@ __device__ __forceinline__ int norm_row(const NormParams& p, int i) {
 // and the modulation rows are 16-byte aligned and come in as float4 loads.
 template <int MAXC, bool VEC>
 __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
+  grid_dep_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunk = p.D / 8;
   float s = 1.f;
@@ -220,25 +221,78 @@ __global__ void __launch_bounds__(128) rmsnorm_modulate_kernel(NormParams p) {
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
 
-// Direct-load variant for the fp32 stream: 8 warps per block, 3 blocks per SM, one row per warp in
-// flight (24 x 6 KB per SM at D = 1536). Lane l owns the float4s l + 32 k of the row, so every warp
-// load is 512 contiguous bytes. The modulation coefficients a = gamma * (1 + scale) and shift of up
-// to two CFG batches sit in a shared-memory table built at block start; rows of other batches
-// (packed variable-length inputs) read them from global memory.
+// Direct-load variant for the fp32 stream: 8 warps per block, one row per warp at a time, lane l
+// owning the float4s l + 32 k of the row, so every warp load is 512 contiguous bytes. The modulation
+// coefficients a = gamma * (1 + scale) and shift of up to two CFG batches sit in a shared-memory table;
+// rows of other batches (packed variable-length inputs) read them from global memory.
+// Latency structure (a warp sees only ~7 rows at the medium shape, so nothing reaches a steady state
+// unless loads are issued early): the first row of every warp is requested before the table is built,
+// the table loads are all issued before any is used, and with DB the next row is loaded while the
+// current one is normalised (2 rows per warp, 16 warps per SM in flight).
 constexpr int NORM_D_THREADS = 256;
-template <int NV>  // float4s per lane: D = 128 * NV
-__global__ void __launch_bounds__(NORM_D_THREADS, 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+constexpr int NORM_D_TAB_IT = 4;  // table float4s per thread: tab_batches * D / 4 <= 4 * 256 (D <= 2048)
+
+// L2 eviction policy of the row loads: the max|y| pass keeps the rows it reads (evict_last) for the
+// write pass that follows, which reads them for the last time (evict_first).
+__device__ __forceinline__ uint64_t norm_l2_policy(int mode) {
+  uint64_t pol;
+  if (mode == SA3_NORM_AMAX)
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ float4 ld_f4_hint(const float4* ptr, uint64_t pol) {
+  float4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(ptr), "l"(pol));
+  return v;
+}
+template <int NV>
+__device__ __forceinline__ void norm_load_row4(const NormParams& p, int row, int lane, uint64_t pol, float4 (&v)[NV]) {
+  const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (long long)row * p.ldx);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = ld_f4_hint(xr + lane + 32 * k, pol);
+}
+
+template <int NV, bool DB>  // NV float4s per lane: D = 128 * NV; DB: next row prefetched
+__global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+  grid_dep_wait();
   extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int idx = threadIdx.x; idx < tab_batches * p.D; idx += blockDim.x) {
-    const int b = idx / p.D, j = idx - b * p.D;
-    const float g = p.gamma ? __ldg(p.gamma + j) : 1.f;
-    if (p.mod) {
-      ntab[(2 * b) * p.D + j] = g * (1.f + __ldg(p.mod + (long long)b * p.ld_mod + p.scale_off + j));
-      ntab[(2 * b + 1) * p.D + j] = __ldg(p.mod + (long long)b * p.ld_mod + p.shift_off + j);
-    } else {
-      ntab[(2 * b) * p.D + j] = g;
-      ntab[(2 * b + 1) * p.D + j] = 0.f;
+  const int nw = gridDim.x * (NORM_D_THREADS / 32);
+  int li = blockIdx.x * (NORM_D_THREADS / 32) + warp;
+  const uint64_t pol = norm_l2_policy(p.mode);
+  float4 v[NV];
+  if (li < p.rows) norm_load_row4<NV>(p, norm_row(p, li), lane, pol, v);
+  {
+    const int D4 = p.D >> 2, n4 = tab_batches * D4;
+    float4 ta[NORM_D_TAB_IT], ts[NORM_D_TAB_IT];
+#pragma unroll
+    for (int it = 0; it < NORM_D_TAB_IT; ++it) {
+      const int idx = threadIdx.x + it * NORM_D_THREADS;
+      if (idx < n4) {
+        const int b = idx / D4, e = 4 * (idx - b * D4);
+        const float4 g = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + e)) : make_float4(1.f, 1.f, 1.f, 1.f);
+        if (p.mod) {
+          const float4 sc = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.scale_off + e));
+          ts[it] = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.shift_off + e));
+          ta[it] = make_float4(g.x * (1.f + sc.x), g.y * (1.f + sc.y), g.z * (1.f + sc.z), g.w * (1.f + sc.w));
+        } else {
+          ta[it] = g;
+          ts[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < NORM_D_TAB_IT; ++it) {
+      const int idx = threadIdx.x + it * NORM_D_THREADS;
+      if (idx < n4) {
+        const int b = idx / D4, e = 4 * (idx - b * D4);
+        *reinterpret_cast<float4*>(ntab + (2 * b) * p.D + e) = ta[it];
+        *reinterpret_cast<float4*>(ntab + (2 * b + 1) * p.D + e) = ts[it];
+      }
     }
   }
   __syncthreads();
@@ -248,13 +302,11 @@ __global__ void __launch_bounds__(NORM_D_THREADS, 3) rmsnorm_direct_kernel(NormP
     if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
   }
   float amax = 0.f;
-  const int nw = gridDim.x * (NORM_D_THREADS / 32);
-  for (int li = blockIdx.x * (NORM_D_THREADS / 32) + warp; li < p.rows; li += nw) {
+  while (li < p.rows) {
     const int row = norm_row(p, li);
-    const float4* xr = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + (long long)row * p.ldx);
-    float4 v[NV];
-#pragma unroll
-    for (int k = 0; k < NV; ++k) v[k] = xr[lane + 32 * k];
+    const int nli = li + nw;
+    float4 nv[DB ? NV : 1];
+    if (DB && nli < p.rows) norm_load_row4<DB ? NV : 1>(p, norm_row(p, nli), lane, pol, nv);
     float ss4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -296,6 +348,13 @@ __global__ void __launch_bounds__(NORM_D_THREADS, 3) rmsnorm_direct_kernel(NormP
             make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
       }
     }
+    if (DB) {
+#pragma unroll
+      for (int k = 0; k < NV; ++k) v[k] = nv[DB ? k : 0];
+    } else if (nli < p.rows) {
+      norm_load_row4<NV>(p, norm_row(p, nli), lane, pol, v);
+    }
+    li = nli;
   }
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
@@ -308,6 +367,7 @@ constexpr int NORM_BULK_THREADS = 160;
 
 template <int MAXC, bool VEC>
 __global__ void __launch_bounds__(NORM_BULK_THREADS, 2) rmsnorm_bulk_kernel(NormParams p, int rowbytes) {
+  grid_dep_wait();
   extern __shared__ __align__(16) uint8_t nsm[];
   uint64_t* full = reinterpret_cast<uint64_t*>(nsm + NORM_RING * rowbytes);
   uint64_t* empty = full + NORM_RING;
@@ -461,6 +521,7 @@ struct QuantParams {
 // (row, chunk) position advances by a precomputed (row, chunk) step instead of a division.
 constexpr int QUANT_INFLIGHT = 8;
 __global__ void __launch_bounds__(256, 3) quantize_e4m3_kernel(QuantParams p) {
+  grid_dep_wait();
   const int cpr = p.cols / 8;  // 8-element chunks per row
   const long long total = (long long)p.rows * cpr;
   float s = 1.f;
@@ -530,6 +591,7 @@ struct QkParams {
 
 // Eight lanes per 64-wide head, 8 elements per lane; a warp handles 4 heads.
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(QkParams p) {
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int sub = lane & 7;
   const int per_row = p.ngroups * p.heads;
@@ -603,6 +665,7 @@ struct ConvParams {
 };
 
 __global__ void __launch_bounds__(256) convert_kernel(ConvParams p) {
+  grid_dep_wait();
   const int cpr = p.cols / 8;
   const long long total = (long long)p.rows * cpr;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -698,17 +761,17 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
                                : 0;
     const int smem = tab_batches * 2 * D * 4;
     int gridd = (rows + 7) / 8;
-    if (gridd > 148 * 3) gridd = 148 * 3;
     int rc;
-#define SA3_NORM_DIRECT(V)                                                               \
-  case V:                                                                                \
-    if ((rc = ensure_smem(rmsnorm_direct_kernel<V>, 2 * 2 * 4096 * 4))) return rc;       \
-    rmsnorm_direct_kernel<V><<<gridd, NORM_D_THREADS, smem, st>>>(p, tab_batches);        \
+#define SA3_NORM_DIRECT(V, DB)                                                                              \
+  case V:                                                                                                   \
+    if (gridd > 148 * ((DB || V > 12) ? 2 : 3)) gridd = 148 * ((DB || V > 12) ? 2 : 3);                     \
+    if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB>, 2 * 2 * 2048 * 4))) return rc;                      \
+    launch_ex(rmsnorm_direct_kernel<V, DB>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
     break;
     switch (D / 128) {
-      SA3_NORM_DIRECT(8)
-      SA3_NORM_DIRECT(12)
-      SA3_NORM_DIRECT(16)
+      SA3_NORM_DIRECT(8, true)
+      SA3_NORM_DIRECT(12, true)
+      SA3_NORM_DIRECT(16, false)
       default:
         goto bulk_path;
     }
@@ -724,10 +787,10 @@ bulk_path:
 #define SA3_NORM_BULK(C)                                                                             \
   if (vec) {                                                                                         \
     if ((rc = ensure_smem(rmsnorm_bulk_kernel<C, true>, 96 * 1024 + 256))) return rc;                \
-    rmsnorm_bulk_kernel<C, true><<<gridb, NORM_BULK_THREADS, smem, st>>>(p, rowbytes);               \
+    launch_ex(rmsnorm_bulk_kernel<C, true>, dim3(gridb), dim3(NORM_BULK_THREADS), smem, st, 1, p, rowbytes);               \
   } else {                                                                                           \
     if ((rc = ensure_smem(rmsnorm_bulk_kernel<C, false>, 96 * 1024 + 256))) return rc;               \
-    rmsnorm_bulk_kernel<C, false><<<gridb, NORM_BULK_THREADS, smem, st>>>(p, rowbytes);              \
+    launch_ex(rmsnorm_bulk_kernel<C, false>, dim3(gridb), dim3(NORM_BULK_THREADS), smem, st, 1, p, rowbytes);              \
   }
     int rc;
     if (nchunk <= 32 * 4) {
@@ -742,9 +805,9 @@ bulk_path:
   }
 #define SA3_NORM_LAUNCH(C)                                      \
   if (vec)                                                      \
-    rmsnorm_modulate_kernel<C, true><<<grid, 128, 0, st>>>(p);  \
+    launch_ex(rmsnorm_modulate_kernel<C, true>, dim3(grid), dim3(128), 0, st, 1, p);  \
   else                                                          \
-    rmsnorm_modulate_kernel<C, false><<<grid, 128, 0, st>>>(p);
+    launch_ex(rmsnorm_modulate_kernel<C, false>, dim3(grid), dim3(128), 0, st, 1, p);
   if (nchunk <= 32 * 4) {
     SA3_NORM_LAUNCH(4)
   } else if (nchunk <= 32 * 6) {
@@ -774,7 +837,7 @@ extern "C" int sa3_quantize_e4m3(const void* x, void* out, int rows, int cols, l
   long long qgrid = ((long long)rows * (cols / 8) + 1023) / 1024;
   if (qgrid > 148 * 3) qgrid = 148 * 3;
   if (qgrid < 1) qgrid = 1;
-  quantize_e4m3_kernel<<<(int)qgrid, 256, 0, st>>>(p);
+  launch_ex(quantize_e4m3_kernel, dim3((int)qgrid), dim3(256), 0, st, 1, p);
   return launch_status();
 }
 
@@ -806,7 +869,7 @@ extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, in
   p.row_pos = row_pos;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const long long items = (long long)rows * ngroups * heads;
-  qk_norm_rope_kernel<<<grid_for(items, 32), 256, 0, st>>>(p);
+  launch_ex(qk_norm_rope_kernel, dim3(grid_for(items, 32)), dim3(256), 0, st, 1, p);
   return launch_status();
 }
 
@@ -817,6 +880,6 @@ extern "C" int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype,
     return SA3_ERR_DTYPE;
   if (!aligned16(x) || !aligned16(out) || (ldx % 8) || (ldo % 8)) return SA3_ERR_ALIGN;
   ConvParams p{x, out, src_rows, x_dtype == SA3_DT_F32, out_dtype == SA3_DT_F32, rows, cols, ldx, ldo};
-  convert_kernel<<<grid_for((long long)rows * (cols / 8), 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  launch_ex(convert_kernel, dim3(grid_for((long long)rows * (cols / 8), 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, p);
   return launch_status();
 }

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <mutex>
 #include <set>
@@ -53,6 +54,44 @@ inline int launch_status() {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Programmatic dependent launch for the hot kernels (every one of them calls grid_dep_wait()
+// before touching global memory). SA3_PDL=0 in the environment turns it off.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SA3_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialisation and, for cluster > 1, a 1-D cluster.
+template <typename... KArgs, typename... Args>
+inline int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? SA3_OK : SA3_ERR_LAUNCH;
+}
 
 // Raise the dynamic shared-memory limit of `func` once per device, so later
 // calls (including those made during CUDA-graph stream capture) only launch.

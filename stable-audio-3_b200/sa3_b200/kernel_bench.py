@@ -6,6 +6,7 @@ bounded workload for ncu captures of a single kernel.
 Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
   ff1_fp8    GLU.proj    FP8 GEMM  M x 12288 x 1536, SwiGLU epilogue
   qkv_fp8    to_qkv      FP8 GEMM  M x 7680 x 1536
+  qkv_fp8_qk to_qkv as in the block: qk RMSNorm + RoPE epilogue
   ff2_fp8    linear_out  FP8 GEMM  M x 1536 x 6144, gate + fp32 residual epilogue
   out_fp8    to_out      FP8 GEMM  M x 1536 x 1536, gate + fp32 residual epilogue
   attn_diff  differential SWA, 24 heads, window (256, 256)
@@ -53,8 +54,8 @@ def case(name: str, iters: int) -> dict:
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(0)
     one = torch.ones(1, device=dev)
-    if name in ("ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8"):
-        n, k = {"ff1_fp8": (12288, 1536), "qkv_fp8": (7680, 1536), "ff2_fp8": (1536, 6144),
+    if name in ("ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8"):
+        n, k = {"ff1_fp8": (12288, 1536), "qkv_fp8": (7680, 1536), "qkv_fp8_qk": (7680, 1536), "ff2_fp8": (1536, 6144),
                 "out_fp8": (1536, 1536)}[name]
         a = torch.randn(M, k, device=dev).to(torch.float8_e4m3fn)
         wq, s = _fp8_weight(n, k, dev, g)
@@ -68,6 +69,15 @@ def case(name: str, iters: int) -> dict:
         elif name == "qkv_fp8":
             out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
             fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s)  # noqa: E731
+        elif name == "qkv_fp8_qk":
+            # as in the DiT block: qk RMSNorm + RoPE of q | k | v | q_diff | k_diff in the epilogue
+            out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
+            gq, gk = torch.rand(64, device=dev) + 0.5, torch.rand(64, device=dev) + 0.5
+            cs = ops.rope_table(N, device=dev)
+            pos = (torch.arange(M, device=dev) % N).to(torch.int32)
+            qk = dict(gammas=[gq, gk, None, gq, gk], group_width=D, rope=[True, True, False, True, True], eps=1e-6,
+                      cos_sin=cs, row_pos=pos)
+            fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s, kind=_lib.EPI_QK_NORM, qk=qk)  # noqa: E731
         else:
             h = torch.randn(M, n, device=dev)
             gate = torch.randn(B, n, device=dev)
@@ -158,7 +168,7 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq"]
+CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq"]
 
 
 def main():
