@@ -37,7 +37,8 @@ struct GemmParams {
   const float* a_scale;
   const float* b_scale;
   sa3_epilogue epi;
-  int tma_store;  // bf16 output through shared memory and TMA stores (no output-row remap)
+  int tma_store;  // 1: bf16 output through shared memory and TMA stores (no output-row remap);
+                  // 2: fp32 residual in and result out through TMA; 3: in-place fp32 residual by TMA reduce-add
 };
 
 // bf16 output chunks of 32 rows x 32 columns go out through a per-warp double buffer in shared
@@ -46,6 +47,14 @@ struct GemmParams {
 // that last read it has finished reading (bulk-group wait).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+// Element-wise add of a shared-memory box into global memory, performed at L2 (fp32 add, rounded to
+// nearest even); the box is read from shared memory asynchronously like a TMA store.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(m)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
@@ -65,6 +74,7 @@ struct StoreStage {
   int next;                // bf16: buffer to fill next
   int uses;                // residual: chunks loaded so far (barrier phase)
   int pending;             // residual: loads issued and not yet consumed
+  int red;                 // in-place residual kinds: the result is added into C by TMA reduce-add
 };
 
 // This thread's row of the chunk (v, columns col..col+31 of output row row0 + lane) -> bf16 -> TMA.
@@ -516,17 +526,24 @@ __device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (
   for (int i = 0; i < 8; ++i)
     if (g == i) gam = e.qk_gamma[i];
   if (gam) {
-    float ss = 0.f;
+    // both gamma halves are requested before the reduction; the sum of squares runs as 4 chains
+    float g_lo[32], g_hi[32];
+    ldg_f32x32(gam, g_lo);
+    ldg_f32x32(gam + 32, g_hi);
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], fmaf(w[i], w[i], ss));
-    const float r = rsqrtf(ss * (1.f / 64.f) + e.qk_eps);
-    float gv[32];
-    ldg_f32x32(gam, gv);
+    for (int i = 0; i < 32; i += 2) {
+      s4[0] = fmaf(v[i], v[i], s4[0]);
+      s4[1] = fmaf(v[i + 1], v[i + 1], s4[1]);
+      s4[2] = fmaf(w[i], w[i], s4[2]);
+      s4[3] = fmaf(w[i + 1], w[i + 1], s4[3]);
+    }
+    const float r = rsqrtf(((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 64.f) + e.qk_eps);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] *= r * gv[i];
-    ldg_f32x32(gam + 32, gv);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) w[i] *= r * gv[i];
+    for (int i = 0; i < 32; ++i) {
+      v[i] *= r * g_lo[i];
+      w[i] *= r * g_hi[i];
+    }
   }
 }
 
@@ -609,6 +626,45 @@ __device__ __forceinline__ void residual_tma_chunk(StoreStage& st, const GemmPar
     }
   }
   st.uses++;
+}
+
+// In-place residual kinds (C is the residual): this warp's 32 rows x 32 columns of the branch output
+// t = v (residual) or v * sigmoid(1 - gate[rb]) (gated) go through the two 2 KB buffers, in the 64-byte
+// swizzle of the 16 x 32 fp32 box, and are added into C by two TMA reduce-adds. The stream is never
+// loaded into the SM. A buffer is rewritten only after the reduce that last read it has read it.
+template <int KIND>
+__device__ __forceinline__ void residual_reduce_chunk(StoreStage& st, const GemmParams& p, int nc, int row0, int rb,
+                                                      float (&v)[32]) {
+  const sa3_epilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+  if (row0 >= p.M) return;  // warp-uniform: no valid row
+  if (KIND == SA3_EPI_GATED_RESIDUAL) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(e.gate + (long long)rb * e.ld_gate + nc + 4 * c));
+      v[4 * c] *= fast_sigmoid(1.f - g.x);
+      v[4 * c + 1] *= fast_sigmoid(1.f - g.y);
+      v[4 * c + 2] *= fast_sigmoid(1.f - g.z);
+      v[4 * c + 3] *= fast_sigmoid(1.f - g.w);
+    }
+  }
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (lane == 0) bulk_wait_read_all_but_one();
+    __syncwarp();
+    uint8_t* rowp = st.buf + h * 2048 + lane * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<float4*>(rowp + ((c ^ sw) * 16)) =
+          make_float4(v[16 * h + 4 * c], v[16 * h + 4 * c + 1], v[16 * h + 4 * c + 2], v[16 * h + 4 * c + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_reduce_add_2d(st.tm, st.buf + h * 2048, nc + 16 * h, row0);
+      bulk_commit_group();
+    }
+  }
 }
 
 // Residual epilogues into the fp32 stream, transposed through a per-warp shared-memory scratch of
@@ -698,6 +754,22 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
                                                  StoreStage* stg = nullptr, const float (*cs_pre)[32] = nullptr) {
   const sa3_epilogue& e = p.epi;
   const int lane = threadIdx.x & 31;
+  if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && stg && stg->red) {
+    const uint32_t trow = tmem_tile + ((uint32_t)(q * 32) << 16);
+    const int m = m0 + q * 32 + lane;
+    int rb = 0;
+    if (KIND == SA3_EPI_GATED_RESIDUAL && m < p.M) rb = e.row_batch ? __ldg(e.row_batch + m) : m / e.rows_per_batch;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      const int nc = n0 + half * 128 + c * 32;
+      if (nc >= p.N) break;  // uniform per warp
+      float v[32];
+      tmem_ld32(trow + half * 128 + c * 32, v);
+      scale_bias32(v, nc, sa, p.b_scale, e.bias);
+      residual_reduce_chunk<KIND>(*stg, p, nc, m0 + q * 32, rb, v);
+    }
+    return;
+  }
   if ((KIND == SA3_EPI_GATED_RESIDUAL || KIND == SA3_EPI_RESIDUAL) && stg && stg->tmr) {
     const uint32_t trow = tmem_tile + ((uint32_t)(q * 32) << 16);
     const int m = m0 + q * 32 + lane;
@@ -904,7 +976,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
     uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
-                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0};
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -1139,7 +1211,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
     uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
-                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0};
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -1578,10 +1650,14 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
     if ((rc = make_tmap_2d(&tmC, C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 16, 32,
                            CU_TENSOR_MAP_SWIZZLE_64B)))
       return rc;
-    if ((rc = make_tmap_2d(&tmR, e.residual, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)M,
-                           (uint64_t)e.ld_residual, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
-      return rc;
-    p.tma_store = 2;
+    if (e.residual == C && e.ld_residual == ldc && !e.amax_out && sa3_residual_reduce_enabled()) {
+      p.tma_store = 3;  // in place and nothing needs the updated values: reduce-add into C
+    } else {
+      if ((rc = make_tmap_2d(&tmR, e.residual, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)N, (uint64_t)M,
+                             (uint64_t)e.ld_residual, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return rc;
+      p.tma_store = 2;
+    }
   }
   if (fast && M >= SA3_PAIR_MIN_ROWS) {
     // enough rows for 256-row tiles: the 2-SM kernel (FP8 or bf16). Its A and B boxes are 128 rows.

@@ -65,6 +65,17 @@ inline bool pdl_enabled() {
   return on;
 }
 
+// In-place fp32 residual GEMM epilogues add their result into C with TMA reduce-add (L2 does the
+// read-modify-write) instead of loading the residual through the SM. SA3_RESIDUAL_REDUCE=0 selects
+// the load / combine / store path.
+inline bool sa3_residual_reduce_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SA3_RESIDUAL_REDUCE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // cudaLaunchKernelEx with programmatic stream serialisation and, for cluster > 1, a 1-D cluster.
 template <typename... KArgs, typename... Args>
 inline int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster,

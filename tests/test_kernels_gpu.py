@@ -75,10 +75,13 @@ def test_gemm_fp8_matches_quantized_definition(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("M", [600, 777, 1030])
-@pytest.mark.parametrize("kind", ["store", "swiglu", "gated_residual_f32", "residual_f32"])
+@pytest.mark.parametrize("kind", ["store", "swiglu", "gated_residual_f32", "residual_f32", "gated_residual_f32_oop",
+                                  "residual_f32_oop"])
 def test_gemm_fp8_pair_epilogues(cuda, M, kind):
     """FP8 GEMMs with M >= 512 run on the 2-SM (CTA pair, 256 x 256 tile) kernel. Every epilogue kind
-    against the FP8 definition, with M leaving the last pair tile partly or wholly empty for one CTA."""
+    against the FP8 definition, with M leaving the last pair tile partly or wholly empty for one CTA.
+    In-place fp32 residuals (C is the residual) are added by TMA reduce-add; out-of-place ones (_oop)
+    load the residual and store the result through TMA."""
     from sa3_b200 import ops, _lib
 
     g = _gen(M + len(kind))
@@ -107,15 +110,19 @@ def test_gemm_fp8_pair_epilogues(cuda, M, kind):
     else:
         res = torch.randn(M, N, generator=g)
         gate = torch.randn(B, N, generator=g)
-        out = res.clone().to(cuda)
-        if kind == "gated_residual_f32":
-            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_GATED_RESIDUAL, residual=out,
+        oop = kind.endswith("_oop")
+        out = torch.full((M, N), float("nan"), device=cuda) if oop else res.clone().to(cuda)
+        resd = res.to(cuda) if oop else out
+        if kind.startswith("gated_residual_f32"):
+            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_GATED_RESIDUAL, residual=resd,
                      gate=gate.to(cuda), rows_per_batch=rows_per_batch)
             bidx = torch.arange(M) // rows_per_batch
             ref = res + h * torch.sigmoid(1 - gate[bidx])
         else:
-            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_RESIDUAL, residual=out)
+            ops.gemm(xq, wd, out, a_scale=s, b_scale=swd, bias=bd, kind=_lib.EPI_RESIDUAL, residual=resd)
             ref = res + h
+        if oop:
+            assert torch.equal(resd.cpu(), res)
     torch.cuda.synchronize()
     assert rel_fro(out, ref) < 5e-3
     assert _lib.device_error() == 0
