@@ -105,6 +105,12 @@ typedef struct {
   /* optional int32 [M]: output (and residual) row of GEMM row m; overrides seg_*. Packs variable-length
      sequences (project_in, the local-conditioning add) into the token-row stream. */
   const int* out_row_map;
+  /* SA3_EPI_QK_NORM with more than 8 groups (the cross-attention K/V projections of every block in one
+     GEMM): when qk_gamma_table is non-NULL it replaces qk_gamma. Groups g < qk_table_groups are
+     RMS-normalised with the 64 fp32 at qk_gamma_table + 64 g (16-byte aligned); later groups are left as
+     is. qk_rope_mask must be 0 in this mode. Zero-initialised callers get the 8-group behaviour. */
+  const float* qk_gamma_table;
+  int qk_table_groups;
 } sa3_epilogue;
 
 int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,

@@ -506,11 +506,14 @@ __device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int o
 
 // RMSNorm over one 64-column head (v = dims 0..31, w = dims 32..63) with its group's gamma, then
 // rotate_half RoPE on dims 0..31 (pairs i, i+16) at this row's position; fp32 throughout.
+// Rotary embedding on for column group g (at most 8 groups carry it; table mode has none).
+__device__ __forceinline__ bool qk_rope_on(const sa3_epilogue& e, int g) { return g < 8 && ((e.qk_rope_mask >> g) & 1u); }
+
 // RoPE cos/sin row of output row m (clamped into [0, M) for the padding rows of the last tile) for the
 // 64-column head at nc, loaded before the tile's accumulator is ready. Leaves cs untouched when the
 // head's group has no rotary embedding.
 __device__ __forceinline__ void qk_rope_prefetch(const sa3_epilogue& e, int m, int M, int nc, int N, float (&cs)[32]) {
-  if (nc >= N || !((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u)) return;
+  if (nc >= N || !qk_rope_on(e, nc / e.qk_group_width)) return;
   m = m < M ? m : M - 1;
   int pos = e.row_pos ? __ldg(e.row_pos + m) : (e.rows_per_batch > 0 ? m % e.rows_per_batch : 0);
   if (pos >= e.max_pos) pos = e.max_pos - 1;
@@ -522,9 +525,13 @@ __device__ __forceinline__ void qk_rope_prefetch(const sa3_epilogue& e, int m, i
 __device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (&v)[32], float (&w)[32]) {
   const int g = nc / e.qk_group_width;
   const float* gam = nullptr;
+  if (e.qk_gamma_table) {
+    if (g < e.qk_table_groups) gam = e.qk_gamma_table + 64 * g;
+  } else {
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    if (g == i) gam = e.qk_gamma[i];
+    for (int i = 0; i < 8; ++i)
+      if (g == i) gam = e.qk_gamma[i];
+  }
   if (gam) {
     // both gamma halves are requested before the reduction; the sum of squares runs as 4 chains
     float g_lo[32], g_hi[32];
@@ -550,7 +557,7 @@ __device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (
 // Rotary embedding of dims 0..31 of the head (pairs i, i + 16) with the cos/sin row cs, when the
 // head's group has one.
 __device__ __forceinline__ void qk_rope64(const sa3_epilogue& e, int nc, const float (&cs)[32], float (&v)[32]) {
-  if ((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u) {
+  if (qk_rope_on(e, nc / e.qk_group_width)) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float a = v[i], b = v[i + 16];
@@ -829,7 +836,7 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           qk_norm64(e, nc, v, w);
           if (CS_PRE) {
             qk_rope64(e, nc, *cs_pre, v);
-          } else if ((e.qk_rope_mask >> (nc / e.qk_group_width)) & 1u) {
+          } else if (qk_rope_on(e, nc / e.qk_group_width)) {
             float cs[32];  // the kernels with fewer registers per thread load it per head
             qk_rope_prefetch(e, m, p.M, nc, p.N, cs);
             qk_rope64(e, nc, cs, v);
@@ -1585,7 +1592,13 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   if (epi) e = *epi;
   if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_QK_NORM) return SA3_ERR_ARG;
   if (e.kind == SA3_EPI_QK_NORM) {
-    if (e.qk_group_width <= 0 || e.qk_group_width % 64 || N > 8 * e.qk_group_width) return SA3_ERR_ARG;
+    if (e.qk_group_width <= 0 || e.qk_group_width % 64) return SA3_ERR_ARG;
+    if (e.qk_gamma_table) {
+      if (e.qk_table_groups <= 0 || e.qk_rope_mask) return SA3_ERR_ARG;
+      if (!aligned16(e.qk_gamma_table)) return SA3_ERR_ALIGN;
+    } else if (N > 8 * e.qk_group_width) {
+      return SA3_ERR_ARG;
+    }
     for (int g = 0; g < 8; ++g)
       if (e.qk_gamma[g] && !aligned16(e.qk_gamma[g])) return SA3_ERR_ALIGN;
     if (e.qk_rope_mask && (!e.cos_sin || !aligned16(e.cos_sin) || e.max_pos <= 0 ||

@@ -256,6 +256,13 @@ __device__ __forceinline__ void norm_load_row4(const NormParams& p, int row, int
   for (int k = 0; k < NV; ++k) v[k] = ld_f4_hint(xr + lane + 32 * k, pol);
 }
 
+// CFG batch of a row for the modulation table (every lane reads the same entry: one transaction).
+__device__ __forceinline__ int norm_batch_load(const NormParams& p, int row) {
+  if (!p.mod) return 0;
+  if (!p.row_batch) return row / p.rows_per_batch;
+  return __ldg(p.row_batch + row);
+}
+
 template <int NV, bool DB>  // NV float4s per lane: D = 128 * NV; DB: next row prefetched
 __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
   grid_dep_wait();
@@ -265,7 +272,11 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
   int li = blockIdx.x * (NORM_D_THREADS / 32) + warp;
   const uint64_t pol = norm_l2_policy(p.mode);
   float4 v[NV];
-  if (li < p.rows) norm_load_row4<NV>(p, norm_row(p, li), lane, pol, v);
+  int vb = 0;  // CFG batch of the row in v, requested with the row so its latency overlaps the row's
+  if (li < p.rows) {
+    vb = norm_batch_load(p, norm_row(p, li));
+    norm_load_row4<NV>(p, norm_row(p, li), lane, pol, v);
+  }
   {
     const int D4 = p.D >> 2, n4 = tab_batches * D4;
     float4 ta[NORM_D_TAB_IT], ts[NORM_D_TAB_IT];
@@ -306,7 +317,11 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
     const int row = norm_row(p, li);
     const int nli = li + nw;
     float4 nv[DB ? NV : 1];
-    if (DB && nli < p.rows) norm_load_row4<DB ? NV : 1>(p, norm_row(p, nli), lane, pol, nv);
+    int nvb = 0;
+    if (DB && nli < p.rows) {
+      nvb = norm_batch_load(p, norm_row(p, nli));
+      norm_load_row4<DB ? NV : 1>(p, norm_row(p, nli), lane, pol, nv);
+    }
     float ss4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -316,7 +331,7 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
       ss4[3] = fmaf(v[k].w, v[k].w, ss4[3]);
     }
     const float r = rsqrtf(warp_sum((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / (float)p.D + p.eps);
-    const int b = p.mod ? (p.row_batch ? __ldg(p.row_batch + row) : row / p.rows_per_batch) : 0;
+    const int b = vb;
     const bool in_tab = b < tab_batches;  // warp-uniform
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
@@ -351,7 +366,9 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
     if (DB) {
 #pragma unroll
       for (int k = 0; k < NV; ++k) v[k] = nv[DB ? k : 0];
+      vb = nvb;
     } else if (nli < p.rows) {
+      vb = norm_batch_load(p, norm_row(p, nli));
       norm_load_row4<NV>(p, norm_row(p, nli), lane, pol, v);
     }
     li = nli;

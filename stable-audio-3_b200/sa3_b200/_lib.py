@@ -56,6 +56,8 @@ class Epilogue(ctypes.Structure):
         ("max_pos", c_int),
         ("row_pos", c_vp),
         ("out_row_map", c_vp),
+        ("qk_gamma_table", c_vp),
+        ("qk_table_groups", c_int),
     ]
 
 

@@ -109,6 +109,9 @@ class _Workspace:
         self.o8 = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.qx = torch.empty(M, (2 if cfg.differential else 1) * D, device=dev, dtype=bf)
         self.kv = torch.empty(max(B * Tc, 1), (3 if cfg.differential else 2) * D, device=dev, dtype=bf)
+        # every block's cross-attention K/V, computed once per forward
+        self.kv_all = torch.empty(max(B * Tc, 1), cfg.depth * (3 if cfg.differential else 2) * D, device=dev,
+                                  dtype=bf) if Tc else None
         self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
         self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.t1 = torch.empty(R, D, device=dev, dtype=bf)
@@ -164,6 +167,32 @@ class DiTEngine:
         ramp = torch.linspace(0, 1, cfg.timestep_features_dim // 2, dtype=torch.float32)
         self.t_freqs = torch.exp(ramp * (math.log(10000.0) - math.log(0.5)) + math.log(0.5)).to(self.dev)
         self.gptq_k = max([ln.gptq["k"] for ln in self.lin.values() if ln.gptq is not None], default=0)
+        self._prep_kv_all()
+
+    def _prep_kv_all(self):
+        """The cross-attention K/V projections of all blocks as one linear (the context is the same for every
+        block, so one GEMM per step replaces one small GEMM per block). Output columns are grouped
+        [k_0 | k'_0 | ... | k_{L-1} | k'_{L-1} | v_0 | ... | v_{L-1}] (k' only when differential); the k groups
+        are k-normalised with their block's gamma from a table, the v groups are stored as computed."""
+        cfg = self.cfg
+        D, L = cfg.embed_dim, cfg.depth
+        names = [f"transformer.layers.{i}.cross_attn.to_kv" for i in range(L)]
+        self.kv_all = None
+        if not all(n in self.lin and self.lin[n].gptq is None for n in names):
+            return
+        lins = [self.lin[n] for n in names]
+        nk = 2 if cfg.differential else 1
+        order = [(i, j) for i in range(L) for j in range(nk)] + [(i, nk) for i in range(L)]
+        w = torch.cat([lins[i].w[j * D:(j + 1) * D] for i, j in order]).contiguous()
+        scale = torch.cat([lins[i].scale[j * D:(j + 1) * D] for i, j in order]).contiguous() if lins[0].fp8 else None
+        bias = None
+        if any(ln.bias is not None for ln in lins):
+            bias = torch.cat([(lins[i].bias[j * D:(j + 1) * D] if lins[i].bias is not None
+                               else torch.zeros(D, device=self.dev)) for i, j in order]).contiguous()
+        gk = [self.gam[f"transformer.layers.{i}.cross_attn.k_norm.gamma"] for i in range(L)]
+        self.kv_gamma = torch.stack([gk[i] for i in range(L) for _ in range(nk)]).float().contiguous()
+        self.kv_all = Lin(w, scale, bias, lins[0].fp8)
+        self.kv_nk = nk
 
     # ------------------------------------------------------------------ prep
     def _prep(self, name, w, b, quantized: bool) -> Lin:
@@ -356,6 +385,11 @@ class DiTEngine:
             slot = 8 * cfg.depth
             ops.absmax(ctx, ws.amax[slot:slot + 1])
             ctx_a, ctx_s = self._quant(ws, ctx, ws.ctx8, slot)
+        kv_all = None
+        if ctx is not None and self.kv_all is not None:
+            # every block's cross-attention K/V (with k-norm) in one GEMM
+            kv_all = self._gemm(ctx_a, self.kv_all, ws.kv_all, x_scale=ctx_s, kind=_lib.EPI_QK_NORM,
+                                qk=dict(gamma_table=self.kv_gamma, group_width=D, eps=cfg.qk_norm_eps))
 
         # ---- trunk input: project_in (preprocess conv folded) into each sequence's latent rows
         h = ws.h
@@ -400,15 +434,22 @@ class DiTEngine:
                 # to_q / to_kv with the qk RMSNorm fused into the epilogue (no RoPE on cross-attention)
                 self._gemm(c, ln[p + "cross_attn.to_q"], qx, x_scale=csc, kind=_lib.EPI_QK_NORM,
                            qk=dict(gammas=[gq, gq] if diff else [gq], group_width=D, eps=cfg.qk_norm_eps))
-                self._gemm(ctx_a, ln[p + "cross_attn.to_kv"], kv, x_scale=ctx_s, kind=_lib.EPI_QK_NORM,
-                           qk=dict(gammas=[gk, gk, None] if diff else [gk, None], group_width=D,
-                                   eps=cfg.qk_norm_eps))
+                if kv_all is not None:
+                    nk = self.kv_nk
+                    kc = [kv_all[:, (i * nk + j) * D:(i * nk + j + 1) * D] for j in range(nk)]
+                    vc = kv_all[:, (cfg.depth * nk + i) * D:(cfg.depth * nk + i + 1) * D]
+                else:
+                    self._gemm(ctx_a, ln[p + "cross_attn.to_kv"], kv, x_scale=ctx_s, kind=_lib.EPI_QK_NORM,
+                               qk=dict(gammas=[gk, gk, None] if diff else [gk, None], group_width=D,
+                                       eps=cfg.qk_norm_eps))
+                    kc = [kv[:, 0:D], kv[:, D:2 * D]] if diff else [kv[:, 0:D]]
+                    vc = kv[:, 2 * D:3 * D] if diff else kv[:, D:2 * D]
                 am = ws.amax[s0 + 3:s0 + 4] if self.fp8 else None
                 if diff:
-                    ops.attention(qx[:, 0:D], kv[:, 0:D], kv[:, 2 * D:3 * D], q2=qx[:, D:2 * D], k2=kv[:, D:2 * D],
-                                  heads=H, out=o, amax_out=am, **xseq)
+                    ops.attention(qx[:, 0:D], kc[0], vc, q2=qx[:, D:2 * D], k2=kc[1], heads=H, out=o, amax_out=am,
+                                  **xseq)
                 else:
-                    ops.attention(qx, kv[:, 0:D], kv[:, D:2 * D], heads=H, out=o, amax_out=am, **xseq)
+                    ops.attention(qx, kc[0], vc, heads=H, out=o, amax_out=am, **xseq)
                 oa, osc = self._quant(ws, o, ws.o8, s0 + 3)
                 self._gemm(oa, ln[p + "cross_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_RESIDUAL, residual=h)
             # -- local additive conditioning, left-padded over the memory tokens (transformer.py:978-994, 77-88)

@@ -76,10 +76,18 @@ def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, s
     epi.c_f32 = 1 if out.dtype == torch.float32 else 0
     epi.out_row_map = _ptr(out_row_map)
     if qk is not None:
-        gams = list(qk["gammas"])
-        _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"))
+        gams = list(qk.get("gammas", []))
+        _need_cuda(*[g for g in gams if g is not None], qk.get("cos_sin"), qk.get("row_pos"), qk.get("gamma_table"))
+        if len(gams) > 8:
+            raise RuntimeError("more than 8 qk groups: pass gamma_table")
         for i, gm in enumerate(gams):
             epi.qk_gamma[i] = _ptr(gm)
+        tab = qk.get("gamma_table")
+        if tab is not None:
+            if tab.dtype != torch.float32 or tab.dim() != 2 or tab.shape[1] != 64 or not tab.is_contiguous():
+                raise RuntimeError("gamma_table must be contiguous float32 [groups, 64]")
+            epi.qk_gamma_table = _ptr(tab)
+            epi.qk_table_groups = int(tab.shape[0])
         epi.qk_group_width = int(qk["group_width"])
         epi.qk_rope_mask = sum(1 << i for i, r in enumerate(qk.get("rope", [])) if r)
         epi.qk_eps = float(qk.get("eps", 1e-6))
@@ -96,7 +104,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     """out = epilogue(a @ b.T * a_scale * b_scale + bias); a [M,K], b [N,K] (K-major), bf16 or e4m3.
 
     qk (for kind EPI_QK_NORM): dict(gammas=[per column group: fp32 [64] or None], group_width=int,
-    rope=[bool per group], eps=float, cos_sin=fp32 [max_pos, 32] or None, row_pos=int32 [M] or None).
+    rope=[bool per group], eps=float, cos_sin=fp32 [max_pos, 32] or None, row_pos=int32 [M] or None),
+    or for more than 8 groups dict(gamma_table=fp32 [G, 64], group_width=int, eps=float): groups < G are
+    normalised with their table row, later groups are stored as computed (no rotary embedding).
     """
     _need_cuda(a, b, out, a_scale, b_scale, bias, residual, gate, row_batch, amax_out)
     if a.dtype != b.dtype:

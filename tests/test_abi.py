@@ -42,3 +42,27 @@ def test_host_side_argument_errors_need_no_gpu():
     assert lib.sa3_rmsnorm_modulate(None, 0, None, 0, 0, 0, 0, None, 1e-5, None, 0, 0, 0, 0, None, 0, 0, None,
                                     None, None, None) == -1
     assert lib.sa3_convert(None, 0, None, 0, 0, 0, 0, 0, None, None) == -1
+
+
+def test_epilogue_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of sa3_epilogue has the C compiler's size and field offsets."""
+    import shutil
+    import subprocess
+
+    import pytest
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f for f, _ in _lib.Epilogue._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "sa3b200.h"\nint main(void) {\n'
+                   '  printf("%zu\\n", sizeof(sa3_epilogue));\n'
+                   + "".join(f'  printf("%zu\\n", offsetof(sa3_epilogue, {f}));\n' for f in fields)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_lib.Epilogue)
+    for f, off in zip(fields, out[1:]):
+        assert getattr(_lib.Epilogue, f).offset == off, f

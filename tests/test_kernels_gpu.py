@@ -436,3 +436,29 @@ def test_gemm_qk_norm_rope_epilogue(cuda, fp8):
         t = ref[:, :, part].permute(0, 2, 1, 3)
         ref[:, :, part] = orf.apply_rotary(orf.rms_norm(t, gm, 1e-6), freqs).permute(0, 2, 1, 3)
     assert max_rel(out.view(B, T, 5, H, 64), ref) < 1e-2
+
+
+@pytest.mark.parametrize("M", [256, 700])
+def test_gemm_qk_norm_gamma_table(cuda, M):
+    """qk-norm epilogue with a gamma table (more than 8 column groups, as for every block's cross-attention
+    K/V in one GEMM): groups below the table size are RMS-normalised per 64-column head with their row of
+    the table, later groups are stored as computed."""
+    from sa3_b200 import ops, _lib
+
+    g = _gen(M + 5)
+    K, gw, ngroups, ntab = 256, 128, 12, 9
+    N = gw * ngroups
+    a = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(N, K, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(N, generator=g) * 0.1
+    tab = torch.rand(ntab, 64, generator=g) + 0.5
+    y = a.float() @ w.float().T + bias
+    ref = y.clone()
+    for c in range(0, ntab * gw, 64):
+        hd = y[:, c:c + 64]
+        ref[:, c:c + 64] = hd * torch.rsqrt(hd.pow(2).mean(-1, keepdim=True) + 1e-6) * tab[c // gw]
+    out = ops.gemm(a.to(cuda), w.to(cuda), bias=bias.to(cuda), kind=_lib.EPI_QK_NORM,
+                   qk=dict(gamma_table=tab.to(cuda), group_width=gw, eps=1e-6))
+    torch.cuda.synchronize()
+    assert rel_fro(out[:, :ntab * gw], ref[:, :ntab * gw]) < 1e-2
+    assert rel_fro(out[:, ntab * gw:], ref[:, ntab * gw:]) < 1e-2
