@@ -43,6 +43,10 @@ from .quant import interleave_swiglu_rows, quantize_weight_e4m3, swiglu_interlea
 QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_kv",
                   "cross_attn.to_out", "ff.ff.0.proj", "ff.ff.2")
 
+# Byte budget of the batched first local-conditioning layer's output (every block's SiLU(W1 c + b1) for all
+# latent rows); larger packed batches compute it block by block.
+_LOCAL_ALL_MAX_BYTES = 4 << 30
+
 
 def _pad_cols(w: torch.Tensor, mult: int = 8) -> torch.Tensor:
     k = w.shape[1]
@@ -77,7 +81,7 @@ class _Workspace:
     row_batch (sequence of each row), row_pos (RoPE position), lat_rows (stream row of each latent row)
     and mem_rows (stream rows of the memory tokens)."""
 
-    def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0):
+    def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False):
         D = cfg.embed_dim
         nm = cfg.num_memory_tokens
         B = len(lengths)
@@ -115,6 +119,10 @@ class _Workspace:
         self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
         self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.t1 = torch.empty(R, D, device=dev, dtype=bf)
+        # every block's first local-conditioning layer, computed once per forward (within a byte budget)
+        self.t1_all = None
+        if local_all and R * cfg.depth * D * 2 <= _LOCAL_ALL_MAX_BYTES:
+            self.t1_all = torch.empty(R, cfg.depth * D, device=dev, dtype=bf)
         self.loc = torch.zeros(R, 264, device=dev, dtype=bf)
         self.xin = torch.empty(R, cfg.io_channels, device=dev, dtype=bf)
         self.hb = torch.empty(R, D, device=dev, dtype=bf)  # bf16 copy of the latent rows for project_out
@@ -168,6 +176,25 @@ class DiTEngine:
         self.t_freqs = torch.exp(ramp * (math.log(10000.0) - math.log(0.5)) + math.log(0.5)).to(self.dev)
         self.gptq_k = max([ln.gptq["k"] for ln in self.lin.values() if ln.gptq is not None], default=0)
         self._prep_kv_all()
+        self._prep_local_all()
+
+    def _prep_local_all(self):
+        """The first local-conditioning layer of all blocks as one linear: its input (the padded local
+        conditioning rows) is the same for every block, so one GEMM per forward replaces one per block."""
+        L = self.cfg.depth
+        names = [f"transformer.layers.{i}.to_local_embed.0" for i in range(L)]
+        self.loc1_all = None
+        if not all(n in self.lin and self.lin[n].gptq is None and not self.lin[n].fp8 for n in names):
+            return
+        lins = [self.lin[n] for n in names]
+        if any(ln.w.shape[0] != self.cfg.embed_dim for ln in lins):
+            return
+        w = torch.cat([ln.w for ln in lins]).contiguous()
+        bias = None
+        if any(ln.bias is not None for ln in lins):
+            bias = torch.cat([ln.bias if ln.bias is not None else torch.zeros(ln.w.shape[0], device=self.dev)
+                              for ln in lins]).contiguous()
+        self.loc1_all = Lin(w, None, bias, False)
 
     def _prep_kv_all(self):
         """The cross-attention K/V projections of all blocks as one linear (the context is the same for every
@@ -220,7 +247,8 @@ class DiTEngine:
         ws = self.ws
         if ws is None or (ws.lengths, ws.Tc) != (tuple(lengths), Tc):
             self.ws = ws = None
-            self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k)
+            self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k,
+                                      local_all=self.loc1_all is not None)
         if self.rope is None or self.rope.shape[0] < ws.max_n:
             self.rope = ops.rope_table(ws.max_n, 32, device=self.dev)
         return ws
@@ -385,6 +413,10 @@ class DiTEngine:
             slot = 8 * cfg.depth
             ops.absmax(ctx, ws.amax[slot:slot + 1])
             ctx_a, ctx_s = self._quant(ws, ctx, ws.ctx8, slot)
+        t1_all = None
+        if has_local and ws.t1_all is not None:
+            # every block's SiLU(W1 c + b1) of the local conditioning in one GEMM
+            t1_all = self._gemm(ws.loc, self.loc1_all, ws.t1_all, kind=_lib.EPI_SILU)
         kv_all = None
         if ctx is not None and self.kv_all is not None:
             # every block's cross-attention K/V (with k-norm) in one GEMM
@@ -454,8 +486,11 @@ class DiTEngine:
                 self._gemm(oa, ln[p + "cross_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_RESIDUAL, residual=h)
             # -- local additive conditioning, left-padded over the memory tokens (transformer.py:978-994, 77-88)
             if has_local and (p + "to_local_embed.0") in ln:
-                self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
-                self._gemm(ws.t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h,
+                if t1_all is not None:
+                    t1 = t1_all[:, i * D:(i + 1) * D]
+                else:
+                    t1 = self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
+                self._gemm(t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h,
                            out_row_map=ws.lat_rows)
             # -- feed-forward with adaLN (transformer.py:1042-1049)
             f, fsc = self._norm_to_a(ws, h, self.gam[p + "ff_norm.gamma"], s0 + 4, ssi, 3 * D, 4 * D)
