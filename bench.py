@@ -42,6 +42,9 @@ WORKLOADS = {
     # denoiser step over every prompt
     "dp_varlen_fp8": dict(model="medium", mode="fp8", dp=True, n_prompts=256, len_lo=108, len_hi=8183, Tc=128,
                           cfg_scale=7.0, apg_scale=1.0, max_tokens=1 << 18),
+    # one long sequence split over the ranks: L = 16384 (+64 memory tokens on rank 0), one CFG pair, contiguous
+    # token ranges per rank, +-256-row halos of q|k|v exchanged over NCCL before every self-attention
+    "seq_split_fp8": dict(model="medium", mode="fp8", seq_split=True, L=16384, Tc=128, cfg_scale=7.0, apg_scale=1.0),
     # small DiT in bf16 (24 blocks, dim 1024, L = 2584, CFG pair)
     "small_bf16": dict(model="small", mode="bf16", L=2584, prompts=1, Tc=128, cfg_scale=7.0, apg_scale=1.0),
 }
@@ -152,7 +155,7 @@ def model_cfg(name):
 
 def make_inputs(wl, cfg, seed, device):
     g = torch.Generator().manual_seed(seed)
-    P, L = wl["prompts"], wl["L"]
+    P, L = wl.get("prompts", 1), wl["L"]
     x = torch.randn(P, cfg.io_channels, L, generator=g)
     t = torch.full((P,), 0.5)
     cond = torch.randn(P, wl["Tc"], cfg.cond_token_dim, generator=g)
@@ -187,7 +190,7 @@ def cpu_block_sample(wl, threads: int, tokens: int = 0):
         dt = time.perf_counter() - t0
     # one step = depth blocks x (cond + uncond) sequences; the cross-attention / local-cond / prologue
     # work not in this sample is < 10% of a block and is left out (the figure is a lower bound on CPU time)
-    return dt * (N_full / N) * cfg.depth * 2 * wl["prompts"], dt
+    return dt * (N_full / N) * cfg.depth * 2 * wl.get("prompts", 1), dt
 
 
 def run_reference(args, wl, world, rank):
@@ -195,7 +198,7 @@ def run_reference(args, wl, world, rank):
     if rank != 0:
         return
     threads = len(os.sched_getaffinity(0))
-    tokens = 2 * wl["L"] * wl["prompts"]
+    tokens = 2 * wl["L"] * wl.get("prompts", 1)
     sample_tokens = 4096
     for _ in range(args.warmup):
         cpu_block_sample(wl, threads, sample_tokens)
@@ -211,7 +214,7 @@ def run_reference(args, wl, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "L": wl["L"], "prompts_per_gpu": wl["prompts"],
+        "config": {"workload": args.workload, "L": wl["L"], "prompts_per_gpu": wl.get("prompts", 1),
                    "parallelism": f"dp{world}"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -280,6 +283,58 @@ def run_dp_varlen(args, wl, world, rank, local):
         }), flush=True)
 
 
+def run_seq_split(args, wl, world, rank, local):
+    """One long sequence over all ranks (sa3_b200.seqsplit): per-layer halo exchange, all-reduced APG sums;
+    max-over-ranks device time of the whole forward (both CFG halves)."""
+    import torch.distributed as dist
+
+    from sa3_b200 import seqsplit as ss
+    from sa3_b200.modules import DiffusionTransformer, init_synthetic_
+
+    dev = torch.device("cuda", local)
+    cfg = model_cfg(wl["model"])
+    eng = init_synthetic_(DiffusionTransformer(cfg), seed=0).quantize(wl["mode"]).engine()
+    L = wl["L"]
+    sp = ss.make_split(L, rank, world, cfg.num_memory_tokens, cfg.sliding_window,
+                       group=dist.group.WORLD if world > 1 else None)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, cfg.io_channels, L, generator=g)[..., sp.lat_start:sp.lat_end].to(dev)
+    cond = torch.randn(1, wl["Tc"], cfg.cond_token_dim, generator=g).to(dev)
+    gemb = torch.randn(1, cfg.global_cond_dim, generator=g).to(dev)
+    t = torch.full((1,), 0.5, device=dev)
+
+    def one_step():
+        return eng.forward_split(x, t, sp, cond, gemb, None, cfg_scale=wl["cfg_scale"], apg_scale=wl["apg_scale"])
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            one_step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        clocks.start()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            one_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": 2 * L / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp8-e4m3 linears / bf16 attention", "data": "synthetic",
+            "config": {"workload": args.workload, "model": f"sa3-{wl['model']} DiT, random init", "L": L,
+                       "memory_tokens": cfg.num_memory_tokens, "global_batch": 2,
+                       "parallelism": f"sequence split over {world} (halo {cfg.sliding_window})",
+                       "tokens_rank0": sp.tok_end - sp.tok_start},
+            "clocks": clk,
+        }), flush=True)
+
+
 def run_ours(args, wl, world, rank, local):
     from sa3_b200 import ops, _lib
     from sa3_b200.modules import DiffusionTransformer, init_synthetic_
@@ -324,7 +379,7 @@ def run_ours(args, wl, world, rank, local):
         ms = e0.elapsed_time(e1) / args.steps
         clk = clocks.stop()
     ms_max = max_over_ranks(ms, world)
-    tokens_per_gpu = 2 * wl["L"] * wl["prompts"]
+    tokens_per_gpu = 2 * wl["L"] * wl.get("prompts", 1)
     value = tokens_per_gpu * world / (ms_max / 1e3)
 
     # ---- e2e: the public module call with pinned HOST inputs (H2D inside), result read back to the host
@@ -404,7 +459,7 @@ def run_ours(args, wl, world, rank, local):
                        "dim": cfg.embed_dim, "depth": cfg.depth, "heads": cfg.num_heads,
                        "differential": cfg.differential, "window": list(cfg.sliding_window), "L": wl["L"],
                        "memory_tokens": cfg.num_memory_tokens, "context_tokens": wl["Tc"],
-                       "prompts_per_gpu": wl["prompts"], "global_batch": 2 * wl["prompts"] * world,
+                       "prompts_per_gpu": wl.get("prompts", 1), "global_batch": 2 * wl.get("prompts", 1) * world,
                        "seq_len": wl["L"], "cfg_scale": wl["cfg_scale"], "parallelism": f"dp{world}",
                        "l2": "working set > L2 (1.45 GB FP8 weights + activations per step); no flush"},
             "clocks": clk,
@@ -444,6 +499,8 @@ def main():
     try:
         if wl.get("dp"):
             run_dp_varlen(args, wl, world, rank, local)
+        elif wl.get("seq_split"):
+            run_seq_split(args, wl, world, rank, local)
         else:
             run_ours(args, wl, world, rank, local)
     finally:

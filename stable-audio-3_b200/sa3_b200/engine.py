@@ -38,6 +38,7 @@ import torch
 from . import ops
 from . import _lib
 from . import gptq as _gptq
+from . import seqsplit as _seqsplit
 from .quant import interleave_swiglu_rows, quantize_weight_e4m3, swiglu_interleave_index
 
 QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cross_attn.to_kv",
@@ -81,9 +82,13 @@ class _Workspace:
     row_batch (sequence of each row), row_pos (RoPE position), lat_rows (stream row of each latent row)
     and mem_rows (stream rows of the memory tokens)."""
 
-    def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False):
+    def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False,
+                 split: Optional["_seqsplit.SeqSplit"] = None):
         D = cfg.embed_dim
-        nm = cfg.num_memory_tokens
+        # a sequence-split rank holds stream tokens [tok_start, tok_end) of each sequence: memory tokens only on
+        # rank 0, RoPE at global positions
+        nm = cfg.num_memory_tokens if split is None else split.memory_here
+        pos0 = 0 if split is None else split.tok_start
         B = len(lengths)
         Ns = [L + nm for L in lengths]
         M = sum(Ns)
@@ -91,6 +96,7 @@ class _Workspace:
         nq = 5 if cfg.differential else 3
         self.lengths, self.B, self.M, self.R, self.Tc = tuple(lengths), B, M, R, Tc
         self.max_n = max(Ns)
+        self.nm, self.max_pos, self.split = nm, pos0 + max(Ns), split
         # sequences of one length (a CFG pair, a uniform batch): batch(row) = row // N, which lets the norm
         # keep every batch's modulation coefficients in shared memory instead of a per-row table lookup
         self.uniform_n = Ns[0] if all(n == Ns[0] for n in Ns) else 0
@@ -98,7 +104,7 @@ class _Workspace:
         cu[1:] = np.cumsum(Ns)
         self.cu_host = cu
         row_batch = np.repeat(np.arange(B, dtype=np.int32), Ns)
-        row_pos = np.concatenate([np.arange(n, dtype=np.int32) for n in Ns])
+        row_pos = np.concatenate([pos0 + np.arange(n, dtype=np.int32) for n in Ns])
         lat_rows = np.concatenate([np.arange(cu[b] + nm, cu[b + 1], dtype=np.int32) for b in range(B)])
         mem_rows = np.concatenate([np.arange(cu[b], cu[b] + nm, dtype=np.int64) for b in range(B)]) if nm else None
         self.cu = torch.from_numpy(cu.astype(np.int32)).to(dev)
@@ -112,6 +118,12 @@ class _Workspace:
         self.h = torch.empty(M, D, device=dev, dtype=torch.float32)  # fp32 residual stream
         self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
         self.qkv = torch.empty(M, nq * D, device=dev, dtype=bf)
+        if split is not None:
+            # per sequence [left halo | own rows | right halo] of the q|k|v|q'|k' projection
+            if any(n != Ns[0] for n in Ns):
+                raise ValueError("a sequence split needs sequences of one length")
+            self.halo_e = split.halo_left + Ns[0] + split.halo_right
+            self.qkv_ext = torch.empty(B * self.halo_e, nq * D, device=dev, dtype=bf)
         self.o = torch.empty(M, D, device=dev, dtype=bf)
         self.o8 = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.qx = torch.empty(M, (2 if cfg.differential else 1) * D, device=dev, dtype=bf)
@@ -246,14 +258,14 @@ class DiTEngine:
             return Lin(wq.to(self.dev).contiguous(), s.to(self.dev), bias, True)
         return Lin(w.to(self.dev, torch.bfloat16).contiguous(), None, bias, False)
 
-    def _workspace(self, lengths, Tc) -> _Workspace:
+    def _workspace(self, lengths, Tc, split=None) -> _Workspace:
         ws = self.ws
-        if ws is None or (ws.lengths, ws.Tc) != (tuple(lengths), Tc):
+        if ws is None or (ws.lengths, ws.Tc, ws.split) != (tuple(lengths), Tc, split):
             self.ws = ws = None
             self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k,
-                                      local_all=self.loc1_all is not None)
-        if self.rope is None or self.rope.shape[0] < ws.max_n:
-            self.rope = ops.rope_table(ws.max_n, 32, device=self.dev)
+                                      local_all=self.loc1_all is not None, split=split)
+        if self.rope is None or self.rope.shape[0] < ws.max_pos:
+            self.rope = ops.rope_table(ws.max_pos, 32, device=self.dev)
         return ws
 
     # ------------------------------------------------------------------ helpers
@@ -290,7 +302,66 @@ class DiTEngine:
         ops.quantize_e4m3(x, ws.amax[slot:slot + 1], out=out8, scale_out=sc)
         return out8, sc
 
+    def _split_self_attention(self, ws, a, asc, lin, groups, rope, o, amax_out, wl, wr):
+        """Self-attention of a sequence-split rank: the q|k|v|q'|k' projection of each sequence lands between
+        its halo rows, the boundary rows are exchanged with the neighbouring ranks, and the queries of the
+        own rows attend over [left halo | own | right halo] with the window re-centred."""
+        cfg, sp = self.cfg, ws.split
+        if (sp.wl, sp.wr) != (wl, wr):
+            raise ValueError(f"split made for window {(sp.wl, sp.wr)}, the model attends over {(wl, wr)}")
+        D, H, n, e, hl = cfg.embed_dim, cfg.num_heads, ws.uniform_n, ws.halo_e, sp.halo_left
+        ext = ws.qkv_ext
+        for b in range(ws.B):
+            self._gemm(a[b * n:(b + 1) * n], lin, ext[b * e + hl:b * e + hl + n], x_scale=asc, kind=_lib.EPI_QK_NORM,
+                       qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
+                               row_pos=ws.row_pos[b * n:(b + 1) * n]))
+        _seqsplit.exchange_halos(ext, ws.B, n, sp)
+        wl2, wr2 = _seqsplit.halo_window(wl, wr, sp.halo_left, sp.halo_right)
+        for b in range(ws.B):
+            blk = ext[b * e:(b + 1) * e]
+            own = blk[hl:hl + n]
+            kw = dict(heads=H, window=(wl2, wr2), out=o[b * n:(b + 1) * n], amax_out=amax_out, batch=1,
+                      max_seqlen_q=n, max_seqlen_k=e)
+            if cfg.differential:
+                ops.attention(own[:, 0:D], blk[:, D:2 * D], blk[:, 2 * D:3 * D], q2=own[:, 3 * D:4 * D],
+                              k2=blk[:, 4 * D:5 * D], **kw)
+            else:
+                ops.attention(own[:, 0:D], blk[:, D:2 * D], blk[:, 2 * D:3 * D], **kw)
+
     # ------------------------------------------------------------------ forward
+    @torch.no_grad()
+    def forward_split(self, x, t, split, cross_attn_cond=None, global_embed=None, local_add_cond=None,
+                      cfg_scale: float = 1.0, apg_scale: float = 1.0):
+        """DiffusionTransformer.forward on this rank's share of one long sequence (sa3_b200.seqsplit): x and
+        local_add_cond hold the latent columns [split.lat_start, split.lat_end); every rank of split.group calls
+        this with the same t / conditioning. Returns this rank's columns of the velocity."""
+        dev = self.dev
+        x = x.to(dev)
+        t = t.to(dev, torch.float32)
+        if cfg_scale != 1.0 and cross_attn_cond is not None:
+            cc = cross_attn_cond.to(dev)
+            bg = torch.cat([global_embed, global_embed]).to(dev) if global_embed is not None else None
+            bl = torch.cat([local_add_cond, local_add_cond]).to(dev) if local_add_cond is not None else None
+            out = self.inner_split(torch.cat([x, x]), torch.cat([t, t]), split, torch.cat([cc, torch.zeros_like(cc)]),
+                                   bg, bl)
+            return _seqsplit.cfg_combine_split(x, t, out, cfg_scale, apg_scale, split.group)
+        return self.inner_split(x, t, split, cross_attn_cond, global_embed, local_add_cond)
+
+    @torch.no_grad()
+    def inner_split(self, x, t, split, cross_attn_cond=None, global_embed=None, local_add_cond=None):
+        """`inner` on a sequence-split rank: x [B, C, lat_end - lat_start] (B sequences of one length, all split
+        the same way); returns fp32 [B, C, lat_end - lat_start]."""
+        B, C, L = x.shape
+        if L != split.lat_end - split.lat_start:
+            raise ValueError(f"rank {split.rank} holds {split.lat_end - split.lat_start} latents, got {L}")
+        Tc = cross_attn_cond.shape[1] if cross_attn_cond is not None else 0
+        ws = self._workspace([L] * B, Tc, split)
+        ws.xin.view(B, L, C).copy_(x.transpose(1, 2))
+        if local_add_cond is not None and self.cfg.local_add_cond_dim > 0:
+            ws.loc.view(B, L, -1)[:, :, :self.cfg.local_add_cond_dim].copy_(local_add_cond.transpose(1, 2))
+        self._trunk(ws, t, cross_attn_cond, global_embed, local_add_cond is not None)
+        return ws.out.view(B, L, C).transpose(1, 2)
+
     @torch.no_grad()
     def forward(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, cfg_scale: float = 1.0,
                 apg_scale: float = 1.0):
@@ -389,7 +460,7 @@ class DiTEngine:
         cfg = self.cfg
         D = cfg.embed_dim
         B, Tc = ws.B, ws.Tc
-        nm = cfg.num_memory_tokens
+        nm = ws.nm
         ln = self.lin
         ws.amax.zero_()
 
@@ -452,16 +523,19 @@ class DiTEngine:
             # to_qkv with qk RMSNorm + RoPE fused into the epilogue (groups q | k | v | q_diff | k_diff)
             groups = [gq, gk, None, gq, gk] if diff else [gq, gk, None]
             rope = [True, True, False, True, True] if diff else [True, True, False]
-            self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM,
-                       qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
-                               row_pos=ws.row_pos))
             am1 = ws.amax[s0 + 1:s0 + 2] if self.fp8 else None
-            if diff:
-                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
-                              k2=qkv[:, 4 * D:5 * D], heads=H, window=(wl, wr), out=o, amax_out=am1, **seq)
+            if ws.split is not None:
+                self._split_self_attention(ws, a, asc, ln[p + "self_attn.to_qkv"], groups, rope, o, am1, wl, wr)
             else:
-                ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, window=(wl, wr), out=o,
-                              amax_out=am1, **seq)
+                self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM,
+                           qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
+                                   row_pos=ws.row_pos))
+                if diff:
+                    ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
+                                  k2=qkv[:, 4 * D:5 * D], heads=H, window=(wl, wr), out=o, amax_out=am1, **seq)
+                else:
+                    ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, window=(wl, wr),
+                                  out=o, amax_out=am1, **seq)
             oa, osc = self._quant(ws, o, ws.o8, s0 + 1)
             self._gemm(oa, ln[p + "self_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
                        gate=ssi[:, 2 * D:3 * D], row_batch=rb)

@@ -1,0 +1,138 @@
+"""One long sequence split across GPUs (sequence parallelism for the windowed DiT trunk).
+
+The token stream of a sequence ([64 memory tokens | L latents], positions 0..N-1,
+stable_audio_3/models/transformer.py:1215-1230) is cut into contiguous ranges, one
+per rank; rank 0 holds the memory tokens. Everything in a block is row-local except
+the windowed self-attention (transformer.py:598-700) with window (wl, wr): before it,
+every rank sends the first wr rows of its post-RoPE q|k|v|q'|k' projection to its left
+neighbour and the last wl rows to its right neighbour (NCCL send/recv through
+torch.distributed), and attends over [left halo | own rows | right halo] with the window
+re-centred on its own rows. RoPE uses global positions. The CFG/APG combine (dit.py:571-625) needs two
+sums over the whole sequence per prompt; they are all-reduced. Cross-attention keys
+(the context) and the conditioning are replicated.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class SeqSplit:
+    """This rank's share of one sequence: stream tokens [tok_start, tok_end) of N = memory + L, i.e. latents
+    [lat_start, lat_end). Before every self-attention with window (wl, wr) the rank receives wl rows from its
+    left neighbour and wr rows from its right neighbour."""
+
+    rank: int
+    world: int
+    tok_start: int
+    tok_end: int
+    memory_tokens: int
+    wl: int
+    wr: int
+    group: object = None
+
+    @property
+    def lat_start(self) -> int:
+        return max(self.tok_start, self.memory_tokens) - self.memory_tokens
+
+    @property
+    def lat_end(self) -> int:
+        return self.tok_end - self.memory_tokens
+
+    @property
+    def memory_here(self) -> int:
+        """Memory tokens in this rank's rows (all of them on rank 0, none elsewhere)."""
+        return max(0, min(self.tok_end, self.memory_tokens) - self.tok_start)
+
+    @property
+    def halo_left(self) -> int:
+        return self.wl if self.rank > 0 else 0
+
+    @property
+    def halo_right(self) -> int:
+        return self.wr if self.rank < self.world - 1 else 0
+
+
+def split_ranges(latents: int, world: int, memory_tokens: int = 64, halo: int = 256) -> List[Tuple[int, int]]:
+    """Contiguous, balanced token ranges of the N = memory + latents stream, one per rank. Every range
+    must hold at least `halo` = max(wl, wr) tokens (a halo never reaches past the neighbouring rank)."""
+    n = latents + memory_tokens
+    bounds = [round(r * n / world) for r in range(world + 1)]
+    ranges = [(bounds[r], bounds[r + 1]) for r in range(world)]
+    if world > 1 and min(e - s for s, e in ranges) < halo:
+        raise ValueError(f"{n} tokens over {world} ranks leave fewer than {halo} tokens on a rank")
+    if ranges[0][1] < memory_tokens:
+        raise ValueError("rank 0 must hold all memory tokens")
+    return ranges
+
+
+def make_split(latents: int, rank: int, world: int, memory_tokens: int = 64, window=(256, 256),
+               group=None) -> SeqSplit:
+    wl, wr = window
+    if wl < 0 or wr < 0:
+        raise ValueError("the sequence split needs a bounded window")
+    s, e = split_ranges(latents, world, memory_tokens, max(wl, wr, 1))[rank]
+    return SeqSplit(rank, world, s, e, memory_tokens, wl, wr, group)
+
+
+def halo_window(wl: int, wr: int, halo_left: int, halo_right: int) -> Tuple[int, int]:
+    """Window for queries = own rows, keys = [halo_left | own | halo_right] under the kernels' convention that
+    the band is centred on key j = i + (lk - lq) (flash-attn's bottom-right alignment): own row i sits at key
+    halo_left + i and lk - lq = halo_left + halo_right, so the band [i - wl, i + wr] becomes
+    (wl + halo_right, wr - halo_right). The halos hold exactly wl (left) and wr (right) rows, or none at
+    the ends of the sequence."""
+    if wl < 0 or wr < 0:
+        raise ValueError("the sequence split needs a bounded window")
+    if halo_left not in (0, wl) or halo_right not in (0, wr):
+        raise ValueError("halos must hold exactly the window's rows")
+    return wl + halo_right, wr - halo_right
+
+
+def exchange_halos(ext: torch.Tensor, batch: int, own: int, split: SeqSplit) -> None:
+    """ext: [batch * (hl + own + hr), C] rows laid out per sequence as [left halo | own rows | right halo].
+    Fills the halo rows from the neighbours (their own rows next to the boundary) and sends this rank's
+    boundary rows. All transfers of one call form one batched group of P2P operations."""
+    hl, hr = split.halo_left, split.halo_right
+    e = hl + own + hr
+    ops = []
+    for b in range(batch):
+        base = b * e
+        if hl:  # the left neighbour's right halo is wr rows; its last wl rows are this rank's left halo
+            ops.append(dist.P2POp(dist.isend, ext[base + hl:base + hl + split.wr], split.rank - 1, split.group))
+            ops.append(dist.P2POp(dist.irecv, ext[base:base + hl], split.rank - 1, split.group))
+        if hr:
+            ops.append(dist.P2POp(dist.isend, ext[base + hl + own - split.wl:base + hl + own], split.rank + 1,
+                                  split.group))
+            ops.append(dist.P2POp(dist.irecv, ext[base + hl + own:base + e], split.rank + 1, split.group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+
+def cfg_combine_split(x: torch.Tensor, t: torch.Tensor, out: torch.Tensor, cfg_scale: float, apg_scale: float,
+                      group=None) -> torch.Tensor:
+    """CFG + APG (dit.py:571-625, apg_project dit.py:311-343) on this rank's latent columns x [B, C, Lr],
+    out [2B, C, Lr] (cond | uncond). The projection's two sums over (C, T) of each prompt, |cond_den|^2 and
+    <diff, cond_den>, are summed over the ranks; the rest is elementwise. fp32."""
+    x = x.float()
+    cond_out, uncond_out = out.float().chunk(2)
+    sigma = t.float()[:, None, None]
+    cond_den = x - cond_out * sigma
+    diff = (uncond_out - cond_out) * sigma
+    if apg_scale == 0.0:
+        cfg_diff = diff
+    else:
+        sums = torch.stack([cond_den.pow(2).sum(dim=(1, 2)), (diff * cond_den).sum(dim=(1, 2))])
+        if dist.is_initialized():
+            dist.all_reduce(sums, group=group)
+        nrm = sums[0].sqrt().clamp_min(1e-12)
+        # apg_project: v1 = cond_den / |cond_den|; parallel = <diff, v1> v1
+        par = (sums[1] / (nrm * nrm))[:, None, None] * cond_den
+        orth = diff - par
+        cfg_diff = orth if apg_scale == 1.0 else apg_scale * orth + (1 - apg_scale) * diff
+    cfg_den = cond_den + (cfg_scale - 1) * cfg_diff
+    return (x - cfg_den) / sigma

@@ -1,0 +1,112 @@
+"""CPU: one sequence split across ranks (sa3_b200.seqsplit), with 2-4 gloo ranks as separate processes.
+
+The split must reproduce the unsplit computation: windowed attention of each rank's own rows over
+[left halo | own | right halo] with the re-centred window equals the rows of the full-sequence oracle
+attention (oracle/ref.py attention, the masked-SDPA definition of transformer.py:696-699), and the
+CFG/APG combine with its two sums all-reduced equals the combine over the whole sequence."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import ref as orf
+from sa3_b200 import seqsplit as ss
+
+
+def test_split_ranges_cover_the_stream():
+    for latents, world in ((8183, 2), (16384, 8), (1000, 4), (300, 2)):
+        r = ss.split_ranges(latents, world, 64, 64)
+        assert r[0][0] == 0 and r[-1][1] == latents + 64
+        assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+        assert max(e - s for s, e in r) - min(e - s for s, e in r) <= 1
+        sp = [ss.make_split(latents, k, world, 64, (64, 64)) for k in range(world)]
+        assert sp[0].memory_here == 64 and all(x.memory_here == 0 for x in sp[1:])
+        assert sum(x.lat_end - x.lat_start for x in sp) == latents
+    with pytest.raises(ValueError):
+        ss.split_ranges(200, 4, 64, 256)
+
+
+def test_halo_window_recentres_the_band():
+    for wl, wr, hl, hr in ((256, 256, 0, 256), (256, 256, 256, 256), (256, 256, 256, 0), (64, 32, 64, 32),
+                           (64, 32, 0, 32), (17, 40, 17, 0)):
+        wl2, wr2 = ss.halo_window(wl, wr, hl, hr)
+        n = 700
+        m = orf.band_mask(n, hl + n + hr, wl2, wr2)
+        i = torch.arange(n)[:, None]
+        j = torch.arange(hl + n + hr)[None, :] - hl  # key position relative to the own rows
+        assert torch.equal(m, (j - i >= -wl) & (j - i <= wr))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, n_tok, window, outq):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator().manual_seed(0)
+        B, d = 2, 64
+        q = torch.randn(B, n_tok, d, generator=g)
+        k = torch.randn(B, n_tok, d, generator=g)
+        v = torch.randn(B, n_tok, d, generator=g)
+        sp = ss.make_split(n_tok - 64, rank, world, 64, window)
+        s0, s1 = sp.tok_start, sp.tok_end
+        own = s1 - s0
+        hl, hr = sp.halo_left, sp.halo_right
+        e = hl + own + hr
+        ext = torch.zeros(B * e, 2 * d)  # columns k | v
+        for b in range(B):
+            ext[b * e + hl:b * e + hl + own] = torch.cat([k[b, s0:s1], v[b, s0:s1]], dim=1)
+        ss.exchange_halos(ext, B, own, sp)
+        wl2, wr2 = ss.halo_window(*window, hl, hr)
+        outs = []
+        for b in range(B):
+            blk = ext[b * e:(b + 1) * e]
+            outs.append(orf.attention(q[b, s0:s1], blk[:, :d], blk[:, d:], wl2, wr2))
+        # CFG/APG combine on this rank's latent columns
+        C = 8
+        x = torch.randn(1, C, n_tok - 64, generator=g)
+        out2 = torch.randn(2, C, n_tok - 64, generator=g)
+        t = torch.tensor([0.6])
+        comb = ss.cfg_combine_split(x[..., sp.lat_start:sp.lat_end], t, out2[..., sp.lat_start:sp.lat_end], 5.0, 0.7)
+        # numpy payloads travel by value (a shared-memory tensor could outlive its sender)
+        outq.put((rank, s0, s1, torch.stack(outs).numpy(), sp.lat_start, sp.lat_end, comb.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n_tok,window", [(2, 1100, (256, 256)), (3, 900, (64, 48)), (4, 700, (17, 40))])
+def test_split_attention_and_cfg_match_unsplit(world, n_tok, window):
+    ctx = mp.get_context("spawn")
+    outq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, n_tok, window, outq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([outq.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g = torch.Generator().manual_seed(0)
+    B, d = 2, 64
+    q = torch.randn(B, n_tok, d, generator=g)
+    k = torch.randn(B, n_tok, d, generator=g)
+    v = torch.randn(B, n_tok, d, generator=g)
+    full = torch.stack([orf.attention(q[b], k[b], v[b], *window) for b in range(B)])
+    got = torch.cat([torch.from_numpy(r[3]) for r in res], dim=1)
+    assert [r[1] for r in res] == sorted(r[1] for r in res) and res[-1][2] == n_tok
+    assert torch.allclose(got, full, atol=1e-5, rtol=1e-5)
+    x = torch.randn(1, 8, n_tok - 64, generator=g)
+    out2 = torch.randn(2, 8, n_tok - 64, generator=g)
+    ref = ss.cfg_combine_split(x, torch.tensor([0.6]), out2, 5.0, 0.7)
+    comb = torch.cat([torch.from_numpy(r[6]) for r in res], dim=-1)
+    assert torch.allclose(comb, ref, atol=1e-5, rtol=1e-4)

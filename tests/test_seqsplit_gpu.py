@@ -1,0 +1,120 @@
+"""One long sequence split over 2 GPUs (sa3_b200.seqsplit): the denoiser velocity of the split forward, with the
+per-layer NCCL halo exchange and the all-reduced CFG/APG sums, against the unsplit forward on one GPU.
+Skipped with fewer than 2 GPUs.
+
+Asserted on the network output for both CFG halves (before the combine) and on the full CFG/APG velocity.
+bf16: the split changes the row grouping and the key-tile grouping of the attention, so it agrees with the
+unsplit forward to rounding; the CFG/APG combine (cfg 5) amplifies that rounding, as it does for the
+reference's own bf16 module, so the velocity gets the full-step bound. FP8: each rank quantizes its own rows
+with its own per-tensor activation scale (the tensor is the rank's shard), so the bounds are the FP8 ones of
+the model tests."""
+import datetime
+import os
+import queue
+import socket
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from sa3_b200.modules import DiffusionTransformer, init_synthetic_
+from tests.golden.cases import _small
+
+pytestmark = pytest.mark.gpu
+
+L, TC, SEED = 900, 16, 11
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.randn(1, _small.io_channels, L, generator=g)
+    t = torch.tensor([0.55])
+    cond = torch.randn(1, TC, _small.cond_token_dim, generator=g)
+    gemb = torch.randn(1, _small.global_cond_dim, generator=g)
+    loc = torch.randn(1, _small.local_add_cond_dim, L, generator=g) * 0.5
+    return x, t, cond, gemb, loc
+
+
+def _model(mode):
+    return init_synthetic_(DiffusionTransformer(_small), seed=SEED).quantize(mode)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, mode, outq):
+    from sa3_b200 import seqsplit as ss
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    # a short timeout: a rank whose peer died errors out instead of waiting in the halo exchange
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        eng = _model(mode).engine()
+        sp = ss.make_split(L, rank, world, _small.num_memory_tokens, _small.sliding_window)
+        x, t, cond, gemb, loc = (v.cuda() for v in _inputs())
+        a, b = sp.lat_start, sp.lat_end
+        with torch.inference_mode():
+            for _ in range(2):  # the second call reuses the workspace
+                v = eng.forward_split(x[..., a:b], t, sp, cond, gemb, loc[..., a:b], cfg_scale=5.0, apg_scale=1.0)
+            xb, lb = x[..., a:b], loc[..., a:b]
+            net = eng.inner_split(torch.cat([xb, xb]), torch.cat([t, t]), sp, torch.cat([cond, torch.zeros_like(cond)]),
+                                  torch.cat([gemb, gemb]), torch.cat([lb, lb]))
+        torch.cuda.synchronize()
+        # by value: the sender exits right after
+        outq.put((rank, a, b, v.cpu().numpy(), net.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode,tol_net,tol_vel", [("bf16", 5e-3, 2e-2), ("fp8", 2e-2, 5e-2)])
+def test_sequence_split_matches_unsplit(cuda, mode, tol_net, tol_vel):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    outq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, outq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res, deadline = [], time.monotonic() + 600
+    try:
+        while len(res) < 2:
+            try:
+                res.append(outq.get(timeout=5))
+            except queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                if dead or time.monotonic() > deadline:
+                    pytest.fail(f"split workers failed (exit codes {[p.exitcode for p in procs]})")
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    res.sort(key=lambda r: r[0])
+    assert res[0][1] == 0 and res[0][2] == res[1][1] and res[1][2] == L
+    split = torch.cat([torch.from_numpy(r[3]) for r in res], dim=-1)
+    net = torch.cat([torch.from_numpy(r[4]) for r in res], dim=-1)
+    x, t, cond, gemb, loc = _inputs()
+    eng = _model(mode).engine()
+    with torch.inference_mode():
+        ref = eng.forward(x.to(cuda), t.to(cuda), cond.to(cuda), gemb.to(cuda), loc.to(cuda), cfg_scale=5.0,
+                          apg_scale=1.0).cpu()
+        ref_net = eng.inner(torch.cat([x, x]).to(cuda), torch.cat([t, t]).to(cuda),
+                            torch.cat([cond, torch.zeros_like(cond)]).to(cuda), torch.cat([gemb, gemb]).to(cuda),
+                            torch.cat([loc, loc]).to(cuda)).cpu()
+    assert torch.isfinite(split).all() and torch.isfinite(net).all()
+    err_net = ((net - ref_net).norm() / ref_net.norm()).item()
+    err_vel = ((split - ref).norm() / ref.norm()).item()
+    assert err_net < tol_net, err_net
+    assert err_vel < tol_vel, err_vel
