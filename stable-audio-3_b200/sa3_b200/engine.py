@@ -83,7 +83,7 @@ class _Workspace:
     and mem_rows (stream rows of the memory tokens)."""
 
     def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False,
-                 split: Optional["_seqsplit.SeqSplit"] = None):
+                 split: Optional["_seqsplit.SeqSplit"] = None, kv_all: bool = False):
         D = cfg.embed_dim
         # a sequence-split rank holds stream tokens [tok_start, tok_end) of each sequence: memory tokens only on
         # rank 0, RoPE at global positions
@@ -130,7 +130,7 @@ class _Workspace:
         self.kv = torch.empty(max(B * Tc, 1), (3 if cfg.differential else 2) * D, device=dev, dtype=bf)
         # every block's cross-attention K/V, computed once per forward
         self.kv_all = torch.empty(max(B * Tc, 1), cfg.depth * (3 if cfg.differential else 2) * D, device=dev,
-                                  dtype=bf) if Tc else None
+                                  dtype=bf) if Tc and kv_all else None
         self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
         self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.t1 = torch.empty(R, D, device=dev, dtype=bf)
@@ -220,7 +220,8 @@ class DiTEngine:
         D, L = cfg.embed_dim, cfg.depth
         names = [f"transformer.layers.{i}.cross_attn.to_kv" for i in range(L)]
         self.kv_all = None
-        if not all(n in self.lin and self.lin[n].gptq is None for n in names):
+        gnames = [f"transformer.layers.{i}.cross_attn.k_norm.gamma" for i in range(L)]
+        if not all(n in self.lin and self.lin[n].gptq is None for n in names) or not all(g in self.gam for g in gnames):
             return
         lins = [self.lin[n] for n in names]
         nk = 2 if cfg.differential else 1
@@ -231,7 +232,7 @@ class DiTEngine:
         if any(ln.bias is not None for ln in lins):
             bias = torch.cat([(lins[i].bias[j * D:(j + 1) * D] if lins[i].bias is not None
                                else torch.zeros(D, device=self.dev)) for i, j in order]).contiguous()
-        gk = [self.gam[f"transformer.layers.{i}.cross_attn.k_norm.gamma"] for i in range(L)]
+        gk = [self.gam[g] for g in gnames]
         self.kv_gamma = torch.stack([gk[i] for i in range(L) for _ in range(nk)]).float().contiguous()
         self.kv_all = Lin(w, scale, bias, lins[0].fp8)
         self.kv_nk = nk
@@ -263,7 +264,8 @@ class DiTEngine:
         if ws is None or (ws.lengths, ws.Tc, ws.split) != (tuple(lengths), Tc, split):
             self.ws = ws = None
             self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k,
-                                      local_all=self.loc1_all is not None, split=split)
+                                      local_all=self.loc1_all is not None, split=split,
+                                      kv_all=self.kv_all is not None)
         if self.rope is None or self.rope.shape[0] < ws.max_pos:
             self.rope = ops.rope_table(ws.max_pos, 32, device=self.dev)
         return ws
