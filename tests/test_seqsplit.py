@@ -110,3 +110,27 @@ def test_split_attention_and_cfg_match_unsplit(world, n_tok, window):
     ref = ss.cfg_combine_split(x, torch.tensor([0.6]), out2, 5.0, 0.7)
     comb = torch.cat([torch.from_numpy(r[6]) for r in res], dim=-1)
     assert torch.allclose(comb, ref, atol=1e-5, rtol=1e-4)
+
+
+def test_split_workspace_tables():
+    """The per-row tables of a split rank: global RoPE positions, memory rows only on rank 0, latent rows after
+    them, and the halo-extended projection buffer (built on the CPU: only shapes and tables are checked)."""
+    from sa3_b200.engine import _Workspace
+    from sa3_b200.modules import DiTConfig
+
+    cfg = DiTConfig(embed_dim=256, depth=2, num_heads=4, sliding_window=(64, 48), differential=True)
+    lat = 1000
+    for world in (2, 3):
+        for rank in range(world):
+            sp = ss.make_split(lat, rank, world, cfg.num_memory_tokens, cfg.sliding_window)
+            own_lat = sp.lat_end - sp.lat_start
+            ws = _Workspace(cfg, [own_lat, own_lat], 0, torch.device("cpu"), False, split=sp)
+            n = sp.tok_end - sp.tok_start
+            assert ws.uniform_n == n and ws.nm == sp.memory_here
+            assert torch.equal(ws.row_pos[:n], torch.arange(sp.tok_start, sp.tok_end, dtype=torch.int32))
+            assert torch.equal(ws.row_pos[n:], ws.row_pos[:n])
+            assert ws.lat_rows.tolist() == list(range(sp.memory_here, n)) + list(range(n + sp.memory_here, 2 * n))
+            assert (ws.mem_rows is not None) == (rank == 0)
+            assert ws.halo_e == sp.halo_left + n + sp.halo_right
+            assert ws.qkv_ext.shape == (2 * ws.halo_e, 5 * cfg.embed_dim)
+            assert ws.max_pos == sp.tok_end
