@@ -15,7 +15,7 @@ ContinuousTransformer.forward (transformer.py:1161-1272) -> TransformerBlock.for
     FF: RMSNorm+modulate (+quant) -> GLU.proj GEMM with SwiGLU epilogue (+amax) (-> quant)
         -> linear_out GEMM with gate*sigmoid(1-g)+residual epilogue
 
-Exact rewrites of the reference (documented in DESIGN.md):
+Exact rewrites of the reference:
   * preprocess_conv (1x1, +x) is folded into project_in: W_in (I + W_pre);
     postprocess_conv (1x1, +y) into project_out: (I + W_post) W_out.
   * GLU.proj rows are interleaved in blocks of 128 so the SwiGLU fuses into the GEMM epilogue.
