@@ -66,3 +66,24 @@ def test_epilogue_struct_layout_matches_header(tmp_path):
     assert out[0] == ctypes.sizeof(_lib.Epilogue)
     for f, off in zip(fields, out[1:]):
         assert getattr(_lib.Epilogue, f).offset == off, f
+
+
+def test_qk_gamma_table_arguments_checked_on_host():
+    """The qk-norm epilogue's gamma-table mode: bad table arguments are rejected before any CUDA call (the
+    pointers below are aligned placeholders that are never dereferenced)."""
+    lib = _lib.load()
+    A = B = C = 0x100000
+
+    def gemm(**kw):
+        e = _lib.Epilogue()
+        e.kind = _lib.EPI_QK_NORM
+        e.qk_group_width = 128
+        for k, v in kw.items():
+            setattr(e, k, v)
+        return lib.sa3_gemm(A, B, C, 256, 1536, 256, 256, 256, 1536, _lib.DT_BF16, None, None, ctypes.byref(e), None)
+
+    assert gemm() == -1  # 12 groups of 128 columns without a table: more than 8
+    assert gemm(qk_gamma_table=0x200000, qk_table_groups=0) == -1
+    assert gemm(qk_gamma_table=0x200000, qk_table_groups=9, qk_rope_mask=1) == -1  # no rotary embedding in table mode
+    assert gemm(qk_gamma_table=0x200004, qk_table_groups=9) == -2  # 16-byte alignment
+    assert gemm(qk_group_width=96, qk_gamma_table=0x200000, qk_table_groups=9) == -1  # group width % 64
