@@ -134,3 +134,17 @@ def test_split_workspace_tables():
             assert ws.halo_e == sp.halo_left + n + sp.halo_right
             assert ws.qkv_ext.shape == (2 * ws.halo_e, 5 * cfg.embed_dim)
             assert ws.max_pos == sp.tok_end
+
+
+@pytest.mark.parametrize("apg_scale", [0.0, 0.5, 1.0])
+def test_split_combine_matches_oracle_on_one_rank(apg_scale):
+    """Without a process group the split combine is the oracle's CFG/APG combine (dit.py:571-625)."""
+    from oracle import dit as odit
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 8, 300, generator=g)
+    out = torch.randn(4, 8, 300, generator=g)
+    t = torch.tensor([0.3, 0.8])
+    ref = odit.cfg_combine(x, t, out, 5.0, apg_scale)
+    got = ss.cfg_combine_split(x, t, out, 5.0, apg_scale)
+    assert torch.allclose(got, ref, atol=1e-5, rtol=1e-5)
