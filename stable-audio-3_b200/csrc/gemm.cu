@@ -405,9 +405,19 @@ __global__ void __launch_bounds__(128, 1)
 constexpr int PG_THREADS = 320;
 constexpr int PG_EPI_WARPS = 8;
 constexpr int PG_TMEM_COLS = 512;
-// ring | barriers (256 B) | epilogue transpose scratch (8 warps x 32 x 33 floats); + 1 KB alignment slack
+// Epilogue region, shared by the persistent kernels: the per-warp transpose scratch (8 warps x 32 x 33 floats)
+// and, on the same bytes, the per-warp 2 x 2 KB TMA-store staging buffers (512-byte aligned); the 2 residual-load
+// mbarriers of each warp follow the whole region, so no data store ever lands on a live mbarrier object.
+constexpr int PG_SCRATCH_BYTES = PG_EPI_WARPS * 32 * 33 * 4;
+constexpr int PG_STAGING_BYTES = PG_EPI_WARPS * 4096;
+constexpr int PG_RBAR_BYTES = 2 * PG_EPI_WARPS * 8;
+static_assert(PG_STAGING_BYTES + 511 <= PG_SCRATCH_BYTES, "TMA-store staging must fit inside the epilogue region");
+// byte offset of the residual-load barriers from the start of the epilogue region
+__host__ __device__ constexpr int pg_rbar_offset() { return PG_SCRATCH_BYTES; }
+// ring | barriers (256 B) | epilogue region | residual barriers; + 1 KB alignment slack
 constexpr int PG_SCRATCH_OFFSET = GEMM_STAGES * GEMM_STAGE_BYTES + 256;
-constexpr int PG_SMEM = PG_SCRATCH_OFFSET + PG_EPI_WARPS * 32 * 33 * 4 + 1024;
+constexpr int PG_SMEM = PG_SCRATCH_OFFSET + PG_SCRATCH_BYTES + PG_RBAR_BYTES + 1024;
+static_assert(PG_SCRATCH_OFFSET % 8 == 0 && PG_SCRATCH_BYTES % 8 == 0, "mbarriers need 8-byte alignment");
 static_assert(PG_SMEM <= 232448, "persistent GEMM exceeds the 227 KB shared-memory limit");
 
 // sigmoid(x) = (1 + tanh(x / 2)) / 2: one MUFU operation (tanh.approx, relative error ~2^-11) instead of an
@@ -901,7 +911,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     }
     *abort_flag = 0;
     {
-      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + PG_SCRATCH_OFFSET + pg_rbar_offset());
       for (int i = 0; i < 2 * PG_EPI_WARPS; ++i) mbar_init(&rb[i], 1);
     }
     fence_mbar_init();
@@ -981,7 +991,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int half = (warp - 2) >> 2;  // column half of the tile
     float* epi_scratch = reinterpret_cast<float*>(smem + PG_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
-    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + PG_SCRATCH_OFFSET + pg_rbar_offset());
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
                    rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
@@ -1041,7 +1051,8 @@ constexpr int P2_A_BYTES = 128 * 128;  // 128 rows x 128-byte K slice
 constexpr int P2_B_BYTES = 128 * 128;  // this CTA's half of the 256 B rows
 constexpr int P2_STAGE_BYTES = P2_A_BYTES + P2_B_BYTES;
 constexpr int P2_SCRATCH_OFFSET = P2_STAGES * P2_STAGE_BYTES + 256;
-constexpr int P2_SMEM = P2_SCRATCH_OFFSET + PG_EPI_WARPS * 32 * 33 * 4 + 1024;
+constexpr int P2_SMEM = P2_SCRATCH_OFFSET + PG_SCRATCH_BYTES + PG_RBAR_BYTES + 1024;
+static_assert(P2_SCRATCH_OFFSET % 8 == 0, "mbarriers need 8-byte alignment");
 static_assert(P2_SMEM <= 232448, "2-SM GEMM exceeds the 227 KB shared-memory limit");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -1136,7 +1147,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     }
     *abort_flag = 0;
     {
-      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+      uint64_t* rb = reinterpret_cast<uint64_t*>(smem + P2_SCRATCH_OFFSET + pg_rbar_offset());
       for (int i = 0; i < 2 * PG_EPI_WARPS; ++i) mbar_init(&rb[i], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1216,7 +1227,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     const int half = (warp - 2) >> 2;
     float* epi_scratch = reinterpret_cast<float*>(smem + P2_SCRATCH_OFFSET) + (warp - 2) * (32 * 33);
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
-    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + PG_EPI_WARPS * 4096);
+    uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + P2_SCRATCH_OFFSET + pg_rbar_offset());
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
                    rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
