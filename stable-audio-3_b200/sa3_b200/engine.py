@@ -80,10 +80,17 @@ class _Workspace:
     Sequences are packed back to back as token rows: sequence b occupies stream rows [cu[b], cu[b+1]),
     memory tokens first, then its L_b latents. Every per-row table the kernels take is built here once:
     row_batch (sequence of each row), row_pos (RoPE position), lat_rows (stream row of each latent row)
-    and mem_rows (stream rows of the memory tokens)."""
+    and mem_rows (stream rows of the memory tokens).
+
+    With a padding mask (`valid[b]` = sorted indices of sequence b's valid latents) the rows are laid out
+    valid-first: rows [0, V) hold every sequence's memory tokens and valid latents back to back (the packed
+    tokens of the reference's flash-varlen path, transformer.py:620-651), rows [V, M) the padded latents. The
+    self-attention then runs varlen over rows [0, V) with `cu`, the feed-forward runs on rows [0, V) only
+    (transformer.py:500-519), and the padded rows keep a zero self-attention output. RoPE positions stay the
+    original token positions."""
 
     def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False,
-                 split: Optional["_seqsplit.SeqSplit"] = None, kv_all: bool = False):
+                 split: Optional["_seqsplit.SeqSplit"] = None, kv_all: bool = False, valid=None):
         D = cfg.embed_dim
         # a sequence-split rank holds stream tokens [tok_start, tok_end) of each sequence: memory tokens only on
         # rank 0, RoPE at global positions
@@ -100,19 +107,59 @@ class _Workspace:
         # sequences of one length (a CFG pair, a uniform batch): batch(row) = row // N, which lets the norm
         # keep every batch's modulation coefficients in shared memory instead of a per-row table lookup
         self.uniform_n = Ns[0] if all(n == Ns[0] for n in Ns) else 0
-        cu = np.zeros(B + 1, dtype=np.int64)
-        cu[1:] = np.cumsum(Ns)
+        self.lat_off = [int(x) for x in np.concatenate([[0], np.cumsum(lengths)])]
+        self.masked = valid is not None
+        self.valid = valid
+        self.cu_pad = None
+        self.max_pad = 0
+        if not self.masked:
+            cu = np.zeros(B + 1, dtype=np.int64)
+            cu[1:] = np.cumsum(Ns)
+            row_batch = np.repeat(np.arange(B, dtype=np.int32), Ns)
+            row_pos = np.concatenate([pos0 + np.arange(n, dtype=np.int32) for n in Ns])
+            lat_rows = np.concatenate([np.arange(cu[b] + nm, cu[b + 1], dtype=np.int32) for b in range(B)])
+            mem_rows = (np.concatenate([np.arange(cu[b], cu[b] + nm, dtype=np.int64) for b in range(B)])
+                        if nm else None)
+            self.V = M
+        else:
+            if split is not None:
+                raise ValueError("a sequence split takes no padding mask")
+            nv = [len(v) for v in valid]
+            pcount = [n_all - n for n_all, n in zip(lengths, nv)]
+            cu = np.zeros(B + 1, dtype=np.int64)
+            cu[1:] = np.cumsum([nm + n for n in nv])
+            V = int(cu[-1])
+            cu_p = np.zeros(B + 1, dtype=np.int64)
+            cu_p[1:] = np.cumsum(pcount)
+            row_batch = np.empty(M, dtype=np.int32)
+            row_pos = np.empty(M, dtype=np.int32)
+            lat_rows = np.empty(R, dtype=np.int32)
+            mem_rows = []
+            for b in range(B):
+                vi = np.asarray(valid[b], dtype=np.int64)
+                pi = np.setdiff1d(np.arange(lengths[b]), vi)
+                r0, r1 = int(cu[b]), int(cu[b + 1])
+                row_batch[r0:r1] = b
+                row_pos[r0:r0 + nm] = np.arange(nm)
+                row_pos[r0 + nm:r1] = nm + vi
+                lat_rows[self.lat_off[b] + vi] = r0 + nm + np.arange(len(vi))
+                p0, p1 = V + int(cu_p[b]), V + int(cu_p[b + 1])
+                row_batch[p0:p1] = b
+                row_pos[p0:p1] = nm + pi
+                lat_rows[self.lat_off[b] + pi] = p0 + np.arange(len(pi))
+                mem_rows.append(np.arange(r0, r0 + nm, dtype=np.int64))
+            mem_rows = np.concatenate(mem_rows) if nm else None
+            self.V = V
+            self.uniform_n = 0
+            self.max_n = nm + max(nv)
+            self.max_pad = max(pcount)
+            self.cu_pad = torch.from_numpy(cu_p.astype(np.int32)).to(dev)
         self.cu_host = cu
-        row_batch = np.repeat(np.arange(B, dtype=np.int32), Ns)
-        row_pos = np.concatenate([pos0 + np.arange(n, dtype=np.int32) for n in Ns])
-        lat_rows = np.concatenate([np.arange(cu[b] + nm, cu[b + 1], dtype=np.int32) for b in range(B)])
-        mem_rows = np.concatenate([np.arange(cu[b], cu[b] + nm, dtype=np.int64) for b in range(B)]) if nm else None
         self.cu = torch.from_numpy(cu.astype(np.int32)).to(dev)
         self.cu_ctx = torch.arange(0, (B + 1) * Tc, max(Tc, 1), dtype=torch.int32, device=dev)[:B + 1] if Tc else None
         self.row_batch = torch.from_numpy(row_batch).to(dev)
         self.row_pos = torch.from_numpy(row_pos).to(dev)
         self.lat_rows = torch.from_numpy(lat_rows).to(dev)
-        self.lat_off = [int(x) for x in np.concatenate([[0], np.cumsum(lengths)])]
         self.mem_rows = torch.from_numpy(mem_rows).to(dev) if nm else None
         bf = torch.bfloat16
         self.h = torch.empty(M, D, device=dev, dtype=torch.float32)  # fp32 residual stream
@@ -124,7 +171,10 @@ class _Workspace:
                 raise ValueError("a sequence split needs sequences of one length")
             self.halo_e = split.halo_left + Ns[0] + split.halo_right
             self.qkv_ext = torch.empty(B * self.halo_e, nq * D, device=dev, dtype=bf)
-        self.o = torch.empty(M, D, device=dev, dtype=bf)
+        # self-attention output; with a padding mask its padded rows stay zero (no attention writes them) and
+        # cross-attention writes a buffer of its own
+        self.o = torch.zeros(M, D, device=dev, dtype=bf) if self.masked else torch.empty(M, D, device=dev, dtype=bf)
+        self.ox = torch.empty(M, D, device=dev, dtype=bf) if self.masked else self.o
         self.o8 = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
         self.qx = torch.empty(M, (2 if cfg.differential else 1) * D, device=dev, dtype=bf)
         self.kv = torch.empty(max(B * Tc, 1), (3 if cfg.differential else 2) * D, device=dev, dtype=bf)
@@ -259,13 +309,15 @@ class DiTEngine:
             return Lin(wq.to(self.dev).contiguous(), s.to(self.dev), bias, True)
         return Lin(w.to(self.dev, torch.bfloat16).contiguous(), None, bias, False)
 
-    def _workspace(self, lengths, Tc, split=None) -> _Workspace:
+    def _workspace(self, lengths, Tc, split=None, valid=None) -> _Workspace:
         ws = self.ws
-        if ws is None or (ws.lengths, ws.Tc, ws.split) != (tuple(lengths), Tc, split):
+        vkey = None if valid is None else tuple(np.asarray(v, dtype=np.int64).tobytes() for v in valid)
+        if ws is None or (ws.lengths, ws.Tc, ws.split, ws.valid_key) != (tuple(lengths), Tc, split, vkey):
             self.ws = ws = None
             self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k,
                                       local_all=self.loc1_all is not None, split=split,
-                                      kv_all=self.kv_all is not None)
+                                      kv_all=self.kv_all is not None, valid=valid)
+            ws.valid_key = vkey
         if self.rope is None or self.rope.shape[0] < ws.max_pos:
             self.rope = ops.rope_table(ws.max_pos, 32, device=self.dev)
         return ws
@@ -281,20 +333,22 @@ class DiTEngine:
         return ops.gemm(x, lin.w, out, a_scale=x_scale if lin.fp8 else None, b_scale=lin.scale, bias=lin.bias, **kw)
 
     def _norm_to_a(self, ws, x, gamma, slot, mod=None, scale_off=0, shift_off=0):
-        """RMSNorm(+modulate) of the stream into ws.a; FP8: two passes (amax, quantize)."""
+        """RMSNorm(+modulate) of the first x.shape[0] stream rows into ws.a; FP8: two passes (amax, quantize)."""
         cfg = self.cfg
+        rows = x.shape[0]
+        a = ws.a[:rows]
         if ws.uniform_n:
             kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, rows_per_batch=ws.uniform_n)
         else:
-            kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, row_batch=ws.row_batch)
+            kw = dict(mod=mod, scale_off=scale_off, shift_off=shift_off, row_batch=ws.row_batch[:rows])
         if self.fp8:
             am = ws.amax[slot:slot + 1]
             sc = ws.scale[slot:slot + 1]
             ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, **kw)
-            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=ws.a, quant_amax=am, scale_out=sc, **kw)
-            return ws.a, sc
-        ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=ws.a, **kw)
-        return ws.a, None
+            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, quant_amax=am, scale_out=sc, **kw)
+            return a, sc
+        ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, **kw)
+        return a, None
 
     def _quant(self, ws, x, out8, slot):
         """FP8: quantize x (whose amax is already in slot) into out8; bf16: pass x through."""
@@ -366,8 +420,10 @@ class DiTEngine:
 
     @torch.no_grad()
     def forward(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, cfg_scale: float = 1.0,
-                apg_scale: float = 1.0):
-        """DiffusionTransformer.forward for the rf_denoiser objective (dit.py:345-643)."""
+                apg_scale: float = 1.0, padding_mask=None):
+        """DiffusionTransformer.forward for the rf_denoiser objective (dit.py:345-643). padding_mask [B, L] bool
+        (True = valid latent) selects the reference's varlen semantics; both CFG halves share it (dit.py:549-550)
+        and the APG projection is restricted to valid positions (dit.py:311-343)."""
         dev = self.dev
         x = x.to(dev)
         t = t.to(dev, torch.float32)
@@ -378,17 +434,22 @@ class DiTEngine:
             bc = torch.cat([cc, torch.zeros_like(cc)])
             bg = torch.cat([global_embed, global_embed]).to(dev) if global_embed is not None else None
             bl = torch.cat([local_add_cond, local_add_cond]).to(dev) if local_add_cond is not None else None
-            out = self.inner(bx, bt, bc, bg, bl)
-            return self.cfg_combine(x, t, out, cfg_scale, apg_scale)
-        return self.inner(x, t, cross_attn_cond, global_embed, local_add_cond)
+            bm = torch.cat([padding_mask, padding_mask]) if padding_mask is not None else None
+            out = self.inner(bx, bt, bc, bg, bl, padding_mask=bm)
+            return self.cfg_combine(x, t, out, cfg_scale, apg_scale, padding_mask)
+        return self.inner(x, t, cross_attn_cond, global_embed, local_add_cond, padding_mask=padding_mask)
 
     def graphed(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, cfg_scale: float = 1.0,
-                apg_scale: float = 1.0) -> "GraphedStep":
-        """Capture one forward at these shapes into a CUDA graph (inputs are copied into static buffers)."""
-        return GraphedStep(self, (x, t, cross_attn_cond, global_embed, local_add_cond), cfg_scale, apg_scale)
+                apg_scale: float = 1.0, padding_mask=None) -> "GraphedStep":
+        """Capture one forward at these shapes into a CUDA graph (inputs are copied into static buffers). The
+        padding mask is part of what is captured (it fixes the row layout); replays use the same mask."""
+        return GraphedStep(self, (x, t, cross_attn_cond, global_embed, local_add_cond), cfg_scale, apg_scale,
+                           padding_mask)
 
-    def cfg_combine(self, x, t, out, cfg_scale, apg_scale):
-        """CFG + APG for rf_denoiser (dit.py:571-625; apg_project dit.py:311-343), fp32."""
+    def cfg_combine(self, x, t, out, cfg_scale, apg_scale, padding_mask=None):
+        """CFG + APG for rf_denoiser (dit.py:571-625; apg_project dit.py:311-343), fp32. With a padding mask the
+        projection direction is cond_den on valid positions (norm floored at 1e-8) and the orthogonal part is
+        zero on padded positions."""
         x = x.float()
         cond_out, uncond_out = out.float().chunk(2)
         sigma = t.float()[:, None, None]
@@ -396,21 +457,46 @@ class DiTEngine:
         diff = (uncond_out - cond_out) * sigma  # cond_den - uncond_den
         if apg_scale == 0.0:
             cfg_diff = diff
-        else:
+        elif padding_mask is None:
             v1 = cond_den / cond_den.flatten(1).norm(dim=1).clamp_min(1e-12)[:, None, None]
             par = (diff * v1).sum(dim=(1, 2), keepdim=True) * v1
             orth = diff - par
             cfg_diff = orth if apg_scale == 1.0 else apg_scale * orth + (1 - apg_scale) * diff
+        else:
+            mask = padding_mask.to(x.device)[:, None, :].float()
+            v1 = cond_den * mask
+            v1 = v1 / v1.flatten(1).norm(dim=1).clamp_min(1e-8)[:, None, None]
+            orth = (diff - (diff * v1).sum(dim=(1, 2), keepdim=True) * v1) * mask
+            cfg_diff = orth if apg_scale == 1.0 else apg_scale * orth + (1 - apg_scale) * diff
         cfg_den = cond_den + (cfg_scale - 1) * cfg_diff
         return (x - cfg_den) / sigma
 
+    def _valid_latents(self, padding_mask, B: int, L: int):
+        """Host-side list of each sequence's valid latent indices, or None when every latent is valid (the
+        unmasked path computes the same thing). Reading the mask is the one host sync the mask costs, as the
+        reference's own varlen metadata does (transformer.py:57-58). Under CUDA-graph capture the mask cannot
+        be read: the warm-up forward that precedes every capture has laid out the workspace for it."""
+        if padding_mask is None:
+            return None
+        if torch.cuda.is_current_stream_capturing():
+            if self.ws is None or self.ws.lengths != tuple([L] * B):
+                raise RuntimeError("padding_mask under graph capture needs a warm-up forward with the same mask")
+            return self.ws.valid
+        pm = padding_mask.detach().to("cpu", torch.bool)
+        if tuple(pm.shape) != (B, L):
+            raise ValueError(f"padding_mask must be [{B}, {L}], got {tuple(pm.shape)}")
+        if bool(pm.all()):
+            return None
+        return [np.nonzero(pm[b].numpy())[0] for b in range(B)]
+
     @torch.no_grad()
-    def inner(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None):
+    def inner(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None, padding_mask=None):
         """DiffusionTransformer._forward + ContinuousTransformer.forward on the kernels for B sequences of one
-        length; returns fp32 [B, C, L]."""
+        length; returns fp32 [B, C, L]. padding_mask [B, L] bool (True = valid latent) as in
+        ContinuousTransformer.forward (transformer.py:1213-1232)."""
         B, C, L = x.shape
         Tc = cross_attn_cond.shape[1] if cross_attn_cond is not None else 0
-        ws = self._workspace([L] * B, Tc)
+        ws = self._workspace([L] * B, Tc, valid=self._valid_latents(padding_mask, B, L))
         ws.xin.view(B, L, C).copy_(x.transpose(1, 2))
         if local_add_cond is not None and self.cfg.local_add_cond_dim > 0:
             ws.loc.view(B, L, -1)[:, :, :self.cfg.local_add_cond_dim].copy_(local_add_cond.transpose(1, 2))
@@ -532,12 +618,15 @@ class DiTEngine:
                 self._gemm(a, ln[p + "self_attn.to_qkv"], qkv, x_scale=asc, kind=_lib.EPI_QK_NORM,
                            qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
                                    row_pos=ws.row_pos))
+                # varlen over the sequences' rows; with a padding mask only the valid rows [0, V) attend and
+                # are attended, and the padded rows' output stays zero (pad_input, transformer.py:650)
+                sq = qkv[:ws.V]
                 if diff:
-                    ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],
-                                  k2=qkv[:, 4 * D:5 * D], heads=H, window=(wl, wr), out=o, amax_out=am1, **seq)
+                    ops.attention(sq[:, 0:D], sq[:, D:2 * D], sq[:, 2 * D:3 * D], q2=sq[:, 3 * D:4 * D],
+                                  k2=sq[:, 4 * D:5 * D], heads=H, window=(wl, wr), out=o[:ws.V], amax_out=am1, **seq)
                 else:
-                    ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H, window=(wl, wr),
-                                  out=o, amax_out=am1, **seq)
+                    ops.attention(sq[:, 0:D], sq[:, D:2 * D], sq[:, 2 * D:3 * D], heads=H, window=(wl, wr),
+                                  out=o[:ws.V], amax_out=am1, **seq)
             oa, osc = self._quant(ws, o, ws.o8, s0 + 1)
             self._gemm(oa, ln[p + "self_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
                        gate=ssi[:, 2 * D:3 * D], row_batch=rb)
@@ -559,12 +648,19 @@ class DiTEngine:
                     kc = [kv[:, 0:D], kv[:, D:2 * D]] if diff else [kv[:, 0:D]]
                     vc = kv[:, 2 * D:3 * D] if diff else kv[:, D:2 * D]
                 am = ws.amax[s0 + 3:s0 + 4] if self.fp8 else None
-                if diff:
-                    ops.attention(qx[:, 0:D], kc[0], vc, q2=qx[:, D:2 * D], k2=kc[1], heads=H, out=o, amax_out=am,
-                                  **xseq)
-                else:
-                    ops.attention(qx, kc[0], vc, heads=H, out=o, amax_out=am, **xseq)
-                oa, osc = self._quant(ws, o, ws.o8, s0 + 3)
+                ox = ws.ox
+                # with a padding mask the rows of a sequence sit in two segments (valid rows, then padded rows);
+                # both attend over the whole context, as the reference's unmasked cross-attention does
+                segs = [(0, ws.V, xseq)]
+                if ws.V < ws.M:
+                    segs.append((ws.V, ws.M, dict(xseq, cu_seqlens_q=ws.cu_pad, max_seqlen_q=ws.max_pad)))
+                for r0, r1, kw in segs:
+                    if diff:
+                        ops.attention(qx[r0:r1, 0:D], kc[0], vc, q2=qx[r0:r1, D:2 * D], k2=kc[1], heads=H,
+                                      out=ox[r0:r1], amax_out=am, **kw)
+                    else:
+                        ops.attention(qx[r0:r1], kc[0], vc, heads=H, out=ox[r0:r1], amax_out=am, **kw)
+                oa, osc = self._quant(ws, ox, ws.o8, s0 + 3)
                 self._gemm(oa, ln[p + "cross_attn.to_out"], h, x_scale=osc, kind=_lib.EPI_RESIDUAL, residual=h)
             # -- local additive conditioning, left-padded over the memory tokens (transformer.py:978-994, 77-88)
             if has_local and (p + "to_local_embed.0") in ln:
@@ -574,13 +670,16 @@ class DiTEngine:
                     t1 = self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
                 self._gemm(t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h,
                            out_row_map=ws.lat_rows)
-            # -- feed-forward with adaLN (transformer.py:1042-1049)
-            f, fsc = self._norm_to_a(ws, h, self.gam[p + "ff_norm.gamma"], s0 + 4, ssi, 3 * D, 4 * D)
-            self._gemm(f, ln[p + "ff.ff.0.proj"], ws.u, x_scale=fsc, kind=_lib.EPI_SWIGLU,
+            # -- feed-forward with adaLN (transformer.py:1042-1049); with a padding mask only the valid rows
+            # [0, V) (transformer.py:500-519: padded rows get a zero FF branch, so they are left as they are)
+            V = ws.V
+            hv = h[:V]
+            f, fsc = self._norm_to_a(ws, hv, self.gam[p + "ff_norm.gamma"], s0 + 4, ssi, 3 * D, 4 * D)
+            self._gemm(f, ln[p + "ff.ff.0.proj"], ws.u[:V], x_scale=fsc, kind=_lib.EPI_SWIGLU,
                        amax_out=ws.amax[s0 + 5:s0 + 6] if self.fp8 else None)
-            ua, usc = self._quant(ws, ws.u, ws.u8, s0 + 5)
-            self._gemm(ua, ln[p + "ff.ff.2"], h, x_scale=usc, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
-                       gate=ssi[:, 5 * D:6 * D], row_batch=rb)
+            ua, usc = self._quant(ws, ws.u[:V], None if ws.u8 is None else ws.u8[:V], s0 + 5)
+            self._gemm(ua, ln[p + "ff.ff.2"], hv, x_scale=usc, kind=_lib.EPI_GATED_RESIDUAL, residual=hv,
+                       gate=ssi[:, 5 * D:6 * D], row_batch=rb[:V])
 
         # ---- drop memory tokens, project_out (postprocess conv folded) (transformer.py:1265-1267, dit.py:297-304)
         ops.convert(h, ws.hb, src_rows=ws.lat_rows)
@@ -594,19 +693,23 @@ class GraphedStep:
     sa3_trt_core.py:511-694): all kernel launches of the step replay with no host work.
     """
 
-    def __init__(self, engine: DiTEngine, inputs, cfg_scale: float, apg_scale: float):
+    def __init__(self, engine: DiTEngine, inputs, cfg_scale: float, apg_scale: float, padding_mask=None):
         self.engine = engine
         self.static = [None if a is None else a.to(engine.dev).clone() for a in inputs]
         self.cfg_scale, self.apg_scale = cfg_scale, apg_scale
+        self.padding_mask = None if padding_mask is None else padding_mask.to(engine.dev).clone()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(2):
-                engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale)
+                engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale, padding_mask=self.padding_mask)
         torch.cuda.current_stream().wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.out = engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale)
+            self.out = engine.forward(*self.static, cfg_scale=cfg_scale, apg_scale=apg_scale,
+                                      padding_mask=self.padding_mask)
+        # the graph replays into these buffers: keep them alive even after the engine switches to another shape
+        self.workspace, self.rope = engine.ws, engine.rope
 
     def __call__(self, x, t, cross_attn_cond=None, global_embed=None, local_add_cond=None) -> torch.Tensor:
         for dst, src in zip(self.static, (x, t, cross_attn_cond, global_embed, local_add_cond)):

@@ -191,24 +191,35 @@ class DiffusionTransformer(nn.Module):
     def forward(self, x, t, cross_attn_cond=None, cross_attn_cond_mask=None, negative_cross_attn_cond=None,
                 negative_cross_attn_mask=None, input_concat_cond=None, local_add_cond=None, global_embed=None,
                 cfg_scale: float = 1.0, apg_scale: float = 1.0, padding_mask=None, **kwargs):
+        cfg_interval = kwargs.pop("cfg_interval", (0, 1))
         unsupported = {k: v for k, v in dict(negative_cross_attn_cond=negative_cross_attn_cond,
-                                             input_concat_cond=input_concat_cond, padding_mask=padding_mask,
-                                             **kwargs).items() if v is not None and v is not False}
+                                             input_concat_cond=input_concat_cond, **kwargs).items()
+                       if v is not None and v is not False}
         for k in ("cfg_dropout_prob", "scale_phi", "cfg_norm_threshold"):
             if unsupported.get(k, 0) in (0, 0.0):
                 unsupported.pop(k, None)
-        unsupported.pop("cfg_interval", None)
         if unsupported:
             raise NotImplementedError(f"arguments not supported on the B200 path: {sorted(unsupported)}")
+        if cfg_scale != 1.0 and tuple(cfg_interval) != (0, 1):
+            # CFG applies only while cfg_interval[0] <= sigma[0] <= cfg_interval[1] (dit.py:479), sigma = t
+            s0 = float(t.reshape(-1)[0])
+            if not (cfg_interval[0] <= s0 <= cfg_interval[1]):
+                cfg_scale = 1.0
+        if padding_mask is not None:
+            padding_mask = padding_mask.bool()
         if self._graphs is not None:
             args = (x, t, cross_attn_cond, global_embed, local_add_cond)
-            key = (tuple(None if a is None else tuple(a.shape) for a in args), float(cfg_scale), float(apg_scale))
+            mkey = None if padding_mask is None else padding_mask.cpu().numpy().tobytes()
+            key = (tuple(None if a is None else tuple(a.shape) for a in args), float(cfg_scale), float(apg_scale),
+                   mkey)
             g = self._graphs.get(key)
             if g is None:
-                g = self._graphs[key] = self.engine().graphed(*args, cfg_scale=cfg_scale, apg_scale=apg_scale)
+                g = self._graphs[key] = self.engine().graphed(*args, cfg_scale=cfg_scale, apg_scale=apg_scale,
+                                                              padding_mask=padding_mask)
             return g(*args).clone()
         return self.engine().forward(x, t, cross_attn_cond=cross_attn_cond, global_embed=global_embed,
-                                     local_add_cond=local_add_cond, cfg_scale=cfg_scale, apg_scale=apg_scale)
+                                     local_add_cond=local_add_cond, cfg_scale=cfg_scale, apg_scale=apg_scale,
+                                     padding_mask=padding_mask)
 
 
 def init_synthetic_(module: nn.Module, seed: int = 0, std: float = 0.02) -> nn.Module:

@@ -29,6 +29,13 @@ CASES = {
                             cfg_scale=1.0, apg_scale=1.0),
     # the reference's chunked-halo SDPA over several 1024-query chunks
     "attn_halo_n2500": dict(kind="attn", seed=6, B=1, H=2, N=2500, window=(256, 256), rows_every=5),
+    # padding_mask as StableAudioModel.generate passes it (valid latent prefix per prompt), through the
+    # reference's flash-varlen call sites: two prompts (one padded, one full), CFG + full APG
+    "dit_small_cfg_mask": dict(kind="dit_mask", seed=7, B=2, L=200, Tc=16, cfg=_small, cfg_scale=5.0,
+                               apg_scale=1.0, valid=[137, 200]),
+    # standard attention, blended APG (the unmasked diff enters the combine), one prompt padded to 90 of 160
+    "dit_small_std_mask": dict(kind="dit_mask", seed=8, B=1, L=160, Tc=12, cfg=replace(_small, differential=False),
+                               cfg_scale=6.0, apg_scale=0.5, valid=[90]),
 }
 
 
@@ -54,6 +61,12 @@ def dit_inputs(case):
     gemb = torch.randn(B, cfg.global_cond_dim, generator=g)
     loc = torch.randn(B, cfg.local_add_cond_dim, L, generator=g) * 0.5
     return x, t, cond, gemb, loc
+
+
+def dit_padding_mask(case):
+    """[B, L] bool, True on each prompt's first `valid` latents (create_padding_mask_from_lengths,
+    stable_audio_3/data/utils.py:195-212)."""
+    return torch.arange(case["L"])[None, :] < torch.tensor(case["valid"])[:, None]
 
 
 def attn_inputs(case):

@@ -9,10 +9,15 @@ is amplified there: the reference's OWN bf16 module deviates from its fp32 modul
 `dit_small_cfg` (cfg 5) and by 8.8e-2 at medium width with cfg 7. Parity is therefore asserted
   * on the network's velocity prediction for both CFG halves (batched forward, before the combine),
   * on the combine itself given identical network outputs (fp32, ~exact),
-  * on the full CFG velocity for the bf16 path (2e-2), and for the FP8 path against a 5e-2 bound
-    (the FP8 definition alone moves the fp32 velocity by 2.7e-2 on this case).
+  * on the full CFG velocity (2e-2) for the bf16 path against the fp32 oracle and for the FP8 path against the
+    FP8 definition evaluated at the bf16 deployment's activations (oracle Cfg.act_bf16). e4m3 rounding is
+    discontinuous: an activation that moves by a bf16 ulp crosses an e4m3 rounding boundary with probability
+    ~ulp/spacing and then jumps by a whole e4m3 step, so the fp32-activation definition itself sits 2.6e-2
+    (velocity, dit_small_cfg) to 2.7e-2 (one medium block, network output) away from the bf16-activation one.
+    The distance to the fp32-activation definition is printed beside each FP8 result.
 """
 import os
+from dataclasses import replace
 
 import numpy as np
 import pytest
@@ -55,13 +60,15 @@ def test_network_velocity_matches_oracle(cuda, name, mode):
     case = CASES[name]
     m = _model(case, mode, round_bf16=(mode == "bf16"))
     inputs = _batched_inputs(case)
+    ocfg = replace(_cfg(case["cfg"]), act_bf16=(mode == "fp8"))
     with torch.inference_mode():
         lin = odit.Linears(m.state_dict(), "fp8" if mode == "fp8" else "fp32")
-        ref = odit.dit_inner_forward(lin, m.state_dict(), _cfg(case["cfg"]), *inputs)
+        ref = odit.dit_inner_forward(lin, m.state_dict(), ocfg, *inputs)
         out = m.engine().inner(*(a.to(cuda) for a in inputs))
     torch.cuda.synchronize()
     assert torch.isfinite(out).all()
     err = rel_l2(out, ref)
+    print(f"{name} {mode}: network velocity rel L2 {err:.3e}")
     assert err < 2e-2, err
 
 
@@ -91,18 +98,25 @@ def test_velocity_bf16_matches_oracle(cuda, name):
     assert err < 2e-2, err
 
 
-@pytest.mark.parametrize("name,bound", [("dit_small_cfg", 5e-2), ("dit_small_nocfg", 2e-2)])
-def test_velocity_fp8_matches_oracle(cuda, name, bound):
+@pytest.mark.parametrize("name", ["dit_small_cfg", "dit_small_nocfg"])
+def test_velocity_fp8_matches_oracle(cuda, name):
+    """The full FP8 velocity (CFG/APG combine included) vs the FP8 definition at the bf16 deployment's
+    activations: <= 2e-2. Printed beside it: the distance to the fp32-activation FP8 definition and, for scale,
+    the reference's own bf16-vs-fp32 distance on the same case (from the golden fixture)."""
     case = CASES[name]
     m = _model(case, "fp8", round_bf16=False)
     x, t, cond, gemb, loc = dit_inputs(case)
+    kw = (x, t, cond, gemb, loc, case["cfg_scale"], case["apg_scale"])
     with torch.inference_mode():
-        ref = odit.dit_forward(m.state_dict(), _cfg(case["cfg"]), x, t, cond, gemb, loc, case["cfg_scale"],
-                               case["apg_scale"], mode="fp8")
+        ref = odit.dit_forward(m.state_dict(), replace(_cfg(case["cfg"]), act_bf16=True), *kw, mode="fp8")
+        ref32 = odit.dit_forward(m.state_dict(), _cfg(case["cfg"]), *kw, mode="fp8")
         out = m(x.to(cuda), t.to(cuda), cross_attn_cond=cond.to(cuda), global_embed=gemb.to(cuda),
                 local_add_cond=loc.to(cuda), cfg_scale=case["cfg_scale"], apg_scale=case["apg_scale"])
     err = rel_l2(out, ref)
-    assert err < bound, err
+    ref_bf16 = float(np.load(os.path.join(HERE, f"{name}.npz"))["ref_bf16_rel"])
+    print(f"{name}: FP8 CFG velocity rel L2 {err:.3e} (vs fp32-activation FP8 definition {rel_l2(out, ref32):.3e}; "
+          f"reference bf16 vs fp32 {ref_bf16:.3e})")
+    assert err < 2e-2, err
 
 
 @pytest.mark.parametrize("name", ["dit_small_cfg", "dit_small_nocfg"])

@@ -1,21 +1,31 @@
-"""Variable-length packed batches on a B200: prompts of different lengths packed back to back (no padding)
-give the same network output as running each prompt on its own (bf16: <= 1e-3; the kernels compute each
-row independently of the others, so only the packing tables differ), and the FP8 path (whose per-tensor
-activation scales span the packed batch) stays within 2e-2."""
+"""Variable-length packed batches on a B200: prompts of different lengths packed back to back (no padding).
+
+  * bf16: each packed prompt's network output equals running that prompt on its own (<= 1e-3; the kernels
+    compute each row independently of the others, so only the packing tables differ).
+  * FP8: the per-tensor activation scales span the packed batch, so a prompt's quantization grid depends on its
+    batch-mates; the packed network output is checked against the oracle's packed restatement
+    (dit_inner_forward_packed, FP8 definition at the bf16 deployment's activations), and each prompt's CFG/APG
+    velocity against the oracle's combine of those outputs: <= 2e-2 each.
+"""
+from dataclasses import replace
+
 import pytest
 import torch
 
+from oracle import dit as odit
 from tests.golden.cases import CASES
+from tests.test_oracle_golden import _cfg
 
 pytestmark = pytest.mark.gpu
 
 
 def rel(a, b):
-    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm()).item()
 
 
-@pytest.mark.parametrize("mode,tol", [("bf16", 1e-3), ("fp8", 2e-2)])
-def test_varlen_matches_per_prompt(cuda, mode, tol):
+@pytest.mark.parametrize("mode", ["bf16", "fp8"])
+def test_varlen_matches_per_prompt(cuda, mode):
     from sa3_b200.modules import DiffusionTransformer, init_synthetic_
 
     cfg = CASES["dit_small_cfg"]["cfg"]
@@ -24,19 +34,38 @@ def test_varlen_matches_per_prompt(cuda, mode, tol):
     g = torch.Generator().manual_seed(3)
     lens = [100, 257, 40]
     P = len(lens)
-    xs = [torch.randn(256, L, generator=g).to(cuda) for L in lens]
-    locs = [torch.randn(257, L, generator=g).to(cuda) * 0.5 for L in lens]
-    t = (torch.rand(P, generator=g) * 0.8 + 0.1).to(cuda)
-    cond = torch.randn(P, 16, 768, generator=g).to(cuda)
-    gemb = torch.randn(P, 768, generator=g).to(cuda)
+    xs = [torch.randn(256, L, generator=g) for L in lens]
+    locs = [torch.randn(257, L, generator=g) * 0.5 for L in lens]
+    t = torch.rand(P, generator=g) * 0.8 + 0.1
+    cond = torch.randn(P, 16, 768, generator=g)
+    gemb = torch.randn(P, 768, generator=g)
+    d = lambda a: a.to(cuda)  # noqa: E731
     with torch.inference_mode():
-        packed = [o.clone() for o in eng.inner_varlen(xs, t, cond, gemb, locs)]
-        for i in range(P):
-            single = eng.inner(xs[i][None], t[i:i + 1], cond[i:i + 1], gemb[i:i + 1], locs[i][None])[0].clone()
-            assert rel(packed[i], single) < tol, i
-        v = eng.forward_varlen(xs, t, cond, gemb, locs, cfg_scale=5.0, apg_scale=1.0)
-        for i in range(P):
-            vi = eng.forward(xs[i][None], t[i:i + 1], cond[i:i + 1], gemb[i:i + 1], locs[i][None], 5.0, 1.0)[0]
-            assert torch.isfinite(v[i]).all()
-            if mode == "bf16":
+        packed = [o.clone() for o in eng.inner_varlen([d(x) for x in xs], d(t), d(cond), d(gemb),
+                                                      [d(lc) for lc in locs])]
+        v = eng.forward_varlen([d(x) for x in xs], d(t), d(cond), d(gemb), [d(lc) for lc in locs], cfg_scale=5.0,
+                               apg_scale=1.0)
+        if mode == "bf16":
+            for i in range(P):
+                single = eng.inner(d(xs[i])[None], d(t[i:i + 1]), d(cond[i:i + 1]), d(gemb[i:i + 1]),
+                                   d(locs[i])[None])[0]
+                assert rel(packed[i], single) < 1e-3, i
+                vi = eng.forward(d(xs[i])[None], d(t[i:i + 1]), d(cond[i:i + 1]), d(gemb[i:i + 1]),
+                                 d(locs[i])[None], 5.0, 1.0)[0]
                 assert rel(v[i], vi) < 1e-3, i
+            return
+        sd = m.state_dict()
+        lin = odit.Linears(sd, "fp8")
+        ocfg = replace(_cfg(cfg), act_bf16=True)
+        ref = odit.dit_inner_forward_packed(lin, sd, ocfg, xs, t, cond, gemb, locs)
+        # both CFG halves of every prompt in one packed batch (cond halves first), as forward_varlen runs them
+        zc = torch.zeros_like(cond)
+        ref2 = odit.dit_inner_forward_packed(lin, sd, ocfg, xs + xs, torch.cat([t, t]), torch.cat([cond, zc]),
+                                             torch.cat([gemb, gemb]), locs + locs)
+    for i in range(P):
+        e_net = rel(packed[i], ref[i])
+        vref = odit.cfg_combine(xs[i][None], t[i:i + 1], torch.stack([ref2[i], ref2[P + i]]), 5.0, 1.0)[0]
+        e_v = rel(v[i], vref)
+        print(f"prompt {i} (L={lens[i]}): FP8 packed network rel L2 {e_net:.3e}, CFG velocity {e_v:.3e}")
+        assert e_net < 2e-2, i
+        assert e_v < 2e-2, i
