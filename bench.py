@@ -165,60 +165,139 @@ def make_inputs(wl, cfg, seed, device):
 
 
 # ----------------------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_block_sample(wl, threads: int, tokens: int = 0):
-    """Time the oracle's fp32 restatement of one block (FP8 fake-quant linears for the FP8 workload)
-    over `tokens` tokens of one sequence (default: the full L + 64) on the host cores. Every op of a
-    block with a fixed window is linear in the token count, so the sample is scaled by
-    (L + 64) / tokens, x depth blocks, x 2 CFG halves. Returns (seconds per full step, seconds measured)."""
+_CPU_MODEL = {}
+
+
+def cpu_dit_sample(wl, threads: int, latents: int = 0):
+    """Time the oracle's fp32 restatement of a one-block DiT forward (prologue MLPs, project_in, one full
+    block with self- and cross-attention, local conditioning and FF, project_out) for ONE sequence of
+    `latents` latents (default: the workload's full L) on the host cores. FP8 workloads use the oracle's
+    FP8 definition (fake-quantized activations, e4m3 weights); GPTQ and bf16 workloads use fp32 linears
+    (the dequantised GPTQ weight costs the same GEMM). A step is `depth` blocks over 2 CFG halves per
+    prompt, so the sample is scaled by depth x 2 x prompts x L / latents (the prologue and projections
+    are a few percent of one block, and are counted once per block: the figure errs on the slow side).
+    Returns (seconds per full step, seconds measured, latents)."""
     from oracle import dit as odit
-    from sa3_b200.modules import TransformerBlock, init_synthetic_
+    from sa3_b200.modules import DiffusionTransformer, init_synthetic_, with_depth
     torch.set_num_threads(threads)
     cfg = model_cfg(wl["model"])
-    oc = odit.Cfg(embed_dim=cfg.embed_dim, depth=1, num_heads=cfg.num_heads, differential=cfg.differential,
-                  sliding_window=cfg.sliding_window, local_add_cond_dim=0, cond_token_dim=0)
-    blk = init_synthetic_(TransformerBlock(cfg, cross_attend=False), seed=0)
-    sd = {"L." + k: v.float() for k, v in blk.state_dict().items()}
-    N_full = wl["L"] + cfg.num_memory_tokens
-    N = min(tokens, N_full) if tokens else N_full
-    g = torch.Generator().manual_seed(1)
-    x = torch.randn(1, N, cfg.embed_dim, generator=g)
-    g6 = torch.randn(1, 6 * cfg.embed_dim, generator=g) * 0.5
+    key = wl["model"]
+    if key not in _CPU_MODEL:
+        sd = init_synthetic_(DiffusionTransformer(with_depth(cfg, 1)), seed=0).state_dict()
+        _CPU_MODEL[key] = {k: v.float() for k, v in sd.items()}
+    sd = _CPU_MODEL[key]
     mode = "fp8" if wl["mode"] == "fp8" else "fp32"
+    if (key, mode) not in _CPU_MODEL:  # weights are quantized once, as a deployed CPU path would keep them
+        _CPU_MODEL[(key, mode)] = odit.Linears(sd, mode)
+    lin = _CPU_MODEL[(key, mode)]
+    oc = odit.Cfg(io_channels=cfg.io_channels, embed_dim=cfg.embed_dim, depth=1, num_heads=cfg.num_heads,
+                  cond_token_dim=cfg.cond_token_dim, global_cond_dim=cfg.global_cond_dim,
+                  local_add_cond_dim=cfg.local_add_cond_dim, num_memory_tokens=cfg.num_memory_tokens,
+                  sliding_window=cfg.sliding_window, differential=cfg.differential, ff_mult=cfg.ff_mult)
+    n = min(latents, wl["L"]) if latents else wl["L"]
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1, cfg.io_channels, n, generator=g)
+    t = torch.full((1,), 0.5)
+    cond = torch.randn(1, wl["Tc"], cfg.cond_token_dim, generator=g)
+    gemb = torch.randn(1, cfg.global_cond_dim, generator=g)
+    loc = torch.zeros(1, cfg.local_add_cond_dim, n)
     with torch.inference_mode():
         t0 = time.perf_counter()
-        odit.block_only(sd, "L", oc, x, g6, mode=mode)
+        odit.dit_inner_forward(lin, sd, oc, x, t, cond, gemb, loc)
         dt = time.perf_counter() - t0
-    # one step = depth blocks x (cond + uncond) sequences; the cross-attention / local-cond / prologue
-    # work not in this sample is < 10% of a block and is left out (the figure is a lower bound on CPU time)
-    return dt * (N_full / N) * cfg.depth * 2 * wl.get("prompts", 1), dt
+    return dt * cfg.depth * 2 * wl.get("prompts", 1) * (wl["L"] / n), dt, n
+
+
+def _cpu_sample_text(wl, n, meas=None):
+    cfg = model_cfg(wl["model"])
+    lin = "FP8-definition" if wl["mode"] == "fp8" else "fp32"
+    m = f" ({meas:.1f} s measured)" if meas is not None else ""
+    scale = "" if n == wl["L"] else f" x{wl['L']}/{n} latents"
+    return (f"oracle fp32 one-block {wl['model']} DiT ({lin} linears; self+cross attention, local cond, FF, "
+            f"projections) over one sequence of {n} latents{m}, scaled x{cfg.depth} blocks x2 CFG halves"
+            f"{' x' + str(wl.get('prompts', 1)) + ' prompts' if wl.get('prompts', 1) > 1 else ''}{scale}")
+
+
+REFERENCE_SAMPLE_LATENTS = 2048
 
 
 def run_reference(args, wl, world, rank):
-    """The reference arm: the oracle port (the reference is Python; nothing compiles) on all host cores."""
+    """The reference arm: the oracle port (the reference is Python; nothing compiles) on all host cores.
+    Each step is a bounded sample: the one-block DiT over REFERENCE_SAMPLE_LATENTS latents."""
     if rank != 0:
         return
+    if "L" not in wl:
+        wl = dict(wl, L=8183, prompts=1)
     threads = len(os.sched_getaffinity(0))
     tokens = 2 * wl["L"] * wl.get("prompts", 1)
-    sample_tokens = 4096
     for _ in range(args.warmup):
-        cpu_block_sample(wl, threads, sample_tokens)
+        cpu_dit_sample(wl, threads, REFERENCE_SAMPLE_LATENTS)
     steps = []
+    n = REFERENCE_SAMPLE_LATENTS
     for _ in range(args.steps):
-        s, _dt = cpu_block_sample(wl, threads, sample_tokens)
-        steps.append(s)
+        s_step, _dt, n = cpu_dit_sample(wl, threads, REFERENCE_SAMPLE_LATENTS)
+        steps.append(s_step)
     step_s = statistics.median(steps)
     value = tokens / step_s
-    sample = (f"one {wl['model']} block ({wl['mode']} fake-quant linears, fp32) over {sample_tokens} tokens per "
-              f"step, scaled x(L+64)/{sample_tokens} x{model_cfg(wl['model']).depth} blocks x2 CFG halves")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "L": wl["L"], "prompts_per_gpu": wl.get("prompts", 1),
                    "parallelism": f"dp{world}"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": _cpu_sample_text(wl, n)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+# ----------------------------------------------------------------------------- peaks and rooflines
+def measured_fp8_peak(dev) -> tuple:
+    """Dense FP8 e4m3 GEMM throughput of the library path on this GPU (cuBLASLt through torch._scaled_mm,
+    8192^3, per-tensor scales, bf16 out), best of 10 with CUDA events: the FP8 counterpart of the driver's
+    measured cuBLAS bf16 figure. Returns (TFLOP/s, source text) or (None, reason)."""
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        f = lambda: torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)  # noqa: E731
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        best = float("inf")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(10):
+            e0.record()
+            f()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12, "measured here: torch._scaled_mm e4m3 8192^3 (cuBLASLt), best of 10"
+    except Exception as exc:  # an image without the FP8 library path
+        return None, f"fp8 library GEMM unavailable ({type(exc).__name__})"
+
+
+def band_pairs(n: int, wl: int, wr: int) -> int:
+    """Visible (query, key) pairs of a length-n sequence under a (wl, wr) band (negative = unbounded)."""
+    import numpy as np
+    i = np.arange(n)
+    hi = np.full(n, n - 1) if wr < 0 else np.minimum(n - 1, i + wr)
+    lo = np.zeros(n, dtype=np.int64) if wl < 0 else np.maximum(0, i - wl)
+    return int((hi - lo + 1).sum())
+
+
+def score_tiles(n: int, wl: int, wr: int, bm: int = 128, bn: int = 128) -> int:
+    """128 x 128 score tiles the attention kernel computes for one head of one length-n sequence: each
+    128-query tile visits the key tiles from its first visible key to its last (fully masked tiles skipped)."""
+    t = 0
+    for i0 in range(0, n, bm):
+        i1 = min(i0 + bm, n) - 1
+        lo = 0 if wl < 0 else max(0, i0 - wl)
+        hi = n if wr < 0 else min(n, i1 + wr + 1)
+        t += (hi - lo + bn - 1) // bn if hi > lo else 0
+    return t
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -401,9 +480,58 @@ def run_ours(args, wl, world, rank, local):
     h2d = sum(a.numel() * a.element_size() for a in (hx, ht, hc, hg, hl))
     d2h = out_host.numel() * out_host.element_size()
 
-    # ---- roofline of the dominant kernel: the FF GLU.proj GEMM (M=B*N, N=2*ff_inner, K=dim) with its SwiGLU
-    # epilogue, timed live with CUDA events on the launching stream, operands from the step's own buffers
+    peaks = _peaks()
+    bf16_peak, bf16_src = (peaks["bf16_tflops"], "measured bf16 burst (MEASURED_PEAKS.json)") if peaks else \
+        (1590.0, "fallback bf16 1.59 PF")
     ws = eng.ws
+    reps = 20
+
+    def _timed(fn):
+        with torch.inference_mode():
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    # ---- roofline of the dominant kernel: the windowed (differential) self-attention of one block, on the step's
+    # own q|k|v rows, timed live with CUDA events on the launching stream (the current stream)
+    D, H = cfg.embed_dim, cfg.num_heads
+    qkv, o = ws.qkv, ws.o
+    wlw, wrw = cfg.sliding_window
+    seq = dict(cu_seqlens_q=ws.cu, cu_seqlens_k=ws.cu, max_seqlen_q=ws.max_n, max_seqlen_k=ws.max_n)
+    if cfg.differential:
+        run_attn = lambda: ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], q2=qkv[:, 3 * D:4 * D],  # noqa
+                                         k2=qkv[:, 4 * D:5 * D], heads=H, window=(wlw, wrw), out=o, **seq)
+    else:
+        run_attn = lambda: ops.attention(qkv[:, 0:D], qkv[:, D:2 * D], qkv[:, 2 * D:3 * D], heads=H,  # noqa: E731
+                                         window=(wlw, wrw), out=o, **seq)
+    a_ms = _timed(run_attn)
+    streams = 2 if cfg.differential else 1
+    seq_lens = [int(v) for v in (ws.cu_host[1:] - ws.cu_host[:-1])]
+    pairs = sum(band_pairs(n, wlw, wrw) for n in seq_lens)
+    a_flops = 4.0 * 64 * pairs * H * streams
+    a_exps = sum(score_tiles(n, wlw, wrw) for n in seq_lens) * 128 * 128 * H * streams
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    clk_mhz = (clk or {}).get("sm_mhz") or 1965.0
+    mufu_floor_ms = a_exps / (16.0 * sm_count * clk_mhz * 1e6) * 1e3  # ex2 at 16 per clock per SM (measured)
+    a_ach = a_flops / (a_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "attention_tc_kernel (windowed self-attention, "
+                + ("differential, shared V" if cfg.differential else "single stream") + ")",
+                "achieved": a_ach, "peak": bf16_peak, "unit": "TFLOP/s", "frac": a_ach / bf16_peak,
+                "peak_source": bf16_src + "; bf16 MMA",
+                "traffic": _profiled_traffic("attention_diff_swa_medium.md")
+                if (cfg.differential and ws.M == 16494) else None,
+                "traffic_source": "profiles/attention_diff_swa_medium.md (ncu dram read+write bytes, one launch)",
+                "per_launch": {"flops": a_flops, "ms": a_ms, "band_pairs": pairs, "heads": H, "streams": streams,
+                               "exp2": a_exps, "mufu_floor_ms": mufu_floor_ms,
+                               "mufu_floor_basis": f"16 ex2/clk/SM x {sm_count} SMs at {clk_mhz:.0f} MHz"}}
+
+    # ---- the largest GEMM: the FF GLU.proj with its SwiGLU epilogue, on the step's own buffers
     lin = eng.lin["transformer.layers.0.ff.ff.0.proj"]
     M, K = ws.a.shape
     Nw = lin.n
@@ -418,34 +546,21 @@ def run_ours(args, wl, world, rank, local):
         # M >= 512 runs on the 2-SM (CTA pair) kernel, smaller M on the single-SM one
         kern = "gemm_pair_kernel" if M >= 512 else "gemm_persistent_kernel"
         kname = f"{kern}<{'fp8' if lin.fp8 else 'bf16'}, SwiGLU> (FF GLU.proj)"
-    reps = 20
-    with torch.inference_mode():
-        for _ in range(3):
-            run_k()
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(reps):
-            run_k()
-        e1.record()
-        torch.cuda.synchronize()
-    k_ms = e0.elapsed_time(e1) / reps
+    k_ms = _timed(run_k)
     flops = 2.0 * M * Nw * K
     achieved = flops / (k_ms / 1e3) / 1e12
-    peaks = _peaks()
-    if wl["mode"] == "fp8":
-        if peaks:
-            peak, peak_src = 2 * peaks["bf16_tflops"], "2x measured bf16 burst (MEASURED_PEAKS.json; no fp8 entry)"
-        else:
-            peak, peak_src = 2 * 1590.0, "2x fallback bf16 1.59 PF"
+    if lin.fp8:
+        peak, peak_src = measured_fp8_peak(dev)
+        if peak is None:
+            peak, peak_src = 2 * bf16_peak, "2x " + bf16_src + " (" + peak_src + ")"
     else:
-        peak, peak_src = (peaks["bf16_tflops"], "measured bf16 burst (MEASURED_PEAKS.json)") if peaks else \
-            (1590.0, "fallback bf16 1.59 PF")
+        peak, peak_src = bf16_peak, bf16_src
     traffic = _profiled_traffic("gemm_fp8_ff1_medium.md") if (lin.fp8 and M == 16494) else None
-    roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
-                "traffic_source": "profiles/gemm_fp8_ff1_medium.md (ncu dram read+write bytes, one launch)"
-                if traffic else None,
-                "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
+    roofline_gemm = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                     "traffic_source": "profiles/gemm_fp8_ff1_medium.md (ncu dram read+write bytes, one launch)"
+                     if traffic else None,
+                     "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
 
     if rank == 0:
         res = {
@@ -468,13 +583,13 @@ def run_ours(args, wl, world, rank, local):
             "gpu_launches": launches_per_step * args.steps,
             "launches_per_step": launches_per_step,
             "roofline": roofline,
+            "roofline_gemm": roofline_gemm,
         }
         if world == 1 and not args.no_cpu_baseline:
             threads = len(os.sched_getaffinity(0))
-            step_s, meas = cpu_block_sample(wl, threads)
+            step_s, meas, n = cpu_dit_sample(wl, threads)
             res["cpu_baseline"] = {"value": tokens_per_gpu / step_s, "unit": UNIT, "cores": threads, "kind": "port",
-                                   "sample": f"oracle fp32 block over L+64 tokens ({meas:.1f} s measured), "
-                                             f"scaled x{cfg.depth} blocks x2 CFG halves"}
+                                   "sample": _cpu_sample_text(wl, n, meas)}
         print(json.dumps(res), flush=True)
     del step
     model._graphs = None
