@@ -29,9 +29,9 @@
 // reference maximum per row and only moves it (rescaling O and the row sum)
 // when a tile's maximum exceeds it by more than 2^8, which keeps every exp2
 // argument <= 8 and leaves the result exactly softmax(S) V. A differential head
-// normalises stream 1 at the end of its pass and parks it in the output rows as
-// 16-bit values (the rounding the reference applies to each attention output
-// before out - out_diff), then subtracts stream 2's result from it.
+// normalises stream 1 at the end of its pass and keeps it in registers as 16-bit
+// values (the rounding the reference applies to each attention output before
+// out - out_diff), then subtracts stream 2's result from it.
 // The key range of a unit is clipped to the window of its queries, so fully
 // masked key tiles are never loaded or multiplied; tiles that lie entirely
 // inside every row's band skip masking, edge tiles mask with a bit mask.
@@ -458,6 +458,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       bool bad = false;
       float inv_l = 0.f;
       float m_i = NEG_INF, l_i = 0.f;  // reference maximum (scaled log2 domain) and row sum
+      uint32_t park[32];               // differential: stream 1's normalised output, 16-bit pairs
+#pragma unroll
+      for (int e = 0; e < 32; ++e) park[e] = 0u;
 
       for (int t = 0; t < max(T, To); ++t) {
         if (t >= T) {
@@ -533,24 +536,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         l_i += r01.x + r01.y;
         // O work once the score registers are dead, before this tile's P V is released
         if (pass == 1 && j == 0) {
-          // end of stream 1: normalise it and park it in the output rows (16-bit, as the
-          // reference's first attention output) until stream 2 is done
+          // end of stream 1: normalise it and keep it in registers as 16-bit pairs (the rounding the
+          // reference applies to its first attention output) until stream 2 is done
           uint32_t ov[32];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             tmem_ld32_async(t_o + 32 * c, ov);
             tmem_wait_ld();
-            if (row_ok && !bad) {
 #pragma unroll
-              for (int qd = 0; qd < 4; ++qd) {
-                uint4 w;
-                w.x = pack_2(__uint_as_float(ov[qd * 8 + 0]) * inv_l, __uint_as_float(ov[qd * 8 + 1]) * inv_l, p.f16);
-                w.y = pack_2(__uint_as_float(ov[qd * 8 + 2]) * inv_l, __uint_as_float(ov[qd * 8 + 3]) * inv_l, p.f16);
-                w.z = pack_2(__uint_as_float(ov[qd * 8 + 4]) * inv_l, __uint_as_float(ov[qd * 8 + 5]) * inv_l, p.f16);
-                w.w = pack_2(__uint_as_float(ov[qd * 8 + 6]) * inv_l, __uint_as_float(ov[qd * 8 + 7]) * inv_l, p.f16);
-                reinterpret_cast<uint4*>(dst)[c * 4 + qd] = w;
-              }
-            }
+            for (int e = 0; e < 16; ++e)
+              park[16 * c + e] = pack_2(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l,
+                                        p.f16);
           }
         }
         if (rescale) {
@@ -590,21 +586,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           for (int d = 0; d < 32; ++d) o[32 * c + d] = __uint_as_float(ov[d]) * inv_l;
         }
         tc_fence_before();
-        if (p.diff && row_ok && !bad) {
-          // differential combine out - out_diff (transformer.py:790-795), stream 1 parked in dst
+        if (p.diff) {
+          // differential combine out - out_diff (transformer.py:790-795), stream 1 from registers
 #pragma unroll
-          for (int qd = 0; qd < 8; ++qd) {
-            const uint4 w = reinterpret_cast<const uint4*>(dst)[qd];
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float lo = p.f16 ? __half2float(__ushort_as_half((unsigned short)(ws[e] & 0xffffu)))
-                                     : __uint_as_float(ws[e] << 16);
-              const float hi = p.f16 ? __half2float(__ushort_as_half((unsigned short)(ws[e] >> 16)))
-                                     : __uint_as_float(ws[e] & 0xffff0000u);
-              o[qd * 8 + 2 * e] = lo - o[qd * 8 + 2 * e];
-              o[qd * 8 + 2 * e + 1] = hi - o[qd * 8 + 2 * e + 1];
-            }
+          for (int e = 0; e < 32; ++e) {
+            const uint32_t w = park[e];
+            const float lo = p.f16 ? __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)))
+                                   : __uint_as_float(w << 16);
+            const float hi = p.f16 ? __half2float(__ushort_as_half((unsigned short)(w >> 16)))
+                                   : __uint_as_float(w & 0xffff0000u);
+            o[2 * e] = lo - o[2 * e];
+            o[2 * e + 1] = hi - o[2 * e + 1];
           }
         }
       } else {
