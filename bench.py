@@ -536,10 +536,12 @@ def run_ours(args, wl, world, rank, local):
     M, K = ws.a.shape
     Nw = lin.n
     if lin.gptq is not None:
-        g = lin.gptq
-        xp = ops.permute_cols(ws.a, g["perm"], ws.xperm[:M, :K])
-        run_k = lambda: ops.gptq_gemm(xp, g["qw"], g["sz"], Nw, ws.u, kind=_lib.EPI_SWIGLU, bias=lin.bias)  # noqa
-        kname = "gemm_gptq_kernel<SwiGLU> (FF GLU.proj, int4 dequant in smem)"
+        # the path the step takes: the engine picks dequantise-once + bf16 GEMM for many rows
+        from sa3_b200.engine import GPTQ_DEQUANT_MIN_ROWS
+        run_k = lambda: eng._gemm(ws.a, lin, ws.u, kind=_lib.EPI_SWIGLU)  # noqa: E731
+        kname = ("gptq_dequant_orig_kernel + gemm_pair_kernel<bf16, SwiGLU> (FF GLU.proj, int4 weight dequantised "
+                 "once per call)" if M >= GPTQ_DEQUANT_MIN_ROWS else
+                 "permute_cols_kernel + gemm_gptq_kernel<SwiGLU> (FF GLU.proj, int4 dequant in smem)")
     else:
         scale = ws.scale[4:5]
         run_k = lambda: eng._gemm(ws.a, lin, ws.u, x_scale=scale, kind=_lib.EPI_SWIGLU)  # noqa: E731

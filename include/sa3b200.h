@@ -140,6 +140,14 @@ int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, void* C, int M
  * with the exact arithmetic of sa3_gptq_gemm's shared-memory stage. */
 int sa3_gptq_dequant(const void* qw, const float* sz, void* out, int N, int K, int group_size, void* stream);
 
+/* Dequantise the packed GPTQ weight to bf16 W [N, K] (row stride ldo) in the ORIGINAL input-channel
+ * order, i.e. the dense weight of the nn.Linear the layer replaces (transformer.py:547-560, 432, 485):
+ * W[n, k] = (q - z) * s of sorted position inv_perm[k] (inv_perm = the inverse of perm), with the exact
+ * arithmetic of sa3_gptq_gemm. For large M, dequantising once per call and running sa3_gemm (bf16) on the
+ * unpermuted activations replaces both the act-order gather and the per-tile dequantisation. */
+int sa3_gptq_dequant_orig(const void* qw, const float* sz, const int* inv_perm, void* out, int N, int K,
+                          long long ldo, int group_size, void* stream);
+
 /* out[r, j] = x[r, perm[j]] for a bf16 [rows, K] view (the act-order gather of GPTQ inputs). */
 int sa3_permute_cols(const void* x, const int* perm, void* out, int rows, int K, long long ldx, long long ldo,
                      void* stream);
@@ -238,13 +246,17 @@ int sa3_attention(const void* q, const void* k, const void* v, const void* q2, c
  * the same FP8 linear as sa3_quantize_e4m3 (max|x| pass, quantise pass) followed
  * by sa3_gemm, but its scratch (max|x|, s_x and the M*K-byte e4m3 copy of x)
  * lives in a file-scope device array of 16 MiB, so the call allocates nothing.
- * x: bf16 [M, K] (row stride ldx); w: e4m3 [N, K] (ldw); w_scale fp32 [N]
- * (or NULL); bias fp32 [N] (or NULL); K a multiple of 16.
+ * x: bf16 [M, K] (row stride ldx >= K, a multiple of 8, 16-byte aligned);
+ * w: e4m3 [N, K] (ldw >= K, a multiple of 16, 16-byte aligned); w_scale fp32
+ * [N] (or NULL); bias fp32 [N] (or NULL); ldo >= N; K a multiple of 16. Every
+ * argument error is returned before anything is launched or the scratch is
+ * touched.
  * Limit: M * K <= SA3_FP8_NOALLOC_MAX_ELEMS, else SA3_ERR_UNSUPPORTED with
  * nothing launched. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make that first call before any stream
- * capture. The array is shared by every call and keeps the last call's
- * contents; calls that overlap on the GPU race on it.
+ * address (cudaGetSymbolAddress) and keeps it for the process, so make that
+ * first call before any stream capture; a device reset (cudaDeviceReset) is
+ * not supported afterwards. The array is shared by every call and keeps the
+ * last call's contents; calls that overlap on the GPU race on it.
  */
 #define SA3_FP8_NOALLOC_MAX_ELEMS ((16LL << 20) - 256)
 int sa3_fp8_linear_noalloc(const void* x, const void* w, const float* w_scale, const float* bias, void* out, int M,

@@ -1546,6 +1546,49 @@ __global__ void __launch_bounds__(256) gptq_dequant_kernel(const uint32_t* qw, c
   }
 }
 
+// W [N, K] bf16 in the ORIGINAL input-channel order: W[n, k] is the weight of sorted position
+// inv_perm[k]. One weight row per iteration: its K/8 packed words and its (s, z*s) pair of every group
+// are staged in shared memory, then each thread writes 8 consecutive channels (one 16-byte store),
+// gathering their nibbles through inv_perm. Same arithmetic as gptq_dequant8: fma(q, s, -z*s), exact in
+// fp32, rounded once to bf16.
+__global__ void __launch_bounds__(256) gptq_dequant_orig_kernel(const uint32_t* qw, const float* sz,
+                                                                const int* inv_perm, __nv_bfloat16* out, int N,
+                                                                int K, long long ldo, int group_size) {
+  grid_dep_wait();
+  extern __shared__ __align__(16) uint8_t dq_raw[];
+  uint32_t* words = reinterpret_cast<uint32_t*>(dq_raw);  // K / 8
+  float* ssz = reinterpret_cast<float*>(words + K / 8);   // [G][2]: s, z*s
+  const int G = K / group_size;
+  for (int n = blockIdx.x; n < N; n += gridDim.x) {
+    for (int c = threadIdx.x; c < K / 8; c += blockDim.x) words[c] = __ldg(qw + (long long)n * (K / 8) + c);
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      ssz[2 * g] = __ldg(sz + (long long)g * 2 * N + n);
+      ssz[2 * g + 1] = __ldg(sz + (long long)g * 2 * N + N + n);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+      const int4 p0 = __ldg(reinterpret_cast<const int4*>(inv_perm) + 2 * c);
+      const int4 p1 = __ldg(reinterpret_cast<const int4*>(inv_perm) + 2 * c + 1);
+      const int sp[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      float w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t q = (words[sp[j] >> 3] >> (4 * (sp[j] & 7))) & 0xFu;
+        const int g = sp[j] / group_size;
+        const float f = __uint_as_float(0x4B000000u | q) - 8388608.f;  // exact float(q)
+        w[j] = fmaf(f, ssz[2 * g], -ssz[2 * g + 1]);                    // (q - z) * s, exact
+      }
+      uint4 u;
+      u.x = pack_bf16x2(w[0], w[1]);
+      u.y = pack_bf16x2(w[2], w[3]);
+      u.z = pack_bf16x2(w[4], w[5]);
+      u.w = pack_bf16x2(w[6], w[7]);
+      *reinterpret_cast<uint4*>(out + (long long)n * ldo + 8 * c) = u;
+    }
+    __syncthreads();
+  }
+}
+
 // out[r, j] = x[r, perm[j]] (bf16); one row staged in shared memory per iteration.
 __global__ void __launch_bounds__(256) permute_cols_kernel(const __nv_bfloat16* x, const int* perm, __nv_bfloat16* out,
                                                            int rows, int K, long long ldx, long long ldo) {
@@ -1787,6 +1830,21 @@ extern "C" int sa3_gptq_dequant(const void* qw, const float* sz, void* out, int 
   if (grid > 148 * 16) grid = 148 * 16;
   launch_ex(gptq_dequant_kernel, dim3((int)grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       reinterpret_cast<const uint32_t*>(qw), sz, reinterpret_cast<__nv_bfloat16*>(out), N, K, group_size);
+  return launch_status();
+}
+
+extern "C" int sa3_gptq_dequant_orig(const void* qw, const float* sz, const int* inv_perm, void* out, int N, int K,
+                                     long long ldo, int group_size, void* stream) {
+  if (!qw || !sz || !inv_perm || !out || N <= 0 || K <= 0 || K % 8 || group_size <= 0 || K % group_size ||
+      ldo < K)
+    return SA3_ERR_ARG;
+  if (!aligned16(out) || !aligned16(inv_perm) || !aligned16(qw) || ldo % 8) return SA3_ERR_ALIGN;
+  const int smem = K / 2 + (K / group_size) * 8;
+  if (smem > 48 * 1024) return SA3_ERR_UNSUPPORTED;
+  const int grid = N < 148 * 8 ? N : 148 * 8;
+  launch_ex(gptq_dequant_orig_kernel, dim3(grid), dim3(256), smem, reinterpret_cast<cudaStream_t>(stream), 1,
+            reinterpret_cast<const uint32_t*>(qw), sz, inv_perm, reinterpret_cast<__nv_bfloat16*>(out), N, K, ldo,
+            group_size);
   return launch_status();
 }
 

@@ -69,6 +69,7 @@ SIGNATURES = {
                  ctypes.POINTER(Epilogue), c_vp],
     "sa3_gptq_gemm": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_int, ctypes.POINTER(Epilogue), c_vp],
     "sa3_gptq_dequant": [c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp],
+    "sa3_gptq_dequant_orig": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_int, c_vp],
     "sa3_permute_cols": [c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp],
     "sa3_rmsnorm_modulate": [c_vp, c_int, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                              c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp],

@@ -48,6 +48,11 @@ QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cr
 # latent rows); larger packed batches compute it block by block.
 _LOCAL_ALL_MAX_BYTES = 4 << 30
 
+# GPTQ linears with at least this many input rows dequantise their weight once per call (bf16, N x K, into one
+# buffer shared by all layers) and run the bf16 GEMM; fewer rows run the kernel that dequantises each weight
+# tile in shared memory (there the int4 weight bytes, not the multiply, bound the call).
+GPTQ_DEQUANT_MIN_ROWS = 1024
+
 
 def _pad_cols(w: torch.Tensor, mult: int = 8) -> torch.Tensor:
     k = w.shape[1]
@@ -240,6 +245,9 @@ class DiTEngine:
         ramp = torch.linspace(0, 1, cfg.timestep_features_dim // 2, dtype=torch.float32)
         self.t_freqs = torch.exp(ramp * (math.log(10000.0) - math.log(0.5)) + math.log(0.5)).to(self.dev)
         self.gptq_k = max([ln.gptq["k"] for ln in self.lin.values() if ln.gptq is not None], default=0)
+        # transient dense weight of the large-batch GPTQ path (the largest layer: 38 MB for the medium GLU.proj)
+        nk = max([ln.gptq["n"] * ln.gptq["k"] for ln in self.lin.values() if ln.gptq is not None], default=0)
+        self.wdq = torch.empty(nk, device=self.dev, dtype=torch.bfloat16) if nk else None
         self._prep_kv_all()
         self._prep_local_all()
 
@@ -326,6 +334,12 @@ class DiTEngine:
     def _gemm(self, x, lin: Lin, out=None, x_scale=None, **kw):
         if lin.gptq is not None:
             g = lin.gptq
+            if x.shape[0] >= GPTQ_DEQUANT_MIN_ROWS and "inv_perm" in g:
+                # many rows: dequantise the int4 weight once, in the original channel order, and run the bf16
+                # GEMM on the unpermuted activations (no act-order gather, no per-tile dequantisation)
+                w = ops.gptq_dequant_orig(g["qw"], g["sz"], g["inv_perm"], g["n"], g["k"], g["group_size"],
+                                          out=self.wdq[:g["n"] * g["k"]].view(g["n"], g["k"]))
+                return ops.gemm(x, w, out, bias=lin.bias, **kw)
             xp = ops.permute_cols(x, g["perm"], self.ws.xperm[:x.shape[0], :g["k"]])
             return ops.gptq_gemm(xp, g["qw"], g["sz"], g["n"], out, group_size=g["group_size"], bias=lin.bias, **kw)
         if lin.fp8 and x.dtype != torch.float8_e4m3fn:
@@ -345,15 +359,25 @@ class DiTEngine:
             am = ws.amax[slot:slot + 1]
             sc = ws.scale[slot:slot + 1]
             ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, **kw)
+            self._sync_amax(ws, slot)
             ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, quant_amax=am, scale_out=sc, **kw)
             return a, sc
         ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, **kw)
         return a, None
 
+    @staticmethod
+    def _sync_amax(ws, slot):
+        """Sequence split: the per-tensor activation scale spans the whole sequence, as in the unsplit step, so
+        each rank's max|x| at a quantisation point is max-reduced over the split's ranks before it is used."""
+        sp = ws.split
+        if sp is not None and sp.world > 1:
+            _seqsplit.all_reduce_max(ws.amax[slot:slot + 1], sp.group)
+
     def _quant(self, ws, x, out8, slot):
         """FP8: quantize x (whose amax is already in slot) into out8; bf16: pass x through."""
         if not self.fp8:
             return x, None
+        self._sync_amax(ws, slot)
         sc = ws.scale[slot:slot + 1]
         ops.quantize_e4m3(x, ws.amax[slot:slot + 1], out=out8, scale_out=sc)
         return out8, sc
@@ -361,7 +385,8 @@ class DiTEngine:
     def _split_self_attention(self, ws, a, asc, lin, groups, rope, o, amax_out, wl, wr):
         """Self-attention of a sequence-split rank: the q|k|v|q'|k' projection of each sequence lands between
         its halo rows, the boundary rows are exchanged with the neighbouring ranks, and the queries of the
-        own rows attend over [left halo | own | right halo] with the window re-centred."""
+        own rows attend over [left halo | own | right halo] with the window re-centred: the interior queries
+        while the exchange is in flight, the queries next to a neighbour after it."""
         cfg, sp = self.cfg, ws.split
         if (sp.wl, sp.wr) != (wl, wr):
             raise ValueError(f"split made for window {(sp.wl, sp.wr)}, the model attends over {(wl, wr)}")
@@ -371,18 +396,27 @@ class DiTEngine:
             self._gemm(a[b * n:(b + 1) * n], lin, ext[b * e + hl:b * e + hl + n], x_scale=asc, kind=_lib.EPI_QK_NORM,
                        qk=dict(gammas=groups, group_width=D, rope=rope, eps=cfg.qk_norm_eps, cos_sin=self.rope,
                                row_pos=ws.row_pos[b * n:(b + 1) * n]))
-        _seqsplit.exchange_halos(ext, ws.B, n, sp)
-        wl2, wr2 = _seqsplit.halo_window(wl, wr, sp.halo_left, sp.halo_right)
-        for b in range(ws.B):
-            blk = ext[b * e:(b + 1) * e]
-            own = blk[hl:hl + n]
-            kw = dict(heads=H, window=(wl2, wr2), out=o[b * n:(b + 1) * n], amax_out=amax_out, batch=1,
-                      max_seqlen_q=n, max_seqlen_k=e)
-            if cfg.differential:
-                ops.attention(own[:, 0:D], blk[:, D:2 * D], blk[:, 2 * D:3 * D], q2=own[:, 3 * D:4 * D],
-                              k2=blk[:, 4 * D:5 * D], **kw)
-            else:
-                ops.attention(own[:, 0:D], blk[:, D:2 * D], blk[:, 2 * D:3 * D], **kw)
+        # the halo transfers run while the interior queries (windows inside the own rows) are attended
+        reqs = _seqsplit.exchange_halos(ext, ws.B, n, sp, wait=False)
+        interior, edges = _seqsplit.attention_views(n, sp)
+
+        def attend(views):
+            for b in range(ws.B):
+                blk = ext[b * e:(b + 1) * e]
+                for q0, q1, k0, k1, win in views:
+                    q, k = blk[hl + q0:hl + q1], blk[k0:k1]
+                    kw = dict(heads=H, window=win, out=o[b * n + q0:b * n + q1], amax_out=amax_out, batch=1,
+                              max_seqlen_q=q1 - q0, max_seqlen_k=k1 - k0)
+                    if cfg.differential:
+                        ops.attention(q[:, 0:D], k[:, D:2 * D], k[:, 2 * D:3 * D], q2=q[:, 3 * D:4 * D],
+                                      k2=k[:, 4 * D:5 * D], **kw)
+                    else:
+                        ops.attention(q[:, 0:D], k[:, D:2 * D], k[:, 2 * D:3 * D], **kw)
+
+        attend(interior)
+        for req in reqs:
+            req.wait()
+        attend(edges)
 
     # ------------------------------------------------------------------ forward
     @torch.no_grad()

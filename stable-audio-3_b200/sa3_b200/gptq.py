@@ -12,7 +12,10 @@ with W[n, k] = (q[k, n] - z[g_idx[k], n]) * s[g_idx[k], n].
 repack() turns them into the kernel layout of sa3_gptq_gemm: input channels
 sorted by group (stable argsort of g_idx, so each 64-wide K tile lies in one
 group), 4-bit values packed along K per output row, and fp32 (s, z*s) rows per
-group. The GEMM's A operand is x[:, perm] (sa3_permute_cols).
+group. The GEMM's A operand is x[:, perm] (sa3_permute_cols). inv_perm (the
+inverse permutation) lets sa3_gptq_dequant_orig write the dense weight in the
+original channel order, which is how large batches run (dequantise once per
+call, then the bf16 GEMM on the unpermuted activations).
 """
 from __future__ import annotations
 
@@ -54,8 +57,9 @@ def repack(qweight, qzeros, scales, g_idx, group_size: int = 128) -> dict:
         words |= qt[:, j::8] << np.uint32(4 * j)
     s = np.asarray(scales).astype(np.float32)
     zs = z.astype(np.float32) * s  # exact: 4-bit integer times an fp16 value
-    return dict(perm=torch.from_numpy(perm.astype(np.int32)), qw=torch.from_numpy(words.view(np.int32)),
-                sz=torch.from_numpy(np.concatenate([s, zs], axis=1)), n=N, k=K, group_size=group_size)
+    return dict(perm=torch.from_numpy(perm.astype(np.int32)), inv_perm=torch.from_numpy(np.argsort(perm).astype(np.int32)),
+                qw=torch.from_numpy(words.view(np.int32)), sz=torch.from_numpy(np.concatenate([s, zs], axis=1)),
+                n=N, k=K, group_size=group_size)
 
 
 def reorder_rows(packed: dict, idx: torch.Tensor) -> dict:
@@ -77,8 +81,9 @@ def random_layer(n: int, k: int, group_size: int = 128, generator: Optional[torc
     s = (torch.rand(G, n, generator=g) * 0.019 + 0.001).half().float()
     z = torch.randint(0, 16, (G, n), generator=g).float()
     perm = torch.randperm(k, generator=g).to(torch.int32)
-    return dict(perm=perm.to(device), qw=words.to(device), sz=torch.cat([s, z * s], dim=1).contiguous().to(device),
-                n=n, k=k, group_size=group_size)
+    inv = torch.argsort(perm).to(torch.int32)
+    return dict(perm=perm.to(device), inv_perm=inv.to(device), qw=words.to(device),
+                sz=torch.cat([s, z * s], dim=1).contiguous().to(device), n=n, k=k, group_size=group_size)
 
 
 def to_device(packed: dict, device) -> dict:

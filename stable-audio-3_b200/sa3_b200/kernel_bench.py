@@ -14,6 +14,7 @@ Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
   norm_fp8   RMSNorm + modulate of the fp32 stream: amax pass + e4m3 write pass
   qknorm     qk RMSNorm + RoPE on q, k, q_diff, k_diff in place
   ff1_gptq   GLU.proj GPTQ int4 GEMM (group 128, act-order gather included separately), M = 16 x 2648
+  ff1_gptq_dense  the same layer on the large-batch path: dequantise once (original channel order) + bf16 GEMM
 Each case's operands exceed the 126 MB L2.
 """
 from __future__ import annotations
@@ -132,6 +133,24 @@ def case(name: str, iters: int) -> dict:
         ms_perm = _time(lambda: ops.permute_cols(a, lay["perm"], xp), iters)
         ms = _time(lambda: ops.gptq_gemm(xp, lay["qw"], lay["sz"], 12288, out, kind=_lib.EPI_SWIGLU), iters)
         return {"case": name, "ms": ms, "tflops": 2.0 * Mg * 12288 * 1536 / ms / 1e9, "gather_ms": ms_perm}
+    if name == "ff1_gptq_dense":
+        # the large-batch GPTQ path: dequantise the int4 weight once (original channel order, bf16), then the
+        # 2-SM bf16 GEMM with the SwiGLU epilogue on the unpermuted activations
+        from .gptq import random_layer
+        Mg = 16 * N_GPTQ
+        lay = random_layer(12288, 1536, 128, g, dev)
+        a = torch.randn(Mg, 1536, device=dev).bfloat16()
+        out = torch.empty(Mg, 6144, device=dev, dtype=torch.bfloat16)
+        wd = torch.empty(12288, 1536, device=dev, dtype=torch.bfloat16)
+        ms_dq = _time(lambda: ops.gptq_dequant_orig(lay["qw"], lay["sz"], lay["inv_perm"], 12288, 1536, 128, wd), iters)
+        ms_mm = _time(lambda: ops.gemm(a, wd, out, kind=_lib.EPI_SWIGLU), iters)
+
+        def fn():
+            ops.gptq_dequant_orig(lay["qw"], lay["sz"], lay["inv_perm"], 12288, 1536, 128, wd)
+            ops.gemm(a, wd, out, kind=_lib.EPI_SWIGLU)
+        ms = _time(fn, iters)
+        return {"case": name, "ms": ms, "tflops": 2.0 * Mg * 12288 * 1536 / ms / 1e9, "dequant_ms": ms_dq,
+                "dequant_GBps": 12288 * 1536 * 2.5 / ms_dq / 1e6, "gemm_ms": ms_mm}
     if name == "norm_fp8":
         x = torch.randn(M, D, device=dev)
         gam = torch.ones(D, device=dev)
@@ -168,7 +187,7 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq"]
+CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq", "ff1_gptq_dense"]
 
 
 def main():

@@ -303,6 +303,23 @@ def gptq_dequant(qw: torch.Tensor, sz: torch.Tensor, n: int, k: int, group_size:
     return out
 
 
+def gptq_dequant_orig(qw: torch.Tensor, sz: torch.Tensor, inv_perm: torch.Tensor, n: int, k: int,
+                      group_size: int = 128, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 W [n, k] of a repacked GPTQ layer in the original input-channel order (the dense nn.Linear weight)."""
+    _need_cuda(qw, sz, inv_perm, out)
+    if inv_perm.dtype != torch.int32:
+        raise RuntimeError("inv_perm must be int32")
+    if out is None:
+        out = torch.empty(n, k, device=qw.device, dtype=torch.bfloat16)
+    if out.dtype != torch.bfloat16 or tuple(out.shape) != (n, k):
+        raise RuntimeError(f"out must be bf16 [{n}, {k}]")
+    _count()
+    rc = _lib.load().sa3_gptq_dequant_orig(qw.data_ptr(), sz.data_ptr(), inv_perm.data_ptr(), out.data_ptr(), n, k,
+                                           _row_stride(out), group_size, _stream())
+    _lib.check(rc, "sa3_gptq_dequant_orig")
+    return out
+
+
 def permute_cols(x: torch.Tensor, perm: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     _need_cuda(x, perm, out)
     rows, K = x.shape

@@ -1,6 +1,7 @@
 """GPTQ int4 path on a B200 vs the oracle's GPTQ definition.
 
-* dequantisation (index math + arithmetic): bit-exact vs bf16(oracle W[:, perm]).
+* dequantisation (index math + arithmetic): bit-exact vs bf16(oracle W[:, perm]) (sorted channels) and vs
+  bf16(oracle W) (original channel order, the large-batch path's dense weight).
 * GEMM / QuantLinearGPTQ: relative Frobenius <= 2e-2 vs F.linear(x, dequant(W)) (asserted 5e-3;
   bf16 rounding of x and W is the only difference).
 * DiT network output in GPTQ mode: <= 2e-2 relative L2 vs the oracle.
@@ -27,6 +28,19 @@ def test_gptq_dequant_bit_exact(cuda):
     p = gptq.to_device(gptq.repack(qw, qz, sc, gi), cuda)
     w = ops.gptq_dequant(p["qw"], p["sz"], 512, 1536)
     ref = torch.from_numpy(oq.gptq_dequant(qw, qz, sc, gi)[:, p["perm"].cpu().numpy()]).bfloat16()
+    assert torch.equal(w.cpu().view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("N,K", [(512, 1536), (768, 6144), (256, 256)])
+def test_gptq_dequant_orig_bit_exact(cuda, N, K):
+    """Dense weight in the original input-channel order (act-order undone through inv_perm): every bf16 bit
+    equals bf16 of the oracle's (q - z[g_idx]) * s[g_idx]."""
+    from sa3_b200 import gptq, ops
+
+    qw, qz, sc, gi = oq.random_gptq_layer(N, K, seed=N + K)
+    p = gptq.to_device(gptq.repack(qw, qz, sc, gi), cuda)
+    w = ops.gptq_dequant_orig(p["qw"], p["sz"], p["inv_perm"], N, K)
+    ref = torch.from_numpy(oq.gptq_dequant(qw, qz, sc, gi)).bfloat16()
     assert torch.equal(w.cpu().view(torch.int16), ref.view(torch.int16))
 
 
@@ -57,13 +71,17 @@ def test_quant_linear_gptq_module(cuda):
     assert rel_fro(y, ref) < 5e-3
 
 
-def test_dit_gptq_network_matches_oracle(cuda):
+@pytest.mark.parametrize("L", [200, 600])
+def test_dit_gptq_network_matches_oracle(cuda, L):
+    """GPTQ DiT network output vs the oracle. L = 200 (528 token rows) runs every int4 linear on the
+    shared-memory-dequantising kernel; L = 600 (1328 rows) runs the block linears on the large-batch path
+    (dense weight dequantised once per call, bf16 GEMM on the unpermuted activations)."""
     from sa3_b200.modules import DiffusionTransformer, init_synthetic_
     from tests.golden.cases import CASES
     from tests.test_oracle_golden import _cfg
     from tests.test_model_gpu import _batched_inputs
 
-    case = CASES["dit_small_cfg"]
+    case = dict(CASES["dit_small_cfg"], L=L)
     m = init_synthetic_(DiffusionTransformer(case["cfg"]), seed=case["seed"])
     layers = {}
     for i, (name, mod) in enumerate(sorted(m.named_modules())):
@@ -80,4 +98,5 @@ def test_dit_gptq_network_matches_oracle(cuda):
         out = m.engine().inner(*(a.to(cuda) for a in inputs))
     assert torch.isfinite(out).all()
     err = rel_fro(out, ref)
+    print(f"GPTQ DiT L={L}: network velocity rel L2 {err:.3e}")
     assert err < 2e-2, err
