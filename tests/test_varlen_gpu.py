@@ -4,8 +4,8 @@
     compute each row independently of the others, so only the packing tables differ).
   * FP8: the per-tensor activation scales span the packed batch, so a prompt's quantization grid depends on its
     batch-mates; the packed network output is checked against the oracle's packed restatement
-    (dit_inner_forward_packed, FP8 definition at the bf16 deployment's activations), and each prompt's CFG/APG
-    velocity against the oracle's combine of those outputs: <= 2e-2 each.
+    (dit_inner_forward_packed, FP8 definition at the bf16 deployment's activations, <= 2e-2), and each prompt's
+    CFG/APG velocity against the oracle's combine of those outputs (tests.tolerance.fp8_network_bound).
 """
 from dataclasses import replace
 
@@ -15,6 +15,7 @@ import torch
 from oracle import dit as odit
 from tests.golden.cases import CASES
 from tests.test_oracle_golden import _cfg
+from tests.tolerance import fp8_network_bound
 
 pytestmark = pytest.mark.gpu
 
@@ -60,12 +61,16 @@ def test_varlen_matches_per_prompt(cuda, mode):
         ref = odit.dit_inner_forward_packed(lin, sd, ocfg, xs, t, cond, gemb, locs)
         # both CFG halves of every prompt in one packed batch (cond halves first), as forward_varlen runs them
         zc = torch.zeros_like(cond)
-        ref2 = odit.dit_inner_forward_packed(lin, sd, ocfg, xs + xs, torch.cat([t, t]), torch.cat([cond, zc]),
-                                             torch.cat([gemb, gemb]), locs + locs)
+        cfg_args = (xs + xs, torch.cat([t, t]), torch.cat([cond, zc]), torch.cat([gemb, gemb]), locs + locs)
+        ref2 = odit.dit_inner_forward_packed(lin, sd, ocfg, *cfg_args)
+        ref2_32 = odit.dit_inner_forward_packed(lin, sd, _cfg(cfg), *cfg_args)
     for i in range(P):
         e_net = rel(packed[i], ref[i])
         vref = odit.cfg_combine(xs[i][None], t[i:i + 1], torch.stack([ref2[i], ref2[P + i]]), 5.0, 1.0)[0]
+        vref32 = odit.cfg_combine(xs[i][None], t[i:i + 1], torch.stack([ref2_32[i], ref2_32[P + i]]), 5.0, 1.0)[0]
         e_v = rel(v[i], vref)
-        print(f"prompt {i} (L={lens[i]}): FP8 packed network rel L2 {e_net:.3e}, CFG velocity {e_v:.3e}")
+        bound = fp8_network_bound(vref, vref32)
+        print(f"prompt {i} (L={lens[i]}): FP8 packed network rel L2 {e_net:.3e}, CFG velocity {e_v:.3e} "
+              f"(bound {bound:.3e})")
         assert e_net < 2e-2, i
-        assert e_v < 2e-2, i
+        assert e_v < bound, i
