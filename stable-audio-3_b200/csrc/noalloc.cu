@@ -57,6 +57,12 @@ extern "C" int sa3_fp8_linear_noalloc(const void* x, const void* w, const float*
                                       void* stream) {
   if (!x || !w || !out || M <= 0 || N <= 0 || K <= 0) return SA3_ERR_ARG;
   if (K % 16) return SA3_ERR_ALIGN;  // the e4m3 copy's rows feed TMA: 16-byte multiples
+  // Everything the three launches below would refuse is refused here, before the shared scratch is
+  // touched: a call that fails leaves the scratch (which an earlier call on the GPU may still be
+  // reading) alone. Activation (sa3_quantize_e4m3): bf16 rows, 16-byte aligned, stride >= K, multiple
+  // of 8. Weight (sa3_gemm, e4m3): 16-byte aligned rows, stride >= K, multiple of 16. Output: stride >= N.
+  if (ldx < K || ldw < K || ldo < N) return SA3_ERR_ARG;
+  if (!aligned16(x) || (ldx % 8) || !aligned16(w) || (ldw % 16)) return SA3_ERR_ALIGN;
   static_assert(SA3_FP8_NOALLOC_MAX_ELEMS == (long long)(kNoAllocScratchBytes - kNoAllocHeaderBytes),
                 "header limit and scratch size disagree");
   if ((unsigned long long)M * (unsigned long long)K > (unsigned long long)SA3_FP8_NOALLOC_MAX_ELEMS)
