@@ -13,7 +13,8 @@ TensorRT is importable; the functions below work with plain torch tensors.
 """
 from __future__ import annotations
 
-from typing import Sequence
+import math
+from typing import Optional, Sequence
 
 import torch
 
@@ -21,6 +22,21 @@ from . import ops
 
 SAMEL_WINDOW = 17
 _streams = {}
+_scratch = {}  # device index -> uint8 workspace of the fp32 path, grown only when a larger call arrives
+
+
+def fp32_workspace_bytes(q_shape: Sequence[int]) -> int:
+    """Scratch of the fp32 path: bf16 copies of q, k, v and the bf16 output (half of q's heads)."""
+    n = math.prod(q_shape)
+    return 2 * (3 * n + n // 2)
+
+
+def _device_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _scratch.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        buf = _scratch[idx] = torch.empty(nbytes, device=device, dtype=torch.uint8)
+    return buf
 
 
 def diff_attn_swa_shape(q_shape: Sequence[int]) -> tuple:
@@ -31,16 +47,31 @@ def diff_attn_swa_shape(q_shape: Sequence[int]) -> tuple:
 
 
 def diff_attn_swa_impl(q_bat: torch.Tensor, k_bat: torch.Tensor, v_bat: torch.Tensor, num_heads: int,
-                       outputs: Sequence[torch.Tensor], stream: int, window: int = SAMEL_WINDOW) -> None:
-    """Write outputs[0] = attn(q,k,v heads :H) - attn(heads H:) on CUDA stream `stream` (no return value)."""
+                       outputs: Sequence[torch.Tensor], stream: int, window: int = SAMEL_WINDOW,
+                       workspace: Optional[torch.Tensor] = None) -> None:
+    """Write outputs[0] = attn(q,k,v heads :H) - attn(heads H:) on CUDA stream `stream` (no return value).
+
+    fp32 I/O runs the bf16 kernel on bf16 copies and writes the result back in fp32. Those copies live in
+    `workspace` (a uint8 CUDA tensor of at least fp32_workspace_bytes(q_bat.shape) bytes, e.g. the workspace
+    a TensorRT plugin is given) or, without one, in a per-device buffer that is allocated only when a call
+    larger than every earlier one arrives: a repeated call (every enqueue of a built engine) allocates nothing.
+    Make the first call of the largest shape before any graph capture."""
     out = outputs[0]
     if stream not in _streams:
         _streams[stream] = torch.cuda.ExternalStream(stream)
     with torch.cuda.stream(_streams[stream]):
         if q_bat.dtype == torch.float32:
-            # fp32 plugin I/O: run the bf16 kernel on converted copies, write back in fp32
-            qb, kb, vb = (t.to(torch.bfloat16) for t in (q_bat, k_bat, v_bat))
-            ob = torch.empty(diff_attn_swa_shape(q_bat.shape), device=q_bat.device, dtype=torch.bfloat16)
+            need = fp32_workspace_bytes(q_bat.shape)
+            ws = workspace if workspace is not None else _device_scratch(q_bat.device, need)
+            if ws.dtype != torch.uint8 or ws.numel() < need or not ws.is_cuda:
+                raise RuntimeError(f"the fp32 path needs a CUDA uint8 workspace of {need} bytes")
+            n = q_bat.numel()
+            buf = ws[:need].view(torch.bfloat16)
+            qb, kb, vb = (buf[i * n:(i + 1) * n].view(q_bat.shape) for i in range(3))
+            ob = buf[3 * n:3 * n + n // 2].view(diff_attn_swa_shape(q_bat.shape))
+            qb.copy_(q_bat)
+            kb.copy_(k_bat)
+            vb.copy_(v_bat)
             ops.diff_attn_swa(qb, kb, vb, num_heads, window, ob)
             out.copy_(ob)
         else:

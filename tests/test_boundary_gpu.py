@@ -96,6 +96,32 @@ def test_diff_attn_swa_plugin(cuda, dtype):
     assert max_rel(_bhnd(out), ref) < 1e-2
 
 
+def test_diff_attn_swa_plugin_fp32_allocates_nothing_per_call(cuda):
+    """The fp32 plugin path after its first call of a shape: repeated calls (every enqueue) make no CUDA
+    allocation, and a caller-given workspace is used as given."""
+    from sa3_b200.plugin import diff_attn_swa_impl, diff_attn_swa_shape, fp32_workspace_bytes
+
+    g = torch.Generator().manual_seed(6)
+    B, N, H = 2, 700, 24
+    qb, kb, vb = (torch.randn(B, N, 2 * H, 64, generator=g).to(cuda) for _ in range(3))
+    out = torch.empty(diff_attn_swa_shape(qb.shape), device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    diff_attn_swa_impl(qb, kb, vb, H, [out], st)
+    torch.cuda.synchronize()
+    first = out.clone()
+    n0 = torch.cuda.memory_stats()["allocation.all.allocated"]
+    for _ in range(3):
+        diff_attn_swa_impl(qb, kb, vb, H, [out], st)
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == n0
+    assert torch.equal(out, first)
+    ws = torch.empty(fp32_workspace_bytes(qb.shape), device=cuda, dtype=torch.uint8)
+    out2 = torch.empty_like(out)
+    diff_attn_swa_impl(qb, kb, vb, H, [out2], st, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(out2, first)
+
+
 def test_quant_linear_fp8(cuda):
     from torch import nn
 
