@@ -8,8 +8,9 @@ every rank sends the first wr rows of its post-RoPE q|k|v|q'|k' projection to it
 neighbour and the last wl rows to its right neighbour (NCCL send/recv through
 torch.distributed), and attends over [left halo | own rows | right halo] with the window
 re-centred on its own rows. RoPE uses global positions. The CFG/APG combine (dit.py:571-625) needs two
-sums over the whole sequence per prompt; they are all-reduced. Cross-attention keys
-(the context) and the conditioning are replicated.
+sums over the whole sequence per prompt; they are all-reduced. With FP8 linears, the max|x| behind each
+per-tensor activation scale is max-reduced over the ranks as well, so the split step quantizes with the
+unsplit step's scales. Cross-attention keys (the context) and the conditioning are replicated.
 """
 from __future__ import annotations
 
@@ -92,10 +93,46 @@ def halo_window(wl: int, wr: int, halo_left: int, halo_right: int) -> Tuple[int,
     return wl + halo_right, wr - halo_right
 
 
-def exchange_halos(ext: torch.Tensor, batch: int, own: int, split: SeqSplit) -> None:
+def view_window(wl: int, wr: int, q0: int, q1: int, k0: int, k1: int, hl: int) -> Tuple[int, int]:
+    """Window for one attention call whose queries are own rows [q0, q1) and whose keys are rows [k0, k1) of
+    [left halo (hl rows) | own rows | right halo], so that own row i still sees rows [i - wl, i + wr] of the
+    sequence. Under the kernels' bottom-right convention key j' of the view is visible to query i' iff
+    -wl2 <= j' - i' - dlt <= wr2 with dlt = (k1 - k0) - (q1 - q0); query i' is own row q0 + i', at view key
+    c = q0 + hl - k0 + i'. Both bounds must come out non-negative (a negative bound would mean unbounded)."""
+    c = q0 + hl - k0
+    dlt = (k1 - k0) - (q1 - q0)
+    wl2, wr2 = dlt - c + wl, c + wr - dlt
+    if wl2 < 0 or wr2 < 0:
+        raise ValueError(f"view [{q0},{q1}) x [{k0},{k1}) cannot express the window ({wl}, {wr})")
+    return wl2, wr2
+
+
+def attention_views(own: int, split: SeqSplit):
+    """The self-attention of a split rank as calls that need no halo (issued while the halo exchange is in
+    flight) and calls that do. Each entry is (q0, q1, k0, k1, (wl2, wr2)) with queries = own rows [q0, q1)
+    and keys = rows [k0, k1) of [left halo | own | right halo]. Interior queries (window inside the own rows)
+    attend over the own rows; the first wl and last wr own rows, next to a neighbour, over the halo too."""
+    wl, wr, hl, hr = split.wl, split.wr, split.halo_left, split.halo_right
+    q0, q1 = (wl if hl else 0), (own - wr if hr else own)
+    if q1 - q0 <= 0:  # no interior: one call over everything after the exchange
+        return [], [(0, own, 0, hl + own + hr, view_window(wl, wr, 0, own, 0, hl + own + hr, hl))]
+    interior = [(q0, q1, hl, hl + own, view_window(wl, wr, q0, q1, hl, hl + own, hl))]
+    edges = []
+    if hl:
+        k1 = min(hl + own + hr, hl + wl + wr)
+        edges.append((0, wl, 0, k1, view_window(wl, wr, 0, wl, 0, k1, hl)))
+    if hr:
+        k0 = max(0, hl + own - wr - wl)
+        edges.append((own - wr, own, k0, hl + own + hr, view_window(wl, wr, own - wr, own, k0, hl + own + hr, hl)))
+    return interior, edges
+
+
+def exchange_halos(ext: torch.Tensor, batch: int, own: int, split: SeqSplit, wait: bool = True):
     """ext: [batch * (hl + own + hr), C] rows laid out per sequence as [left halo | own rows | right halo].
     Fills the halo rows from the neighbours (their own rows next to the boundary) and sends this rank's
-    boundary rows. All transfers of one call form one batched group of P2P operations."""
+    boundary rows. All transfers of one call form one batched group of P2P operations. With wait=False the
+    requests are returned: waiting on them later makes the current stream wait for the transfers, and work
+    queued in between overlaps them."""
     hl, hr = split.halo_left, split.halo_right
     e = hl + own + hr
     ops = []
@@ -108,9 +145,19 @@ def exchange_halos(ext: torch.Tensor, batch: int, own: int, split: SeqSplit) -> 
             ops.append(dist.P2POp(dist.isend, ext[base + hl + own - split.wl:base + hl + own], split.rank + 1,
                                   split.group))
             ops.append(dist.P2POp(dist.irecv, ext[base + hl + own:base + e], split.rank + 1, split.group))
-    if ops:
-        for req in dist.batch_isend_irecv(ops):
+    reqs = dist.batch_isend_irecv(ops) if ops else []
+    if wait:
+        for req in reqs:
             req.wait()
+        return []
+    return reqs
+
+
+def all_reduce_max(t: torch.Tensor, group=None) -> None:
+    """In-place max over the split's ranks (a per-tensor FP8 activation amax: the tensor is the whole
+    sequence, so every rank quantizes with the scale the unsplit step would use)."""
+    if dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
 
 
 def cfg_combine_split(x: torch.Tensor, t: torch.Tensor, out: torch.Tensor, cfg_scale: float, apg_scale: float,

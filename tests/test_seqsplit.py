@@ -148,3 +148,31 @@ def test_split_combine_matches_oracle_on_one_rank(apg_scale):
     ref = odit.cfg_combine(x, t, out, 5.0, apg_scale)
     got = ss.cfg_combine_split(x, t, out, 5.0, apg_scale)
     assert torch.allclose(got, ref, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("window", [(64, 64), (256, 256), (17, 17), (32, 64)])
+def test_attention_views_cover_each_window_exactly(world, window):
+    """The split self-attention runs as calls without halo (interior queries, issued while the halo exchange is
+    in flight) and calls with it (queries next to a neighbour). Under the kernel's band convention every own
+    row must see exactly the rows [i - wl, i + wr] of the sequence, and be computed by exactly one call."""
+    for L in (700, 1500, 3000):
+        try:
+            splits = [ss.make_split(L, r, world, 64, window) for r in range(world)]
+        except ValueError:
+            continue
+        for sp in splits:
+            n = sp.tok_end - sp.tok_start
+            hl, hr = sp.halo_left, sp.halo_right
+            interior, edges = ss.attention_views(n, sp)
+            seen, owner = {}, {}
+            for q0, q1, k0, k1, (wl2, wr2) in interior + edges:
+                dlt = (k1 - k0) - (q1 - q0)
+                for i in range(q1 - q0):
+                    assert q0 + i not in owner
+                    owner[q0 + i] = (q0, q1)
+                    seen[q0 + i] = {k0 + j for j in range(k1 - k0) if -wl2 <= j - i - dlt <= wr2}
+            assert sorted(owner) == list(range(n))
+            for i in range(n):
+                want = {hl + i + d for d in range(-sp.wl, sp.wr + 1) if 0 <= hl + i + d < hl + n + hr}
+                assert seen[i] == want, (sp.rank, i)

@@ -5,9 +5,11 @@ Skipped with fewer than 2 GPUs.
 Asserted on the network output for both CFG halves (before the combine) and on the full CFG/APG velocity.
 bf16: the split changes the row grouping and the key-tile grouping of the attention, so it agrees with the
 unsplit forward to rounding; the CFG/APG combine (cfg 5) amplifies that rounding, as it does for the
-reference's own bf16 module, so the velocity gets the full-step bound. FP8: each rank quantizes its own rows
-with its own per-tensor activation scale (the tensor is the rank's shard), so the bounds are the FP8 ones of
-the model tests."""
+reference's own bf16 module, so the velocity gets the full-step bound. FP8: the max|x| behind every per-tensor
+activation scale is max-reduced over the ranks, so the split step quantizes with the unsplit step's scales;
+the attention's different key-tile grouping still moves activations at rounding level, which e4m3 rounding
+can turn into whole-step differences, so the velocity gets tests.tolerance.fp8_network_bound (measured with
+the oracle on the same inputs)."""
 import datetime
 import os
 import queue
@@ -75,7 +77,22 @@ def _worker(rank, world, port, mode, outq):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode,tol_net,tol_vel", [("bf16", 5e-3, 2e-2), ("fp8", 2e-2, 5e-2)])
+def _fp8_velocity_bound():
+    from dataclasses import replace
+
+    from oracle import dit as odit
+    from tests.test_oracle_golden import _cfg
+    from tests.tolerance import fp8_network_bound
+
+    sd = _model("fp8").state_dict()
+    x, t, cond, gemb, loc = _inputs()
+    with torch.inference_mode():
+        a = odit.dit_forward(sd, replace(_cfg(_small), act_bf16=True), x, t, cond, gemb, loc, 5.0, 1.0, mode="fp8")
+        b = odit.dit_forward(sd, _cfg(_small), x, t, cond, gemb, loc, 5.0, 1.0, mode="fp8")
+    return fp8_network_bound(a, b)
+
+
+@pytest.mark.parametrize("mode,tol_net,tol_vel", [("bf16", 5e-3, 2e-2), ("fp8", 2e-2, None)])
 def test_sequence_split_matches_unsplit(cuda, mode, tol_net, tol_vel):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -116,5 +133,9 @@ def test_sequence_split_matches_unsplit(cuda, mode, tol_net, tol_vel):
     assert torch.isfinite(split).all() and torch.isfinite(net).all()
     err_net = ((net - ref_net).norm() / ref_net.norm()).item()
     err_vel = ((split - ref).norm() / ref.norm()).item()
+    if tol_vel is None:
+        tol_vel = _fp8_velocity_bound()
+    print(f"split over 2 GPUs, {mode}: network rel L2 {err_net:.3e} (bound {tol_net:.1e}), CFG velocity "
+          f"{err_vel:.3e} (bound {tol_vel:.3e})")
     assert err_net < tol_net, err_net
     assert err_vel < tol_vel, err_vel
