@@ -984,6 +984,12 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         tc_commit(&acc_full[a]);
         if (!ok) break;
       }
+      // after an abort the epilogue may not wait for every accumulator: TMEM is released only once the
+      // last commit on empty[] (it covers every MMA issued) has landed
+      if (it > 0) {
+        volatile int never = 0;
+        mbar_wait(&empty[(it - 1) % GEMM_STAGES], ((it - 1) / GEMM_STAGES) & 1, &never, 36);
+      }
     }
   } else {
     // ---------------- epilogue warps
@@ -1216,10 +1222,15 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
         }
         commit_pair_both(&acc_full[a]);
       }
-      // TMEM is released after the final cluster barrier: no MMA may still be running then
-      volatile int never = 0;
-      commit_pair_both(&acc_full[lt & 1]);
-      warp_wait_g(&acc_full[lt & 1], (lt >> 1) & 1, &never, 75);
+      // TMEM is released after the final cluster barrier: no MMA may still be running then. The last
+      // commit on empty[] covers every MMA this thread issued, and nothing commits to that barrier
+      // afterwards. (An extra commit on acc_full here would complete a second phase of a buffer whose
+      // previous phase a lagging epilogue warp may not have observed yet; with a phase-parity wait that
+      // warp would then wait for a phase that never comes.)
+      if (it > 0) {
+        volatile int never = 0;
+        warp_wait_g(&empty[(it - 1) % P2_STAGES], ((it - 1) / P2_STAGES) & 1, &never, 75);
+      }
     }
   } else {
     // ---------------- epilogue warps
@@ -1475,6 +1486,11 @@ __global__ void __launch_bounds__(GQ_THREADS, 1)
         }
         tc_commit(&acc_full[a]);
         if (!ok) break;
+      }
+      // TMEM is released only once the last commit on empty[] (it covers every MMA issued) has landed
+      if (it > 0) {
+        volatile int never = 0;
+        mbar_wait(&empty[(it - 1) % GQ_STAGES], ((it - 1) / GQ_STAGES) & 1, &never, 57);
       }
     }
   } else if (warp < 6) {
