@@ -148,6 +148,17 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
+def gather_over_ranks(v: float, world: int) -> list:
+    """Every rank's value, in rank order (same collective on every rank)."""
+    if world == 1:
+        return [v]
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def model_cfg(name):
     from sa3_b200.modules import MEDIUM, SMALL
     return {"medium": MEDIUM, "small": SMALL}[name]
@@ -346,7 +357,12 @@ def run_dp_varlen(args, wl, world, rank, local):
         torch.cuda.synchronize()
         barrier(world)
         clk = clocks.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    my_ms = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(my_ms, world)
+    # per-rank device time and stream rows (latents + memory tokens, both CFG halves): the straggler and the
+    # LPT balance the scaling depends on
+    rank_ms = gather_over_ranks(my_ms, world)
+    rank_rows = gather_over_ranks(float(sum(2 * (lengths[i] + cfg.num_memory_tokens) for i in shard)), world)
     tokens = 2 * sum(lengths)
     if rank == 0:
         print(json.dumps({
@@ -358,6 +374,8 @@ def run_dp_varlen(args, wl, world, rank, local):
                        "tokens_per_step": tokens, "parallelism": f"dp{world} (LPT, CFG pair per GPU)",
                        "packing": f"variable-length, <= {wl['max_tokens']} rows per batch",
                        "micro_batches_rank0": len(mbs)},
+            "per_rank": {"ms": [round(x, 2) for x in rank_ms], "rows": [int(x) for x in rank_rows],
+                         "rows_per_s": [round(r / (m / 1e3)) for r, m in zip(rank_rows, rank_ms)]},
             "clocks": clk,
         }), flush=True)
 
@@ -557,10 +575,13 @@ def run_ours(args, wl, world, rank, local):
             peak, peak_src = 2 * bf16_peak, "2x " + bf16_src + " (" + peak_src + ")"
     else:
         peak, peak_src = bf16_peak, bf16_src
-    traffic = _profiled_traffic("gemm_fp8_ff1_medium.md") if (lin.fp8 and M == 16494) else None
+    # DRAM bytes of one launch from the committed ncu summary of this exact shape, when there is one
+    tprof = ("gemm_fp8_ff1_medium.md" if (lin.fp8 and M == 16494) else
+             "gemm_gptq_dense_ff1.md" if (lin.gptq is not None and M == 42368) else None)
+    traffic = _profiled_traffic(tprof) if tprof else None
     roofline_gemm = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
-                     "traffic_source": "profiles/gemm_fp8_ff1_medium.md (ncu dram read+write bytes, one launch)"
+                     "traffic_source": f"profiles/{tprof} (ncu dram read+write bytes, one launch)"
                      if traffic else None,
                      "per_launch": {"flops": flops, "ms": k_ms, "M": M, "N": Nw, "K": K}}
 
