@@ -80,7 +80,7 @@ int sa3_get_device_error(int* err);
 typedef struct {
   int kind;                 /* SA3_EPI_* */
   const float* bias;        /* [N] fp32 or NULL */
-  const void* residual;     /* bf16, row stride ld_residual; may alias C */
+  const void* residual;     /* C's dtype (bf16, or fp32 / fp16 below), row stride ld_residual; may alias C */
   long long ld_residual;
   const float* gate;        /* fp32 gate rows: batch b reads gate + b*ld_gate */
   long long ld_gate;
@@ -111,6 +111,11 @@ typedef struct {
      is. qk_rope_mask must be 0 in this mode. Zero-initialised callers get the 8-group behaviour. */
   const float* qk_gamma_table;
   int qk_table_groups;
+  /* nonzero (with c_f32 zero): C and residual are fp16, the half-precision residual stream. Supported for
+     SA3_EPI_STORE / SILU (any row remap) and the residual kinds; an in-place residual (residual == C, same row
+     stride, no row remap, no amax_out) is added by a TMA reduce-add in fp16: the L2 adds fp16(acc) to C with
+     round-to-nearest. Other combinations return SA3_ERR_UNSUPPORTED. */
+  int c_f16;
 } sa3_epilogue;
 
 int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int K, long long lda, long long ldb,

@@ -47,6 +47,10 @@ class Cfg:
     # FP8 definition evaluated at the activations a bf16 model actually quantizes: e4m3 rounding is
     # discontinuous, so the fp32-activation definition is itself ~2-3e-2 away from it at these shapes.
     act_bf16: bool = False
+    # The residual stream held in fp16 between the layers (the precision of the reference's half-precision GPU
+    # deployment, loading_utils.py:69-70): project_in's output and the memory tokens are stored in fp16, and every
+    # residual update adds the fp16-rounded branch to the fp16 stream and rounds the sum to fp16.
+    stream_f16: bool = False
 
 
 # Linears the quantized variants replace (suffixes of the reference key names).
@@ -111,6 +115,17 @@ def _fp16(t: torch.Tensor) -> torch.Tensor:
 def _b(cfg: Cfg, t: torch.Tensor) -> torch.Tensor:
     """A tensor the bf16 deployment stores in bf16 (Cfg.act_bf16); unchanged otherwise."""
     return t.bfloat16().float() if cfg.act_bf16 else t
+
+
+def _s(cfg: Cfg, t: torch.Tensor) -> torch.Tensor:
+    """A value the residual stream stores (Cfg.stream_f16: rounded to fp16)."""
+    return t.half().float() if cfg.stream_f16 else t
+
+
+def _add(cfg: Cfg, res: torch.Tensor, delta: torch.Tensor) -> torch.Tensor:
+    """A residual update of the stream: res + delta, with fp16 rounding of both the branch and the sum when the
+    stream is fp16."""
+    return _s(cfg, res + _s(cfg, delta))
 
 
 def _bn(cfg: Cfg, lin: "Linears", t: torch.Tensor) -> torch.Tensor:
@@ -232,19 +247,19 @@ def block_forward(lin: Linears, sd, p: str, x, cfg: Cfg, global_cond6, freqs, co
     res = x
     y = _bn(cfg, lin, R.modulate(R.rms_norm(x, sd[p + ".pre_norm.gamma"].float(), cfg.norm_eps), sc_s, sh_s))
     y = self_attention(lin, sd, p + ".self_attn", y, cfg, freqs, valid, segs)
-    x = R.gate_residual(y, g_s, res)
+    x = _add(cfg, res, R.gate_residual(y, g_s, torch.zeros_like(res)))
     if context is not None and (p + ".cross_attn.to_q.weight") in sd:
         c = _bn(cfg, lin, R.rms_norm(x, sd[p + ".cross_attend_norm.gamma"].float(), cfg.norm_eps))
-        x = x + cross_attention(lin, sd, p + ".cross_attn", c, context, cfg, segs)
+        x = _add(cfg, x, cross_attention(lin, sd, p + ".cross_attn", c, context, cfg, segs))
     if local_add_cond is not None and (p + ".to_local_embed.0.weight") in sd:
         def emb_of(lc, n):
             e = lin(p + ".to_local_embed.2", _b(cfg, R.silu(lin(p + ".to_local_embed.0", _b(cfg, lc)))))
             pad = n - e.shape[-2]   # _left_pad_to_match (transformer.py:77-88)
             return F.pad(e, (0, 0, pad, 0)) if pad > 0 else e[..., -n:, :]
         if segs is None:
-            x = x + emb_of(local_add_cond, x.shape[1])
+            x = _add(cfg, x, emb_of(local_add_cond, x.shape[1]))
         else:
-            x = x + torch.cat([emb_of(lc, s1 - s0) for lc, (s0, s1) in zip(local_add_cond, segs)])[None]
+            x = _add(cfg, x, torch.cat([emb_of(lc, s1 - s0) for lc, (s0, s1) in zip(local_add_cond, segs)])[None])
     res = x
     y = _bn(cfg, lin, R.modulate(R.rms_norm(x, sd[p + ".ff_norm.gamma"].float(), cfg.norm_eps), sc_f, sh_f))
     if valid is None:
@@ -253,7 +268,7 @@ def block_forward(lin: Linears, sd, p: str, x, cfg: Cfg, global_cond6, freqs, co
         packed = lin(p + ".ff.ff.2", _b(cfg, R.swiglu(lin(p + ".ff.ff.0.proj", y[valid]))))
         y = torch.zeros_like(y)
         y[valid] = packed
-    return R.gate_residual(y, g_f, res)
+    return _add(cfg, res, R.gate_residual(y, g_f, torch.zeros_like(res)))
 
 
 def dit_inner_forward(lin: Linears, sd, cfg: Cfg, x, t, cross_attn_cond=None, global_embed=None,
@@ -268,10 +283,10 @@ def dit_inner_forward(lin: Linears, sd, cfg: Cfg, x, t, cross_attn_cond=None, gl
     wpre = sd["preprocess_conv.weight"].float()[:, :, 0]
     x = _b(cfg, x.float())
     x = torch.einsum("oc,bct->bot", wpre, x) + x
-    h = lin("transformer.project_in", x.transpose(1, 2))
+    h = _s(cfg, lin("transformer.project_in", x.transpose(1, 2)))
     B = h.shape[0]
     if cfg.num_memory_tokens:
-        h = torch.cat([sd["transformer.memory_tokens"].float().expand(B, -1, -1), h], dim=1)
+        h = torch.cat([_s(cfg, sd["transformer.memory_tokens"].float()).expand(B, -1, -1), h], dim=1)
     freqs = R.rotary_freqs(h.shape[1], max(cfg.embed_dim // cfg.num_heads // 2, 32))
     valid = None
     if padding_mask is not None:
@@ -309,9 +324,9 @@ def dit_inner_forward_packed(lin: Linears, sd, cfg: Cfg, xs, t, cross_attn_cond=
     rows, segs, pos, rb, r0 = [], [], [], [], 0
     for b, x in enumerate(xs):
         x = _b(cfg, x.float())
-        hb = lin("transformer.project_in", (wpre @ x + x).transpose(0, 1))
+        hb = _s(cfg, lin("transformer.project_in", (wpre @ x + x).transpose(0, 1)))
         if nm:
-            hb = torch.cat([sd["transformer.memory_tokens"].float().reshape(nm, -1), hb])
+            hb = torch.cat([_s(cfg, sd["transformer.memory_tokens"].float()).reshape(nm, -1), hb])
         rows.append(hb)
         segs.append((r0, r0 + hb.shape[0]))
         pos.append(torch.arange(hb.shape[0]))

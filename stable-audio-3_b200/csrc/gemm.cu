@@ -75,6 +75,7 @@ struct StoreStage {
   int uses;                // residual: chunks loaded so far (barrier phase)
   int pending;             // residual: loads issued and not yet consumed
   int red;                 // in-place residual kinds: the result is added into C by TMA reduce-add
+  int f16;                 // reduce-add into an fp16 C: one 32 x 32 box per chunk, buffers alternate by `next`
 };
 
 // This thread's row of the chunk (v, columns col..col+31 of output row row0 + lane) -> bf16 -> TMA.
@@ -125,6 +126,26 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float (&v)[
       v[i * 8 + 2 * j + 1] = f.y;
     }
   }
+}
+
+__device__ __forceinline__ void load_f16x32(const __half* p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = q[i];
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(h[j]);
+      v[i * 8 + 2 * j] = f.x;
+      v[i * 8 + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 __device__ __forceinline__ void load_f32x32(const float* p, float (&v)[32]) {
@@ -473,6 +494,8 @@ __device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int o
     float r[32];
     if (e.c_f32)
       load_f32x32(reinterpret_cast<const float*>(e.residual) + (long long)orow * e.ld_residual + nc, r);
+    else if (e.c_f16)
+      load_f16x32(reinterpret_cast<const __half*>(e.residual) + (long long)orow * e.ld_residual + nc, r);
     else
       load_bf16x32(reinterpret_cast<const __nv_bfloat16*>(e.residual) + (long long)orow * e.ld_residual + nc, r);
     if (KIND == SA3_EPI_GATED_RESIDUAL) {
@@ -490,6 +513,25 @@ __device__ __forceinline__ void pg_store_chunk(const GemmParams& p, int m, int o
     if (e.amax_out) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+  } else if (e.c_f16) {
+    uint4* q = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.C) + (long long)orow * p.ldc + nc);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 u;
+      u.x = pack_f16x2(v[i * 8 + 0], v[i * 8 + 1]);
+      u.y = pack_f16x2(v[i * 8 + 2], v[i * 8 + 3]);
+      u.z = pack_f16x2(v[i * 8 + 4], v[i * 8 + 5]);
+      u.w = pack_f16x2(v[i * 8 + 6], v[i * 8 + 7]);
+      q[i] = u;
+      if (e.amax_out) {
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h[j]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
     }
   } else {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)orow * p.ldc + nc;
@@ -666,6 +708,26 @@ __device__ __forceinline__ void residual_reduce_chunk(StoreStage& st, const Gemm
     }
   }
   const int sw = (lane >> 1) & 3;
+  if (st.f16) {
+    // fp16 stream: this thread's 32 columns as fp16 in one 64-byte row of a 32 x 32 box, added by the L2
+    uint8_t* b = st.buf + st.next * 2048;
+    if (lane == 0) bulk_wait_read_all_but_one();  // the reduce issued two chunks ago has read this buffer
+    __syncwarp();
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = pack_f16x2(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ sw) * 16)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_reduce_add_2d(st.tm, b, nc, row0);
+      bulk_commit_group();
+    }
+    st.next ^= 1;
+    return;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     if (lane == 0) bulk_wait_read_all_but_one();
@@ -999,7 +1061,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
     uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + PG_SCRATCH_OFFSET + pg_rbar_offset());
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((PG_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
-                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3, p.epi.c_f16};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -1240,7 +1302,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     // bf16 TMA-store staging reuses the same region with 512-byte aligned 2 x 2 KB buffers per warp
     uint64_t* rbars = reinterpret_cast<uint64_t*>(smem + P2_SCRATCH_OFFSET + pg_rbar_offset());
     StoreStage stg{&tmC, p.tma_store == 2 ? &tmR : nullptr, smem + ((P2_SCRATCH_OFFSET + 511) & ~511) + (warp - 2) * 4096,
-                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3};
+                   rbars + 2 * (warp - 2), abort_flag, 0, 0, 0, p.tma_store == 3, p.epi.c_f16};
     StoreStage* stgp = p.tma_store ? &stg : nullptr;
     const sa3_epilogue& e = p.epi;
     const float sa = p.a_scale ? __ldg(p.a_scale) : 1.f;
@@ -1661,6 +1723,8 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
   sa3_epilogue e{};
   if (epi) e = *epi;
   if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_QK_NORM) return SA3_ERR_ARG;
+  if (e.c_f32 && e.c_f16) return SA3_ERR_ARG;
+  if (e.c_f16 && (e.kind == SA3_EPI_SWIGLU || e.kind == SA3_EPI_QK_NORM)) return SA3_ERR_UNSUPPORTED;
   if (e.kind == SA3_EPI_QK_NORM) {
     if (e.qk_group_width <= 0 || e.qk_group_width % 64) return SA3_ERR_ARG;
     if (e.qk_gamma_table) {
@@ -1714,11 +1778,11 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
               (e.kind != SA3_EPI_SWIGLU || N % GEMM_BN == 0);
   if (res_kind) fast = fast && aligned16(e.residual) && ((e.ld_residual * celt) % 16 == 0);
   if (e.kind == SA3_EPI_GATED_RESIDUAL) fast = fast && aligned16(e.gate) && (e.ld_gate % 4 == 0);
-  if (!fast && e.kind == SA3_EPI_QK_NORM) return SA3_ERR_UNSUPPORTED;  // only the persistent kernel fuses it
+  if (!fast && (e.kind == SA3_EPI_QK_NORM || e.c_f16)) return SA3_ERR_UNSUPPORTED;  // only the persistent kernels
   // bf16 outputs without a row remap leave through TMA stores (tmC); otherwise tmC is unused
   CUtensorMap tmC = tmA;
   p.tma_store = 0;
-  if (fast && !e.c_f32 && !e.out_row_map && e.seg_in == 0 &&
+  if (fast && !e.c_f32 && !e.c_f16 && !e.out_row_map && e.seg_in == 0 &&
       (e.kind == SA3_EPI_STORE || e.kind == SA3_EPI_SILU || e.kind == SA3_EPI_SWIGLU || e.kind == SA3_EPI_QK_NORM)) {
     const uint64_t ccols = e.kind == SA3_EPI_SWIGLU ? (uint64_t)N / 2 : (uint64_t)N;
     if ((rc = make_tmap_2d(&tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ccols, (uint64_t)M, (uint64_t)ldc, 32, 32,
@@ -1741,6 +1805,15 @@ extern "C" int sa3_gemm(const void* A, const void* B, void* C, int M, int N, int
         return rc;
       p.tma_store = 2;
     }
+  }
+  // fp16 residual stream, in place: reduce-add of the fp16-rounded result into C (tma_store = 3 with an fp16 map of
+  // 32 x 32 boxes, the bf16 store layout)
+  if (fast && e.c_f16 && res_kind && !e.out_row_map && e.seg_in == 0 && e.residual == C && e.ld_residual == ldc &&
+      !e.amax_out && sa3_residual_reduce_enabled()) {
+    if ((rc = make_tmap_2d(&tmC, C, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 32, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+    p.tma_store = 3;
   }
   if (fast && M >= SA3_PAIR_MIN_ROWS) {
     // enough rows for 256-row tiles: the 2-SM kernel (FP8 or bf16). Its A and B boxes are 128 rows.
@@ -1774,6 +1847,8 @@ extern "C" int sa3_gptq_gemm(const void* A, const void* qw, const float* sz, voi
   sa3_epilogue e{};
   if (epi) e = *epi;
   if (e.kind < SA3_EPI_STORE || e.kind > SA3_EPI_QK_NORM) return SA3_ERR_ARG;
+  if (e.c_f32 && e.c_f16) return SA3_ERR_ARG;
+  if (e.c_f16 && (e.kind == SA3_EPI_SWIGLU || e.kind == SA3_EPI_QK_NORM)) return SA3_ERR_UNSUPPORTED;
   const int celt = e.c_f32 ? 4 : 2;
   if ((ldc * celt) % 16) return SA3_ERR_ALIGN;
   if (e.kind == SA3_EPI_SWIGLU ? ldc < N / 2 : ldc < N) return SA3_ERR_ARG;

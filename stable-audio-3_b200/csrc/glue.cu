@@ -9,6 +9,8 @@
 //                      transformer.py:589-595) + partial rotary embedding on the
 //                      first 32 of 64 dims, fp32 math (apply_rotary_pos_emb /
 //                      rotate_half, transformer.py:296-322; use at :755-781).
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_util.h"
 
@@ -21,6 +23,16 @@ constexpr float kE4M3Max = 448.f;
 // inv = 448 / max(amax, 1e-12) quantises (one IEEE division per thread, a multiply per element).
 __device__ __forceinline__ float quant_scale(const float* amax) { return fmaxf(__ldg(amax), 1e-12f) / kE4M3Max; }
 __device__ __forceinline__ float quant_inv_scale(const float* amax) { return kE4M3Max / fmaxf(__ldg(amax), 1e-12f); }
+
+__device__ __forceinline__ void unpack8_f16(const uint4& u, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -81,6 +93,7 @@ __device__ __forceinline__ void block_amax_commit(float v, float* amax_out) {
 struct NormParams {
   const void* x;
   int x_f32;
+  int x_f16;  // the fp16 residual stream (x_f32 zero)
   void* out;
   int rows, D;
   long long ldx, ldo;
@@ -118,6 +131,9 @@ __device__ __forceinline__ void norm_load_row(const NormParams& p, int row, floa
         const float4 a = xr[0], b = xr[1];
         v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
         v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      } else if (p.x_f16) {
+        const __half* xr = reinterpret_cast<const __half*>(p.x) + (long long)row * p.ldx;
+        unpack8_f16(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
       } else {
         const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(p.x) + (long long)row * p.ldx;
         unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
@@ -255,6 +271,25 @@ __device__ __forceinline__ void norm_load_row4(const NormParams& p, int row, int
 #pragma unroll
   for (int k = 0; k < NV; ++k) v[k] = ld_f4_hint(xr + lane + 32 * k, pol);
 }
+// fp16 stream: the same four elements per (lane, k) as the fp32 kernel, in one 8-byte load, kept packed until
+// used so the loads stay in flight.
+__device__ __forceinline__ uint2 ld_u2_hint(const uint2* ptr, uint64_t pol) {
+  uint2 v;
+  asm volatile("ld.global.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;" : "=r"(v.x), "=r"(v.y) : "l"(ptr), "l"(pol));
+  return v;
+}
+template <int NV>
+__device__ __forceinline__ void norm_load_row4(const NormParams& p, int row, int lane, uint64_t pol, uint2 (&v)[NV]) {
+  const uint2* xr = reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.x) + (long long)row * p.ldx);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = ld_u2_hint(xr + lane + 32 * k, pol);
+}
+__device__ __forceinline__ float4 norm_f4(const float4& v) { return v; }
+__device__ __forceinline__ float4 norm_f4(const uint2& v) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
 
 // CFG batch of a row for the modulation table (every lane reads the same entry: one transaction).
 __device__ __forceinline__ int norm_batch_load(const NormParams& p, int row) {
@@ -263,15 +298,17 @@ __device__ __forceinline__ int norm_batch_load(const NormParams& p, int row) {
   return __ldg(p.row_batch + row);
 }
 
-template <int NV, bool DB>  // NV float4s per lane: D = 128 * NV; DB: next row prefetched
+// NV groups of four elements per lane: D = 128 * NV; DB: next row prefetched; XH: the stream is fp16 (8-byte loads)
+template <int NV, bool DB, bool XH>
 __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+  using Raw = typename std::conditional<XH, uint2, float4>::type;  // the fp16 stream is kept packed until used
   grid_dep_wait();
   extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = gridDim.x * (NORM_D_THREADS / 32);
   int li = blockIdx.x * (NORM_D_THREADS / 32) + warp;
   const uint64_t pol = norm_l2_policy(p.mode);
-  float4 v[NV];
+  Raw v[NV];
   int vb = 0;  // CFG batch of the row in v, requested with the row so its latency overlaps the row's
   if (li < p.rows) {
     vb = norm_batch_load(p, norm_row(p, li));
@@ -316,7 +353,7 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
   while (li < p.rows) {
     const int row = norm_row(p, li);
     const int nli = li + nw;
-    float4 nv[DB ? NV : 1];
+    Raw nv[DB ? NV : 1];
     int nvb = 0;
     if (DB && nli < p.rows) {
       nvb = norm_batch_load(p, norm_row(p, nli));
@@ -325,10 +362,11 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
     float ss4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
-      ss4[0] = fmaf(v[k].x, v[k].x, ss4[0]);
-      ss4[1] = fmaf(v[k].y, v[k].y, ss4[1]);
-      ss4[2] = fmaf(v[k].z, v[k].z, ss4[2]);
-      ss4[3] = fmaf(v[k].w, v[k].w, ss4[3]);
+      const float4 x = norm_f4(v[k]);
+      ss4[0] = fmaf(x.x, x.x, ss4[0]);
+      ss4[1] = fmaf(x.y, x.y, ss4[1]);
+      ss4[2] = fmaf(x.z, x.z, ss4[2]);
+      ss4[3] = fmaf(x.w, x.w, ss4[3]);
     }
     const float r = rsqrtf(warp_sum((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / (float)p.D + p.eps);
     const int b = vb;
@@ -351,8 +389,9 @@ __global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsno
           sh = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      const float y0 = fmaf(v[k].x * r, a.x, sh.x), y1 = fmaf(v[k].y * r, a.y, sh.y);
-      const float y2 = fmaf(v[k].z * r, a.z, sh.z), y3 = fmaf(v[k].w * r, a.w, sh.w);
+      const float4 x = norm_f4(v[k]);
+      const float y0 = fmaf(x.x * r, a.x, sh.x), y1 = fmaf(x.y * r, a.y, sh.y);
+      const float y2 = fmaf(x.z * r, a.z, sh.z), y3 = fmaf(x.w * r, a.w, sh.w);
       if (p.mode == SA3_NORM_AMAX) {
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
       } else if (p.out_dtype == SA3_DT_E4M3) {
@@ -444,6 +483,8 @@ __global__ void __launch_bounds__(NORM_BULK_THREADS, 2) rmsnorm_bulk_kernel(Norm
             const float4 b = reinterpret_cast<const float4*>(rb)[2 * c + 1];
             v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
             v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+          } else if (p.x_f16) {
+            unpack8_f16(reinterpret_cast<const uint4*>(rb)[c], v[i]);
           } else {
             unpack8(reinterpret_cast<const uint4*>(rb)[c], v[i]);
           }
@@ -676,7 +717,7 @@ struct ConvParams {
   const void* x;
   void* out;
   const int* src_rows;
-  int x_f32, out_f32;
+  int x_dt, out_dt;  // SA3_DT_BF16 / SA3_DT_F16 / SA3_DT_F32
   int rows, cols;
   long long ldx, ldo;
 };
@@ -690,17 +731,32 @@ __global__ void __launch_bounds__(256) convert_kernel(ConvParams p) {
     const int c = (int)(i - r * cpr);
     const long long rs = p.src_rows ? (long long)__ldg(p.src_rows + r) : r;
     float v[8];
-    if (p.x_f32) {
+    if (p.x_dt == SA3_DT_F32) {
       const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + rs * p.ldx + c * 8);
       const float4 a = s[0], b = s[1];
       v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else if (p.x_dt == SA3_DT_F16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + rs * p.ldx + c * 8);
+      const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+      }
     } else {
       unpack8(*reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.x) + rs * p.ldx + c * 8), v);
     }
-    if (p.out_f32) {
+    if (p.out_dt == SA3_DT_F32) {
       float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + r * p.ldo + c * 8);
       d[0] = make_float4(v[0], v[1], v[2], v[3]);
       d[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else if (p.out_dt == SA3_DT_F16) {
+      uint4 u;
+      __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + r * p.ldo + c * 8) = u;
     } else {
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + r * p.ldo + c * 8) = pack8(v);
     }
@@ -724,7 +780,7 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
                                     int shift_off, int rows_per_batch, const int* row_batch, int mode, int out_dtype,
                                     const float* quant_amax, float* scale_out, float* amax_out, void* stream) {
   if (!x || rows <= 0 || D <= 0 || (D % 8) || ldx < D) return SA3_ERR_ARG;
-  if (x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32) return SA3_ERR_DTYPE;
+  if (x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32 && x_dtype != SA3_DT_F16) return SA3_ERR_DTYPE;
   if (!aligned16(x) || (ldx % 8)) return SA3_ERR_ALIGN;
   if (mode == SA3_NORM_AMAX) {
     if (!amax_out) return SA3_ERR_ARG;
@@ -745,6 +801,7 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   NormParams p;
   p.x = x;
   p.x_f32 = x_dtype == SA3_DT_F32;
+  p.x_f16 = x_dtype == SA3_DT_F16;
   p.out = out;
   p.rows = rows;
   p.D = D;
@@ -770,7 +827,8 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   const bool vec = aligned16(gamma) && (!mod || (aligned16(mod) && ld_mod % 4 == 0 && scale_off % 4 == 0 &&
                                                     shift_off % 4 == 0));
   const int rowbytes = D * (x_dtype == SA3_DT_F32 ? 4 : 2);
-  if (vec && x_dtype == SA3_DT_F32 && D % 128 == 0 && D <= 4096 && ldx % 4 == 0 &&
+  const bool xh = x_dtype == SA3_DT_F16;
+  if (vec && (x_dtype == SA3_DT_F32 || xh) && D % 128 == 0 && D <= 4096 && ldx % 4 == 0 &&
       (mode == SA3_NORM_AMAX || out_dtype == SA3_DT_BF16 ? (ldo % 4 == 0) : (ldo % 4 == 0))) {
     int tab_batches = 1;
     if (mod) tab_batches = (!row_batch && rows_per_batch > 0 && (rows + rows_per_batch - 1) / rows_per_batch <= 2)
@@ -779,11 +837,16 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
     const int smem = tab_batches * 2 * D * 4;
     int gridd = (rows + 7) / 8;
     int rc;
-#define SA3_NORM_DIRECT(V, DB)                                                                              \
-  case V:                                                                                                   \
-    if (gridd > 148 * ((DB || V > 12) ? 2 : 3)) gridd = 148 * ((DB || V > 12) ? 2 : 3);                     \
-    if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB>, 2 * 2 * 2048 * 4))) return rc;                      \
-    launch_ex(rmsnorm_direct_kernel<V, DB>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
+#define SA3_NORM_DIRECT(V, DB)                                                                                 \
+  case V:                                                                                                      \
+    if (gridd > 148 * ((DB || V > 12) ? 2 : 3)) gridd = 148 * ((DB || V > 12) ? 2 : 3);                        \
+    if (xh) {                                                                                                  \
+      if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB, true>, 2 * 2 * 2048 * 4))) return rc;                 \
+      launch_ex(rmsnorm_direct_kernel<V, DB, true>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
+    } else {                                                                                                   \
+      if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB, false>, 2 * 2 * 2048 * 4))) return rc;                \
+      launch_ex(rmsnorm_direct_kernel<V, DB, false>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
+    }                                                                                                          \
     break;
     switch (D / 128) {
       SA3_NORM_DIRECT(8, true)
@@ -893,10 +956,10 @@ extern "C" int sa3_qk_norm_rope(void* buf, int rows, long long ld, int heads, in
 extern "C" int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype, int rows, int cols, long long ldx,
                            long long ldo, const int* src_rows, void* stream) {
   if (!x || !out || rows <= 0 || cols <= 0 || (cols % 8) || ldx < cols || ldo < cols) return SA3_ERR_ARG;
-  if ((x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32) || (out_dtype != SA3_DT_BF16 && out_dtype != SA3_DT_F32))
-    return SA3_ERR_DTYPE;
+  auto known = [](int d) { return d == SA3_DT_BF16 || d == SA3_DT_F16 || d == SA3_DT_F32; };
+  if (!known(x_dtype) || !known(out_dtype)) return SA3_ERR_DTYPE;
   if (!aligned16(x) || !aligned16(out) || (ldx % 8) || (ldo % 8)) return SA3_ERR_ALIGN;
-  ConvParams p{x, out, src_rows, x_dtype == SA3_DT_F32, out_dtype == SA3_DT_F32, rows, cols, ldx, ldo};
+  ConvParams p{x, out, src_rows, x_dtype, out_dtype, rows, cols, ldx, ldo};
   launch_ex(convert_kernel, dim3(grid_for((long long)rows * (cols / 8), 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, p);
   return launch_status();
 }

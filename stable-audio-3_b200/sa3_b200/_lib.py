@@ -58,6 +58,7 @@ class Epilogue(ctypes.Structure):
         ("out_row_map", c_vp),
         ("qk_gamma_table", c_vp),
         ("qk_table_groups", c_int),
+        ("c_f16", c_int),
     ]
 
 

@@ -95,7 +95,8 @@ class _Workspace:
     original token positions."""
 
     def __init__(self, cfg, lengths, Tc: int, dev, fp8: bool, gptq_k: int = 0, local_all: bool = False,
-                 split: Optional["_seqsplit.SeqSplit"] = None, kv_all: bool = False, valid=None):
+                 split: Optional["_seqsplit.SeqSplit"] = None, kv_all: bool = False, valid=None,
+                 stream_dtype: torch.dtype = torch.float16):
         D = cfg.embed_dim
         # a sequence-split rank holds stream tokens [tok_start, tok_end) of each sequence: memory tokens only on
         # rank 0, RoPE at global positions
@@ -167,7 +168,7 @@ class _Workspace:
         self.lat_rows = torch.from_numpy(lat_rows).to(dev)
         self.mem_rows = torch.from_numpy(mem_rows).to(dev) if nm else None
         bf = torch.bfloat16
-        self.h = torch.empty(M, D, device=dev, dtype=torch.float32)  # fp32 residual stream
+        self.h = torch.empty(M, D, device=dev, dtype=stream_dtype)  # residual stream (fp16 or fp32)
         self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
         self.qkv = torch.empty(M, nq * D, device=dev, dtype=bf)
         if split is not None:
@@ -208,9 +209,13 @@ class _Workspace:
 
 
 class DiTEngine:
-    def __init__(self, module, mode: str = "bf16", gptq_layers: Optional[dict] = None, device="cuda"):
+    def __init__(self, module, mode: str = "bf16", gptq_layers: Optional[dict] = None, device="cuda",
+                 stream_dtype: torch.dtype = torch.float16):
         if mode not in ("bf16", "fp8", "gptq"):
             raise ValueError(mode)
+        if stream_dtype not in (torch.float16, torch.float32):
+            raise ValueError(f"residual stream dtype {stream_dtype}: fp16 or fp32")
+        self.stream_dtype = stream_dtype
         if not torch.cuda.is_available():
             raise RuntimeError("DiTEngine needs a CUDA device (no CPU path)")
         _lib.load()
@@ -236,7 +241,7 @@ class DiTEngine:
         w_out = (eye + sd["postprocess_conv.weight"][:, :, 0]) @ sd["transformer.project_out.weight"]
         self.lin["project_in"] = Lin(w_in.to(self.dev, torch.bfloat16).contiguous(), None, None, False)
         self.lin["project_out"] = Lin(w_out.to(self.dev, torch.bfloat16).contiguous(), None, None, False)
-        self.memory = sd["transformer.memory_tokens"].to(self.dev, torch.float32) if cfg.num_memory_tokens else None
+        self.memory = sd["transformer.memory_tokens"].to(self.dev, stream_dtype) if cfg.num_memory_tokens else None
         self.sst = torch.stack([sd[f"transformer.layers.{i}.to_scale_shift_gate"] for i in range(cfg.depth)]).to(
             self.dev)
         self.gam = {k: v.to(self.dev).contiguous() for k, v in sd.items() if k.endswith("gamma")}
@@ -324,7 +329,7 @@ class DiTEngine:
             self.ws = ws = None
             self.ws = ws = _Workspace(self.cfg, lengths, Tc, self.dev, self.fp8, self.gptq_k,
                                       local_all=self.loc1_all is not None, split=split,
-                                      kv_all=self.kv_all is not None, valid=valid)
+                                      kv_all=self.kv_all is not None, valid=valid, stream_dtype=self.stream_dtype)
             ws.valid_key = vkey
         if self.rope is None or self.rope.shape[0] < ws.max_pos:
             self.rope = ops.rope_table(ws.max_pos, 32, device=self.dev)

@@ -9,9 +9,11 @@ Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
   qkv_fp8_qk to_qkv as in the block: qk RMSNorm + RoPE epilogue
   ff2_fp8    linear_out  FP8 GEMM  M x 1536 x 6144, gate + fp32 residual epilogue
   out_fp8    to_out      FP8 GEMM  M x 1536 x 1536, gate + fp32 residual epilogue
+  ff2_fp8_f16, out_fp8_f16, local2_bf16_f16  the residual epilogues into the fp16 stream
   attn_diff  differential SWA, 24 heads, window (256, 256)
   attn_cross differential cross-attention over 128 context tokens
   norm_fp8   RMSNorm + modulate of the fp32 stream: amax pass + e4m3 write pass
+  norm_fp8_f16  the same on the fp16 stream
   qknorm     qk RMSNorm + RoPE on q, k, q_diff, k_diff in place
   ff1_gptq   GLU.proj GPTQ int4 GEMM (group 128, act-order gather included separately), M = 16 x 2648
   ff1_gptq_dense  the same layer on the large-batch path: dequantise once (original channel order) + bf16 GEMM
@@ -55,9 +57,11 @@ def case(name: str, iters: int) -> dict:
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(0)
     one = torch.ones(1, device=dev)
-    if name in ("ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8"):
+    if name in ("ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8", "ff2_fp8_f16", "out_fp8_f16"):
+        # _f16: the gated residual goes into the fp16 stream (TMA reduce-add in fp16) instead of the fp32 one
+        stream = torch.float16 if name.endswith("_f16") else torch.float32
         n, k = {"ff1_fp8": (12288, 1536), "qkv_fp8": (7680, 1536), "qkv_fp8_qk": (7680, 1536), "ff2_fp8": (1536, 6144),
-                "out_fp8": (1536, 1536)}[name]
+                "out_fp8": (1536, 1536)}[name.replace("_f16", "")]
         a = torch.randn(M, k, device=dev).to(torch.float8_e4m3fn)
         wq, s = _fp8_weight(n, k, dev, g)
         if name == "ff1_fp8":
@@ -80,13 +84,13 @@ def case(name: str, iters: int) -> dict:
                       cos_sin=cs, row_pos=pos)
             fn = lambda: ops.gemm(a, wq, out, a_scale=one, b_scale=s, kind=_lib.EPI_QK_NORM, qk=qk)  # noqa: E731
         else:
-            h = torch.randn(M, n, device=dev)
+            h = torch.randn(M, n, device=dev).to(stream)
             gate = torch.randn(B, n, device=dev)
             fn = lambda: ops.gemm(a, wq, h, a_scale=one, b_scale=s, kind=_lib.EPI_GATED_RESIDUAL,  # noqa: E731
                                   residual=h, gate=gate, rows_per_batch=N)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 2.0 * M * n * k / ms / 1e9}
-    if name in ("out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16"):
+    if name in ("out_fp8_store", "local2_bf16", "local2_bf16_f16", "local2_bf16_store", "local1_bf16"):
         # epilogue cost: the same M x 1536 x 1536 shapes with a plain bf16 store vs the fp32 residual
         k = 264 if name == "local1_bf16" else 1536
         n = 1536
@@ -99,8 +103,8 @@ def case(name: str, iters: int) -> dict:
         else:
             a = torch.randn(M, k, device=dev).bfloat16()
             w = (torch.randn(n, k, generator=g) * 0.02).bfloat16().to(dev)
-            if name == "local2_bf16":
-                h = torch.randn(M, n, device=dev)
+            if name in ("local2_bf16", "local2_bf16_f16"):
+                h = torch.randn(M, n, device=dev).to(torch.float16 if name.endswith("_f16") else torch.float32)
                 fn = lambda: ops.gemm(a, w, h, kind=_lib.EPI_RESIDUAL, residual=h)  # noqa: E731
             else:
                 out = torch.empty(M, n, device=dev, dtype=torch.bfloat16)
@@ -151,8 +155,9 @@ def case(name: str, iters: int) -> dict:
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 2.0 * Mg * 12288 * 1536 / ms / 1e9, "dequant_ms": ms_dq,
                 "dequant_GBps": 12288 * 1536 * 2.5 / ms_dq / 1e6, "gemm_ms": ms_mm}
-    if name == "norm_fp8":
-        x = torch.randn(M, D, device=dev)
+    if name in ("norm_fp8", "norm_fp8_f16"):
+        # RMSNorm + modulate + FP8 quantisation of the residual stream (fp32, or the fp16 stream for _f16)
+        x = torch.randn(M, D, device=dev).to(torch.float16 if name.endswith("f16") else torch.float32)
         gam = torch.ones(D, device=dev)
         mod = torch.randn(B, 6 * D, device=dev) * 0.1
         am = torch.zeros(1, device=dev)
@@ -164,7 +169,7 @@ def case(name: str, iters: int) -> dict:
             ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, out=out,
                                  quant_amax=am, scale_out=sc)
         ms = _time(fn, iters)
-        return {"case": name, "ms": ms, "GBps": (2 * M * D * 4 + M * D) / ms / 1e6}
+        return {"case": name, "ms": ms, "GBps": (2 * M * D * x.element_size() + M * D) / ms / 1e6}
     if name in ("quant_attn", "quant_ff"):
         # activation quantisation with the scale from a producer's max|x|: M x 1536 (attention output) and
         # M x 6144 (FF hidden)
@@ -187,7 +192,9 @@ def case(name: str, iters: int) -> dict:
     raise ValueError(name)
 
 
-CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "out_fp8", "out_fp8_store", "local2_bf16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8", "quant_attn", "quant_ff", "qknorm", "ff1_gptq", "ff1_gptq_dense"]
+CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "ff2_fp8_f16", "out_fp8", "out_fp8_f16", "out_fp8_store",
+         "local2_bf16", "local2_bf16_f16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8",
+         "norm_fp8_f16", "quant_attn", "quant_ff", "qknorm", "ff1_gptq", "ff1_gptq_dense"]
 
 
 def main():

@@ -163,15 +163,22 @@ class DiffusionTransformer(nn.Module):
         self._engine = None
         self._mode = "bf16"
         self._gptq = None
+        self._stream = "fp16"
         self._graphs = None
 
-    def quantize(self, mode: str = "fp8", gptq_layers: Optional[dict] = None) -> "DiffusionTransformer":
+    def quantize(self, mode: str = "fp8", gptq_layers: Optional[dict] = None,
+                 stream: str = "fp16") -> "DiffusionTransformer":
         """Select the linear path: 'bf16', 'fp8' (e4m3 weights, per-channel scales, dynamic
         per-tensor activation scale) or 'gptq' (int4 weight-only; gptq_layers maps reference
-        linear names to packed (qweight, qzeros, scales, g_idx))."""
+        linear names to packed (qweight, qzeros, scales, g_idx)), and the precision of the residual
+        stream between the blocks: 'fp16' (the precision of the reference's half-precision GPU
+        deployment, StableAudioModel.from_pretrained(model_half=True) -> model.to(torch.float16),
+        stable_audio_3/loading_utils.py:69-70) or 'fp32'."""
         if mode not in ("bf16", "fp8", "gptq"):
             raise ValueError(mode)
-        self._mode, self._gptq, self._engine = mode, gptq_layers, None
+        if stream not in ("fp16", "fp32"):
+            raise ValueError(stream)
+        self._mode, self._gptq, self._stream, self._engine = mode, gptq_layers, stream, None
         return self
 
     def enable_cuda_graph(self, enabled: bool = True) -> "DiffusionTransformer":
@@ -185,7 +192,8 @@ class DiffusionTransformer(nn.Module):
         from .engine import DiTEngine
 
         if self._engine is None:
-            self._engine = DiTEngine(self, mode=self._mode, gptq_layers=self._gptq)
+            self._engine = DiTEngine(self, mode=self._mode, gptq_layers=self._gptq,
+                                     stream_dtype=torch.float16 if self._stream == "fp16" else torch.float32)
         return self._engine
 
     def forward(self, x, t, cross_attn_cond=None, cross_attn_cond_mask=None, negative_cross_attn_cond=None,

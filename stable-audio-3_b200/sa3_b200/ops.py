@@ -74,6 +74,7 @@ def _epilogue(kind, bias, residual, gate, rows_per_batch, row_batch, amax_out, s
     if seg is not None:
         epi.seg_in, epi.seg_out, epi.seg_offset = seg
     epi.c_f32 = 1 if out.dtype == torch.float32 else 0
+    epi.c_f16 = 1 if out.dtype == torch.float16 else 0
     epi.out_row_map = _ptr(out_row_map)
     if qk is not None:
         gams = list(qk.get("gammas", []))
@@ -120,8 +121,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
         if seg is not None or out_row_map is not None:
             raise RuntimeError("row remap needs an explicit out")
         out = torch.empty(M, ncols, device=a.device, dtype=torch.bfloat16)
-    if out.dtype not in (torch.bfloat16, torch.float32):
-        raise RuntimeError("gemm output is bf16 or fp32")
+    if out.dtype not in (torch.bfloat16, torch.float32, torch.float16):
+        raise RuntimeError("gemm output is bf16, fp32 or fp16")
     if kind == _lib.EPI_SWIGLU and out.dtype != torch.bfloat16:
         raise RuntimeError("SwiGLU epilogue writes bf16")
     if residual is not None and residual.dtype != out.dtype:
@@ -186,7 +187,7 @@ def absmax(x: torch.Tensor, amax_out: torch.Tensor) -> None:
 
 
 def convert(x: torch.Tensor, out: torch.Tensor, src_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out = x cast between fp32 and bf16; with src_rows (int32), out[r] = x[src_rows[r]]."""
+    """out = x cast between fp32, fp16 and bf16; with src_rows (int32), out[r] = x[src_rows[r]]."""
     _need_cuda(x, out, src_rows)
     rows, cols = out.shape
     _count()

@@ -178,6 +178,69 @@ def test_gemm_pair_short_k_many_tiles(cuda, variant):
     assert rel_fro(got, ref) < 5e-3
 
 
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("M", [300, 1030, 9000])
+def test_gemm_fp16_stream(cuda, M, fp8):
+    """Epilogues into an fp16 residual stream. In place (residual = C, no row map) the result is added by a TMA
+    reduce-add in fp16: C = fp16(C + fp16(gate * acc)); with an output-row map (the local-conditioning add and
+    project_in) the generic epilogue loads the fp16 residual and stores fp16(C + acc). M = 300 runs the single-SM
+    kernel, 1030 and 9000 the 2-SM kernel (9000: 36 tiles per pair, both TMEM accumulators). Against the fp32
+    product with the same fp16 roundings: at most one fp16 ulp apart, relative Frobenius <= 1e-3."""
+    from sa3_b200 import _lib, ops
+
+    g = _gen(M + 7 * fp8)
+    N, K, B = 512, 384, 2
+    x = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.05
+    bias = torch.randn(N, generator=g) * 0.1
+    res = (torch.randn(M, N, generator=g) * 2).half()
+    gate = torch.randn(B, N, generator=g)
+    rpb = (M + 1) // 2
+    bidx = torch.arange(M) // rpb
+    if fp8:
+        wq, sw = oq.quantize_weight_e4m3(w)
+        xd = x.to(cuda).bfloat16()
+        amax, s = torch.zeros(1, device=cuda), torch.zeros(1, device=cuda)
+        ops.absmax(xd, amax)
+        a = ops.quantize_e4m3(xd, amax, scale_out=s)
+        h = oq.fp8_linear(x.bfloat16().float(), wq, sw, bias)
+        args = dict(a_scale=s, b_scale=sw.to(cuda), bias=bias.to(cuda))
+        wd = wq.to(cuda)
+    else:
+        a, wd = x.bfloat16().to(cuda), w.bfloat16().to(cuda)
+        h = a.float().cpu() @ w.bfloat16().float().T + bias
+        args = dict(bias=bias.to(cuda))
+
+    def close(out, ref):
+        out = out.float().cpu()
+        ulp = torch.finfo(torch.float16).eps * ref.abs().clamp_min(2.0 ** -14)
+        assert ((out - ref).abs() <= 1.01 * ulp).float().mean().item() > 0.999
+        assert rel_fro(out, ref) < 1e-3
+
+    # in place, gated (to_out / FF2) and plain (cross to_out)
+    out = res.clone().to(cuda)
+    ops.gemm(a, wd, out, kind=_lib.EPI_GATED_RESIDUAL, residual=out, gate=gate.to(cuda), rows_per_batch=rpb, **args)
+    close(out, (res.float() + (h * torch.sigmoid(1 - gate[bidx])).half().float()).half().float())
+    out = res.clone().to(cuda)
+    ops.gemm(a, wd, out, kind=_lib.EPI_RESIDUAL, residual=out, **args)
+    close(out, (res.float() + h.half().float()).half().float())
+    # row-mapped residual and store into a larger stream (rows interleaved with untouched memory-token rows)
+    rmap = (torch.arange(M) * 2 + 1).to(torch.int32)
+    big = (torch.randn(2 * M + 1, N, generator=g)).half()
+    out = big.clone().to(cuda)
+    ops.gemm(a, wd, out, kind=_lib.EPI_RESIDUAL, residual=out, out_row_map=rmap.to(cuda), **args)
+    ref = big.clone().float()
+    ref[rmap.long()] = (big[rmap.long()].float() + h).half().float()
+    close(out, ref)
+    out = big.clone().to(cuda)
+    ops.gemm(a, wd, out, out_row_map=rmap.to(cuda), **args)
+    ref = big.clone().float()
+    ref[rmap.long()] = h.half().float()
+    close(out, ref)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+
 def test_gemm_epilogues(cuda):
     from sa3_b200 import ops, _lib
 
@@ -258,6 +321,13 @@ def test_convert_and_fp32_norm_input(cuda):
     gamma = 1 + 0.1 * torch.randn(1536, generator=g)
     y = ops.rmsnorm_modulate(x.to(cuda), gamma.to(cuda), 1e-5)
     assert max_rel(y, orf.rms_norm(x, gamma, 1e-5)) < 1e-2
+    # the fp16 stream: fp32 -> fp16 (round to nearest), fp16 -> bf16 with a row gather, fp16 -> fp32
+    xh = ops.convert(x.to(cuda), torch.empty(301, 1536, device=cuda, dtype=torch.float16))
+    assert torch.equal(xh.cpu(), x.half())
+    rows = torch.randperm(301, generator=g)[:150].to(torch.int32)
+    hb = ops.convert(xh, torch.empty(150, 1536, device=cuda, dtype=torch.bfloat16), src_rows=rows.to(cuda))
+    assert torch.equal(hb.cpu(), x.half()[rows.long()].bfloat16())
+    assert torch.equal(ops.convert(xh, torch.empty(301, 1536, device=cuda)).cpu(), x.half().float())
 
 
 # ----------------------------------------------------------------------------- glue
@@ -289,11 +359,13 @@ def test_rmsnorm_modulate(cuda):
     assert max_rel(out, orf.rms_norm(x.float(), gamma, 1e-5)) < 1e-2
 
 
+@pytest.mark.parametrize("stream", [torch.float32, torch.float16])
 @pytest.mark.parametrize("layout", ["two_batches", "three_batches", "row_batch", "no_mod"])
-def test_rmsnorm_modulate_fp32_stream(cuda, layout):
-    """RMSNorm + modulate of the fp32 residual stream (the direct-load kernel): the per-block coefficient table
-    (<= 2 CFG batches), the per-row global path (3 batches, or a row -> batch table as in packed variable-length
-    batches) and plain RMSNorm; max|y| pass, e4m3 and bf16 outputs vs the oracle."""
+def test_rmsnorm_modulate_fp32_stream(cuda, layout, stream):
+    """RMSNorm + modulate of the residual stream, fp32 or fp16 (the direct-load kernel): the per-block coefficient
+    table (<= 2 CFG batches), the per-row global path (3 batches, or a row -> batch table as in packed
+    variable-length batches) and plain RMSNorm; max|y| pass, e4m3 and bf16 outputs vs the oracle on the same
+    (fp16-rounded) stream values."""
     from sa3_b200 import ops
 
     g = _gen(41)
@@ -301,7 +373,7 @@ def test_rmsnorm_modulate_fp32_stream(cuda, layout):
     lens = {"two_batches": [333, 333], "three_batches": [200, 200, 200], "row_batch": [120, 301, 77],
             "no_mod": [250]}[layout]
     B, M = len(lens), sum(lens)
-    x = torch.randn(M, D, generator=g) * 3
+    x = (torch.randn(M, D, generator=g) * 3).to(stream).float()
     gamma = 1 + 0.1 * torch.randn(D, generator=g)
     mod = torch.randn(B, 6 * D, generator=g) * 0.3
     bidx = torch.repeat_interleave(torch.arange(B), torch.tensor(lens))
@@ -315,7 +387,7 @@ def test_rmsnorm_modulate_fp32_stream(cuda, layout):
             kw["row_batch"] = bidx.to(torch.int32).to(cuda)
         else:
             kw["rows_per_batch"] = lens[0]
-    xd, gd = x.to(cuda), gamma.to(cuda)
+    xd, gd = x.to(stream).to(cuda), gamma.to(cuda)
     out = ops.rmsnorm_modulate(xd, gd, 1e-5, **kw)
     assert max_rel(out, ref) < 1e-2
     amax = torch.zeros(1, device=cuda)

@@ -71,6 +71,30 @@ def test_network_velocity_matches_oracle(cuda, name, mode):
     assert err < 2e-2, err
 
 
+@pytest.mark.parametrize("stream", ["fp32", "fp16"])
+@pytest.mark.parametrize("mode", ["bf16", "fp8"])
+def test_residual_stream_precision(cuda, mode, stream):
+    """Both residual-stream precisions of the engine against the oracle holding its stream in the same precision
+    (Cfg.stream_f16: the fp16-rounded branch added to the fp16 stream, rounded again): <= 2e-2 relative L2 on the
+    network output."""
+    case = CASES["dit_small_cfg"]
+    m = _model(case, mode, round_bf16=(mode == "bf16"))
+    m.quantize(mode, stream=stream)
+    inputs = _batched_inputs(case)
+    ocfg = replace(_cfg(case["cfg"]), act_bf16=(mode == "fp8"), stream_f16=(stream == "fp16"))
+    with torch.inference_mode():
+        lin = odit.Linears(m.state_dict(), "fp8" if mode == "fp8" else "fp32")
+        ref = odit.dit_inner_forward(lin, m.state_dict(), ocfg, *inputs)
+        eng = m.engine()
+        assert eng.stream_dtype == (torch.float16 if stream == "fp16" else torch.float32)
+        out = eng.inner(*(a.to(cuda) for a in inputs))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    err = rel_l2(out, ref)
+    print(f"{mode}, {stream} stream: network velocity rel L2 {err:.3e} vs the oracle with the same stream")
+    assert err < 2e-2, err
+
+
 def test_cfg_combine_matches_oracle(cuda):
     case = CASES["dit_small_cfg"]
     m = _model(case, "bf16", round_bf16=False)
