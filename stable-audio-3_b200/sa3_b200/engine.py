@@ -189,12 +189,22 @@ class _Workspace:
                                   dtype=bf) if Tc and kv_all else None
         self.u = torch.empty(M, cfg.ff_inner, device=dev, dtype=bf)
         self.u8 = torch.empty(M, cfg.ff_inner, device=dev, dtype=torch.float8_e4m3fn) if fp8 else None
-        self.t1 = torch.empty(R, D, device=dev, dtype=bf)
+        # The local conditioning (transformer.py:978-994) runs over all M stream rows in stream order: its input
+        # rows are the latent rows' conditioning with zero rows at the memory tokens, and its output is added in
+        # place with a per-row gate factor of exactly 1 on latent rows and 0 on memory tokens (stream_kind), so
+        # the memory tokens get no conditioning, as the reference's left padding gives them (:77-88).
+        self.t1 = torch.empty(M, D, device=dev, dtype=bf)
         # every block's first local-conditioning layer, computed once per forward (within a byte budget)
         self.t1_all = None
-        if local_all and R * cfg.depth * D * 2 <= _LOCAL_ALL_MAX_BYTES:
-            self.t1_all = torch.empty(R, cfg.depth * D, device=dev, dtype=bf)
-        self.loc = torch.zeros(R, 264, device=dev, dtype=bf)
+        if local_all and M * cfg.depth * D * 2 <= _LOCAL_ALL_MAX_BYTES:
+            self.t1_all = torch.empty(M, cfg.depth * D, device=dev, dtype=bf)
+        self.loc = torch.zeros(R, 264, device=dev, dtype=bf)  # latent order, as the caller passes it
+        self.loc_s = torch.zeros(M, 264, device=dev, dtype=bf)  # stream order; memory-token rows stay zero
+        self.lat_rows_l = self.lat_rows.long()
+        kind = torch.zeros(M, dtype=torch.int32)
+        if mem_rows is not None:
+            kind[torch.from_numpy(mem_rows).long()] = 1
+        self.stream_kind = kind.to(dev)
         self.xin = torch.empty(R, cfg.io_channels, device=dev, dtype=bf)
         self.hb = torch.empty(R, D, device=dev, dtype=bf)  # bf16 copy of the latent rows for project_out
         self.out = torch.empty(R, cfg.io_channels, device=dev, dtype=torch.float32)
@@ -245,6 +255,10 @@ class DiTEngine:
         self.sst = torch.stack([sd[f"transformer.layers.{i}.to_scale_shift_gate"] for i in range(cfg.depth)]).to(
             self.dev)
         self.gam = {k: v.to(self.dev).contiguous() for k, v in sd.items() if k.endswith("gamma")}
+        # gate rows of the local-conditioning add: sigmoid(1 - g) is exactly 1 for g = -inf (latent rows) and
+        # exactly 0 for g = +inf (memory tokens)
+        self.loc_gate = torch.tensor([-math.inf, math.inf], device=self.dev).repeat_interleave(
+            cfg.embed_dim).view(2, cfg.embed_dim).contiguous()
         self.rope = None
         self.ws: Optional[_Workspace] = None
         ramp = torch.linspace(0, 1, cfg.timestep_features_dim // 2, dtype=torch.float32)
@@ -618,9 +632,11 @@ class DiTEngine:
             ops.absmax(ctx, ws.amax[slot:slot + 1])
             ctx_a, ctx_s = self._quant(ws, ctx, ws.ctx8, slot)
         t1_all = None
+        if has_local:
+            ws.loc_s.index_copy_(0, ws.lat_rows_l, ws.loc)  # latent rows into stream order
         if has_local and ws.t1_all is not None:
             # every block's SiLU(W1 c + b1) of the local conditioning in one GEMM
-            t1_all = self._gemm(ws.loc, self.loc1_all, ws.t1_all, kind=_lib.EPI_SILU)
+            t1_all = self._gemm(ws.loc_s, self.loc1_all, ws.t1_all, kind=_lib.EPI_SILU)
         kv_all = None
         if ctx is not None and self.kv_all is not None:
             # every block's cross-attention K/V (with k-norm) in one GEMM
@@ -706,9 +722,9 @@ class DiTEngine:
                 if t1_all is not None:
                     t1 = t1_all[:, i * D:(i + 1) * D]
                 else:
-                    t1 = self._gemm(ws.loc, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
-                self._gemm(t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_RESIDUAL, residual=h,
-                           out_row_map=ws.lat_rows)
+                    t1 = self._gemm(ws.loc_s, ln[p + "to_local_embed.0"], ws.t1, kind=_lib.EPI_SILU)
+                self._gemm(t1, ln[p + "to_local_embed.2"], h, kind=_lib.EPI_GATED_RESIDUAL, residual=h,
+                           gate=self.loc_gate, row_batch=ws.stream_kind)
             # -- feed-forward with adaLN (transformer.py:1042-1049); with a padding mask only the valid rows
             # [0, V) (transformer.py:500-519: padded rows get a zero FF branch, so they are left as they are)
             V = ws.V

@@ -241,6 +241,34 @@ def test_gemm_fp16_stream(cuda, M, fp8):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("stream", [torch.float32, torch.float16])
+@pytest.mark.parametrize("M", [300, 2000])
+def test_gated_residual_row_mask(cuda, M, stream):
+    """The local-conditioning add over all stream rows: a gated residual whose gate rows are -inf (factor
+    sigmoid(+inf) = 1) and +inf (factor 0), chosen per row. Rows with factor 1 are bit-identical to the plain
+    residual add; rows with factor 0 (the memory tokens) are left bit-identical."""
+    from sa3_b200 import _lib, ops
+
+    g = _gen(M + 3)
+    N, K = 512, 256
+    a = torch.randn(M, K, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(N, K, generator=g) * 0.05).bfloat16().to(cuda)
+    bias = (torch.randn(N, generator=g) * 0.1).to(cuda)
+    h0 = torch.randn(M, N, generator=g).to(stream).to(cuda)
+    kind = (torch.rand(M, generator=g) < 0.2).to(torch.int32)
+    gate = torch.tensor([-math.inf, math.inf]).repeat_interleave(N).view(2, N).to(cuda)
+    plain = h0.clone()
+    ops.gemm(a, w, plain, kind=_lib.EPI_RESIDUAL, residual=plain, bias=bias)
+    gated = h0.clone()
+    ops.gemm(a, w, gated, kind=_lib.EPI_GATED_RESIDUAL, residual=gated, gate=gate, row_batch=kind.to(cuda),
+             bias=bias)
+    torch.cuda.synchronize()
+    lat, mem = kind == 0, kind == 1
+    assert torch.equal(gated.cpu()[lat], plain.cpu()[lat])
+    assert torch.equal(gated.cpu()[mem], h0.cpu()[mem])
+    assert _lib.device_error() == 0
+
+
 def test_gemm_epilogues(cuda):
     from sa3_b200 import ops, _lib
 
