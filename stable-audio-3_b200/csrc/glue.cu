@@ -299,8 +299,13 @@ __device__ __forceinline__ int norm_batch_load(const NormParams& p, int row) {
 }
 
 // NV groups of four elements per lane: D = 128 * NV; DB: next row prefetched; XH: the stream is fp16 (8-byte loads)
+// Blocks per SM (register-limited at 128 per thread with a prefetched row). Three blocks of the fp16-stream variant at 80
+// registers spill and ran slower (41.5 vs 38.0 us per norm pair at the medium shape).
 template <int NV, bool DB, bool XH>
-__global__ void __launch_bounds__(NORM_D_THREADS, (DB || NV > 12) ? 2 : 3) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+constexpr int norm_direct_blocks() { return (DB || NV > 12) ? 2 : 3; }
+
+template <int NV, bool DB, bool XH>
+__global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>()) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
   using Raw = typename std::conditional<XH, uint2, float4>::type;  // the fp16 stream is kept packed until used
   grid_dep_wait();
   extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
@@ -839,11 +844,12 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
     int rc;
 #define SA3_NORM_DIRECT(V, DB)                                                                                 \
   case V:                                                                                                      \
-    if (gridd > 148 * ((DB || V > 12) ? 2 : 3)) gridd = 148 * ((DB || V > 12) ? 2 : 3);                        \
     if (xh) {                                                                                                  \
+      if (gridd > 148 * norm_direct_blocks<V, DB, true>()) gridd = 148 * norm_direct_blocks<V, DB, true>();    \
       if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB, true>, 2 * 2 * 2048 * 4))) return rc;                 \
       launch_ex(rmsnorm_direct_kernel<V, DB, true>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
     } else {                                                                                                   \
+      if (gridd > 148 * norm_direct_blocks<V, DB, false>()) gridd = 148 * norm_direct_blocks<V, DB, false>();  \
       if ((rc = ensure_smem(rmsnorm_direct_kernel<V, DB, false>, 2 * 2 * 2048 * 4))) return rc;                \
       launch_ex(rmsnorm_direct_kernel<V, DB, false>, dim3(gridd), dim3(NORM_D_THREADS), smem, st, 1, p, tab_batches); \
     }                                                                                                          \
