@@ -574,6 +574,37 @@ __device__ __forceinline__ void qk_rope_prefetch(const sa3_epilogue& e, int m, i
 }
 
 // qk RMSNorm (gamma of the head's group) of one 64-column head held as v = dims 0..31, w = dims 32..63.
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction per two elements, each lane rounded as the scalar op.
+__device__ __forceinline__ uint64_t epi_pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 epi_up2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t epi_fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t epi_mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// v[i] *= x[i] * y[i] over 32 elements in pairs (the scalar order: the product x*y first).
+__device__ __forceinline__ void mul_prod32(float (&v)[32], const float (&x)[32], const float (&y)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const float2 r = epi_up2(epi_mul2(epi_pk2(v[i], v[i + 1]), epi_mul2(epi_pk2(x[i], x[i + 1]), epi_pk2(y[i], y[i + 1]))));
+    v[i] = r.x;
+    v[i + 1] = r.y;
+  }
+}
+
 __device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (&v)[32], float (&w)[32]) {
   const int g = nc / e.qk_group_width;
   const float* gam = nullptr;
@@ -589,20 +620,21 @@ __device__ __forceinline__ void qk_norm64(const sa3_epilogue& e, int nc, float (
     float g_lo[32], g_hi[32];
     ldg_f32x32(gam, g_lo);
     ldg_f32x32(gam + 32, g_hi);
-    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    // four chains of squares, (0, 1) over v and (2, 3) over w, as packed pairs
+    uint64_t a01 = epi_pk2(0.f, 0.f), a23 = epi_pk2(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
-      s4[0] = fmaf(v[i], v[i], s4[0]);
-      s4[1] = fmaf(v[i + 1], v[i + 1], s4[1]);
-      s4[2] = fmaf(w[i], w[i], s4[2]);
-      s4[3] = fmaf(w[i + 1], w[i + 1], s4[3]);
+      const uint64_t pv = epi_pk2(v[i], v[i + 1]), pw = epi_pk2(w[i], w[i + 1]);
+      a01 = epi_fma2(pv, pv, a01);
+      a23 = epi_fma2(pw, pw, a23);
     }
-    const float r = rsqrtf(((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / 64.f) + e.qk_eps);
+    const float2 s01 = epi_up2(a01), s23 = epi_up2(a23);
+    const float r = rsqrtf(((s01.x + s01.y) + (s23.x + s23.y)) * (1.f / 64.f) + e.qk_eps);
+    float rr[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] *= r * g_lo[i];
-      w[i] *= r * g_hi[i];
-    }
+    for (int i = 0; i < 32; ++i) rr[i] = r;
+    mul_prod32(v, rr, g_lo);
+    mul_prod32(w, rr, g_hi);
   }
 }
 
@@ -901,10 +933,20 @@ __device__ __forceinline__ void pg_epilogue_tile(const GemmParams& p, uint32_t t
           const int nc = n0 + col;
           if (nc >= p.N) break;  // uniform per warp
           float v[32], w[32];
-          tmem_ld32(trow + col, v);
-          tmem_ld32(trow + col + 32, w);
-          scale_bias32(v, nc, sa, p.b_scale, e.bias);
-          scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
+          tmem_ld64(trow + col, v, w);  // both halves of the head under one wait
+          if (p.b_scale && !e.bias) {
+            // acc * (sa * b_scale[n]) in packed pairs, the scalar path's order
+            float s[32], sa32[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sa32[i] = sa;
+            ldg_f32x32(p.b_scale + nc, s);
+            mul_prod32(v, sa32, s);
+            ldg_f32x32(p.b_scale + nc + 32, s);
+            mul_prod32(w, sa32, s);
+          } else {
+            scale_bias32(v, nc, sa, p.b_scale, e.bias);
+            scale_bias32(w, nc + 32, sa, p.b_scale, e.bias);
+          }
           qk_norm64(e, nc, v, w);
           if (CS_PRE) {
             qk_rope64(e, nc, *cs_pre, v);
