@@ -39,6 +39,24 @@ def _device_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
     return buf
 
 
+def _torch_stream(handle: int) -> torch.cuda.Stream:
+    """The torch stream object that launches onto the CUDA stream `handle`.
+
+    The caller's current stream (and the legacy default stream, handle 0) are used as they are:
+    torch.cuda.ExternalStream(0) is not the default stream but maps to another stream, so work on it
+    would not be ordered after what the caller queued on the default stream. Any other handle (a
+    TensorRT enqueue's stream) is wrapped once per handle."""
+    cur = torch.cuda.current_stream()
+    if handle == cur.cuda_stream:
+        return cur
+    if handle == 0:
+        return torch.cuda.default_stream()
+    s = _streams.get(handle)
+    if s is None:
+        s = _streams[handle] = torch.cuda.ExternalStream(handle)
+    return s
+
+
 def diff_attn_swa_shape(q_shape: Sequence[int]) -> tuple:
     """Output shape: q_bat's shape with the head axis (dim -2) halved (diff_attn_nocast_plugin.py:14-19)."""
     s = list(q_shape)
@@ -57,9 +75,7 @@ def diff_attn_swa_impl(q_bat: torch.Tensor, k_bat: torch.Tensor, v_bat: torch.Te
     larger than every earlier one arrives: a repeated call (every enqueue of a built engine) allocates nothing.
     Make the first call of the largest shape before any graph capture."""
     out = outputs[0]
-    if stream not in _streams:
-        _streams[stream] = torch.cuda.ExternalStream(stream)
-    with torch.cuda.stream(_streams[stream]):
+    with torch.cuda.stream(_torch_stream(stream)):
         if q_bat.dtype == torch.float32:
             need = fp32_workspace_bytes(q_bat.shape)
             ws = workspace if workspace is not None else _device_scratch(q_bat.device, need)

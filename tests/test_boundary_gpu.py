@@ -96,6 +96,36 @@ def test_diff_attn_swa_plugin(cuda, dtype):
     assert max_rel(_bhnd(out), ref) < 1e-2
 
 
+@pytest.mark.parametrize("where", ["default", "side"])
+def test_diff_attn_swa_plugin_stream_order(cuda, where):
+    """The op runs on the stream it is given, after the work already queued there: a fill of the output
+    queued behind a ~2 ms spin on that stream must be overwritten by the op. Handle 0 (the default
+    stream, what the functional form passes from the default stream) once went to another stream, so
+    the op ran first and the late fill replaced its output."""
+    from sa3_b200 import ops
+    from sa3_b200.plugin import diff_attn_swa, diff_attn_swa_impl
+
+    g = torch.Generator().manual_seed(8)
+    B, N, H = 1, 1836, 24
+    qb, kb, vb = (torch.randn(B, N, 2 * H, 64, generator=g).bfloat16().to(cuda) for _ in range(3))
+    want = torch.empty(B, N, H, 64, device=cuda, dtype=torch.bfloat16)
+    ops.diff_attn_swa(qb, kb, vb, H, 17, want)
+    torch.cuda.synchronize()
+    s = torch.cuda.default_stream() if where == "default" else torch.cuda.Stream()
+    for _ in range(2):
+        with torch.cuda.stream(s):
+            torch.cuda._sleep(4_000_000)  # bounded spin (clock cycles): what follows stays pending a while
+            out = torch.full((B, N, H, 64), 1000.0, device=cuda, dtype=torch.bfloat16)
+            q2 = qb.clone()  # an input produced after the spin as well
+            f = diff_attn_swa(q2, kb, vb, H) if where == "default" else None  # functional form, handle 0
+        # the handle of s, given from the caller's default stream context (as a TensorRT enqueue does)
+        diff_attn_swa_impl(q2, kb, vb, H, [out], s.cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+        if f is not None:
+            assert torch.equal(f, want)
+
+
 def test_diff_attn_swa_plugin_fp32_allocates_nothing_per_call(cuda):
     """The fp32 plugin path after its first call of a shape: repeated calls (every enqueue) make no CUDA
     allocation, and a caller-given workspace is used as given."""
