@@ -17,7 +17,9 @@ Cases (medium: B=2 CFG halves, N = 8183 + 64 tokens, M = 16494 rows, D = 1536):
   qknorm     qk RMSNorm + RoPE on q, k, q_diff, k_diff in place
   ff1_gptq   GLU.proj GPTQ int4 GEMM (group 128, act-order gather included separately), M = 16 x 2648
   ff1_gptq_dense  the same layer on the large-batch path: dequantise once (original channel order) + bf16 GEMM
-Each case's operands exceed the 126 MB L2.
+  samel_w17_N  SAME-L plugin operator (differential, window 17, 2 x 24 heads) at N tokens (200, 1836, 5000, 21964),
+             CUDA-graph timed
+The medium cases' operands exceed the 126 MB L2; the samel cases are the plugin's own small shapes (L2-resident).
 """
 from __future__ import annotations
 
@@ -46,6 +48,28 @@ def _time(fn, iters: int, warm: int = 3) -> float:
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
+
+
+def _time_graph(fn, reps: int, iters: int) -> float:
+    """ms per call of `reps` calls captured in one CUDA graph (no host launch cost in the timed region)."""
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / (iters * reps)
 
 
 def _fp8_weight(n, k, dev, g):
@@ -127,6 +151,16 @@ def case(name: str, iters: int) -> dict:
                                    heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=128)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 4.0 * 64 * N * 128 * H * 2 * B / ms / 1e9}
+    if name.startswith("samel_w17_"):
+        # SAME-L plugin operator (window 17, 48 stacked heads = 2 x 24) at the reference kernel's self-test
+        # lengths; each call is a few microseconds, so 20 calls are replayed from one CUDA graph
+        n = int(name.rsplit("_", 1)[1])
+        qb, kb, vb = (torch.randn(1, n, 48, 64, device=dev).bfloat16() for _ in range(3))
+        out = torch.empty(1, n, 24, 64, device=dev, dtype=torch.bfloat16)
+        fn = lambda: ops.diff_attn_swa(qb, kb, vb, 24, 17, out)  # noqa: E731
+        ms = _time_graph(fn, 20, max(iters // 4, 3))
+        pairs = n * 35 - 17 * 18
+        return {"case": name, "ms": ms, "us": ms * 1e3, "tflops": 4.0 * 64 * pairs * 48 / ms / 1e9}
     if name == "ff1_gptq":
         from .gptq import random_layer
         Mg = 16 * N_GPTQ
@@ -194,7 +228,8 @@ def case(name: str, iters: int) -> dict:
 
 CASES = ["ff1_fp8", "qkv_fp8", "qkv_fp8_qk", "ff2_fp8", "ff2_fp8_f16", "out_fp8", "out_fp8_f16", "out_fp8_store",
          "local2_bf16", "local2_bf16_f16", "local2_bf16_store", "local1_bf16", "attn_diff", "attn_cross", "norm_fp8",
-         "norm_fp8_f16", "quant_attn", "quant_ff", "qknorm", "ff1_gptq", "ff1_gptq_dense"]
+         "norm_fp8_f16", "quant_attn", "quant_ff", "qknorm", "ff1_gptq", "ff1_gptq_dense", "samel_w17_200",
+         "samel_w17_1836", "samel_w17_5000", "samel_w17_21964"]
 
 
 def main():
