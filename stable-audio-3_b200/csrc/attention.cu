@@ -604,20 +604,22 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int d = 0; d < 64; ++d) o[d] = 0.f;
       }
       if (row_ok && !bad && !bad_turn && !*abort_flag) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int qd = 0; qd < 8; ++qd) {
-          uint4 w;
-          w.x = pack_2(o[qd * 8 + 0], o[qd * 8 + 1], p.f16);
-          w.y = pack_2(o[qd * 8 + 2], o[qd * 8 + 3], p.f16);
-          w.z = pack_2(o[qd * 8 + 4], o[qd * 8 + 5], p.f16);
-          w.w = pack_2(o[qd * 8 + 6], o[qd * 8 + 7], p.f16);
-          reinterpret_cast<uint4*>(dst)[qd] = w;
-        }
+        for (int e = 0; e < 32; ++e) pk[e] = pack_2(o[2 * e], o[2 * e + 1], p.f16);
+#pragma unroll
+        for (int qd = 0; qd < 8; ++qd)
+          reinterpret_cast<uint4*>(dst)[qd] = make_uint4(pk[4 * qd], pk[4 * qd + 1], pk[4 * qd + 2], pk[4 * qd + 3]);
         if (p.amax_out) {
+          // max |y| over the stored 16-bit values; for bf16 the halves widen to f32 with integer shifts and
+          // masks, which keeps these conversions off the MUFU that the partner warp's exponentials use
 #pragma unroll
-          for (int d = 0; d < 64; ++d)
-            amax = fmaxf(amax, fabsf(p.f16 ? __half2float(__float2half(o[d]))
-                                           : __bfloat162float(__float2bfloat16(o[d]))));
+          for (int e = 0; e < 32; ++e) {
+            const uint32_t w = pk[e];
+            const float lo = p.f16 ? __half2float(__ushort_as_half((unsigned short)(w & 0xffffu))) : __uint_as_float(w << 16);
+            const float hi = p.f16 ? __half2float(__ushort_as_half((unsigned short)(w >> 16))) : __uint_as_float(w & 0xffff0000u);
+            amax = fmax3(amax, fabsf(lo), fabsf(hi));
+          }
         }
       }
     }

@@ -139,16 +139,18 @@ def case(name: str, iters: int) -> dict:
     if name == "attn_diff":
         qkv = torch.randn(M, 5 * D, device=dev).bfloat16()
         q, k, v, q2, k2 = (qkv[:, i * D:(i + 1) * D] for i in range(5))
+        am = torch.zeros(1, device=dev)  # max|out| for the FP8 quantisation that follows, as in the block
         fn = lambda: ops.attention(q, k, v, q2=q2, k2=k2, heads=H, batch=B, max_seqlen_q=N,  # noqa: E731
-                                   max_seqlen_k=N, window=(256, 256))
+                                   max_seqlen_k=N, window=(256, 256), amax_out=am)
         pairs = N * 513 - 256 * 257
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 4.0 * 64 * pairs * H * 2 * B / ms / 1e9}
     if name == "attn_cross":
         q = torch.randn(M, 2 * D, device=dev).bfloat16()
         kv = torch.randn(B * 128, 3 * D, device=dev).bfloat16()
+        am = torch.zeros(1, device=dev)
         fn = lambda: ops.attention(q[:, :D], kv[:, :D], kv[:, 2 * D:], q2=q[:, D:], k2=kv[:, D:2 * D],  # noqa
-                                   heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=128)
+                                   heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=128, amax_out=am)
         ms = _time(fn, iters)
         return {"case": name, "ms": ms, "tflops": 4.0 * 64 * N * 128 * H * 2 * B / ms / 1e9}
     if name.startswith("samel_w17_"):

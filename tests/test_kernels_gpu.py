@@ -484,6 +484,28 @@ def test_attention_differential(cuda):
     assert max_rel(hh(out), ref) < 1e-2
 
 
+@pytest.mark.parametrize("diff", [False, True])
+def test_attention_amax_out(cuda, diff):
+    """amax_out (the max |out| that feeds the next FP8 quantisation) equals max |out| over the stored 16-bit
+    output exactly, accumulated over earlier contents of the slot (never lowered)."""
+    from sa3_b200 import ops
+
+    g = _gen(31)
+    B, N, H, w = 2, 700, 3, 256
+    D = H * 64
+    qkv = torch.randn(B * N, 5 * D, generator=g).bfloat16().to(cuda)
+    q, k, v, q2, k2 = (qkv[:, i * D:(i + 1) * D] for i in range(5))
+    kw = dict(q2=q2, k2=k2) if diff else {}
+    am = torch.zeros(1, device=cuda)
+    out = ops.attention(q, k, v, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w), amax_out=am, **kw)
+    torch.cuda.synchronize()
+    assert am.item() == out.float().abs().max().item()
+    big = torch.full((1,), 1e3, device=cuda)
+    ops.attention(q, k, v, heads=H, batch=B, max_seqlen_q=N, max_seqlen_k=N, window=(w, w), amax_out=big, **kw)
+    torch.cuda.synchronize()
+    assert big.item() == 1e3
+
+
 @pytest.mark.parametrize("w,diff", [(-1, False), (256, False), (256, True)])
 def test_attention_growing_scores(cuda, w, diff):
     """Key norms grow along the sequence, so a row's maximum score keeps rising across key tiles by far
