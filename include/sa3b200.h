@@ -171,7 +171,13 @@ int sa3_permute_cols(const void* x, const int* perm, void* out, int rows, int K,
  *   is non-NULL, stores s = max(*quant_amax, 1e-12) / 448 there for the
  *   consuming GEMM's a_scale).
  * mode SA3_NORM_AMAX writes nothing and atomically maxes |y| into *amax_out.
- * x is bf16 or fp32 (x_dtype) [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
+ * x is bf16, fp16 or fp32 (x_dtype) [rows, D]; D must be a multiple of 8, rows 16-byte aligned.
+ * row_r (optional, fp32 [rows]): the AMAX pass stores each row's 1/rms there and the WRITE pass of the
+ *   same x reads it instead of recomputing it, which turns that pass into an elementwise stream (same
+ *   output). The AMAX pass with row_r must have run on the same stream before such a WRITE pass. The
+ *   AMAX pass stores it for fp16 / fp32 x with D = 1024, 1536 or 2048 (16-byte aligned gamma /
+ *   modulation rows); the WRITE pass uses it for fp16 x with at most two uniform modulation batches
+ *   (row_batch NULL) or no modulation. Other calls ignore row_r.
  */
 #define SA3_NORM_WRITE 0
 #define SA3_NORM_AMAX 1
@@ -179,7 +185,8 @@ int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D,
                          const float* gamma,
                          float eps, const float* mod, long long ld_mod, int scale_off, int shift_off,
                          int rows_per_batch, const int* row_batch, int mode, int out_dtype,
-                         const float* quant_amax, float* scale_out, float* amax_out, void* stream);
+                         const float* quant_amax, float* scale_out, float* amax_out, float* row_r,
+                         void* stream);
 
 /* Per-tensor dynamic FP8 quantisation: out = e4m3(x * r), r = 448/max(*amax,1e-12);
  * the dequantisation scale s = max(*amax,1e-12)/448 is stored to *scale_out when non-NULL. If amax_out is non-NULL, the

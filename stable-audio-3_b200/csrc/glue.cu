@@ -108,6 +108,7 @@ struct NormParams {
   const float* quant_amax;
   float* scale_out;
   float* amax_out;
+  float* row_r;  // optional [rows]: 1/rms of each row, stored by the AMAX pass, read by the WRITE pass
 };
 
 __device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
@@ -374,6 +375,7 @@ __global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>
       ss4[3] = fmaf(x.w, x.w, ss4[3]);
     }
     const float r = rsqrtf(warp_sum((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / (float)p.D + p.eps);
+    if (p.mode == SA3_NORM_AMAX && p.row_r && lane == 0) p.row_r[row] = r;
     const int b = vb;
     const bool in_tab = b < tab_batches;  // warp-uniform
 #pragma unroll
@@ -418,6 +420,121 @@ __global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>
     li = nli;
   }
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
+}
+
+// WRITE pass from the per-row 1/rms that the AMAX pass stored (p.row_r): no row reductions are left, so
+// the pass is an elementwise stream over 8-element chunks with NORM_APPLY_INFLIGHT independent loads per
+// thread (the structure of quantize_e4m3_kernel), y = fmaf(x * r, a, shift) with the modulation
+// coefficients of the row's CFG batch from a shared-memory table: the same operations, in the same
+// order, as the direct kernel's WRITE pass, so the output is identical. The first chunks' loads are
+// issued before the table is built, so the table's loads overlap them. tab_batches (1 or 2) uniform
+// batches of rows_per_batch rows. The fp16 stream only: on the fp32 stream this pass was no faster than
+// the direct kernel's (24.0 vs 23.6 us at the medium shape). Coefficients from L1-cached global loads
+// instead of the table: 25.7 us against 20.0 us.
+constexpr int NORM_APPLY_INFLIGHT = 8;
+
+struct NormApplyChunks {
+  uint4 u[NORM_APPLY_INFLIGHT];  // 8 fp16 values each
+  float rr[NORM_APPLY_INFLIGHT];
+};
+
+// (row, chunk) stepping by a fixed (dr, dc) per chunk, as in quantize_e4m3_kernel
+__device__ __forceinline__ void norm_apply_step(int& r, int& c, int dr, int dc, int cpr) {
+  r += dr;
+  c += dc;
+  if (c >= cpr) {
+    c -= cpr;
+    ++r;
+  }
+}
+
+__device__ __forceinline__ void norm_apply_load(const NormParams& p, NormApplyChunks& ch, int r, int c, int dr, int dc,
+                                                int cpr) {
+#pragma unroll
+  for (int k = 0; k < NORM_APPLY_INFLIGHT; ++k) {
+    if (r < p.rows) {
+      ch.u[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + (long long)r * p.ldx + c * 8);
+      ch.rr[k] = __ldg(p.row_r + r);
+    }
+    norm_apply_step(r, c, dr, dc, cpr);
+  }
+}
+
+__global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int tab_batches) {
+  constexpr int NF = NORM_APPLY_INFLIGHT;
+  grid_dep_wait();
+  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
+  const int cpr = p.D / 8;  // 8-element chunks per row
+  const long long total = (long long)p.rows * cpr;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int dr = (int)(stride / cpr), dc = (int)(stride % cpr);
+  long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  int r0 = (int)(i0 / cpr), c0 = (int)(i0 % cpr);
+  NormApplyChunks ch;
+  norm_apply_load(p, ch, r0, c0, dr, dc, cpr);
+  {
+    const int D4 = p.D >> 2, n4 = tab_batches * D4;
+    for (int idx = threadIdx.x; idx < n4; idx += blockDim.x) {
+      const int b = idx / D4, e = 4 * (idx - b * D4);
+      const float4 g = p.gamma ? __ldg(reinterpret_cast<const float4*>(p.gamma + e)) : make_float4(1.f, 1.f, 1.f, 1.f);
+      float4 ta, ts;
+      if (p.mod) {
+        const float4 sc = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.scale_off + e));
+        ts = __ldg(reinterpret_cast<const float4*>(p.mod + (long long)b * p.ld_mod + p.shift_off + e));
+        ta = make_float4(g.x * (1.f + sc.x), g.y * (1.f + sc.y), g.z * (1.f + sc.z), g.w * (1.f + sc.w));
+      } else {
+        ta = g;
+        ts = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      *reinterpret_cast<float4*>(ntab + (2 * b) * p.D + e) = ta;
+      *reinterpret_cast<float4*>(ntab + (2 * b + 1) * p.D + e) = ts;
+    }
+  }
+  __syncthreads();
+  float s = 1.f;
+  if (p.out_dtype == SA3_DT_E4M3) {
+    s = quant_inv_scale(p.quant_amax);
+    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
+  }
+  while (i0 < total) {
+    int r = r0, c = c0;
+#pragma unroll
+    for (int k = 0; k < NF; ++k) {
+      if (r < p.rows) {
+        float x[8];
+        const __half2* h = reinterpret_cast<const __half2*>(&ch.u[k]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h[j]);
+          x[2 * j] = f.x;
+          x[2 * j + 1] = f.y;
+        }
+        const int b = tab_batches == 2 && r >= p.rows_per_batch ? 1 : 0;
+        const float4* ap = reinterpret_cast<const float4*>(ntab + (2 * b) * p.D + c * 8);
+        const float4* sp = reinterpret_cast<const float4*>(ntab + (2 * b + 1) * p.D + c * 8);
+        const float4 a0 = ap[0], a1 = ap[1], s0 = sp[0], s1 = sp[1];
+        const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float sh[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = fmaf(x[j] * ch.rr[k], a[j], sh[j]);
+        if (p.out_dtype == SA3_DT_E4M3) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(p.out) + (long long)r * p.ldo + c * 8) =
+              make_uint2(e4m3x2(y[0] * s, y[1] * s) | (e4m3x2(y[2] * s, y[3] * s) << 16),
+                         e4m3x2(y[4] * s, y[5] * s) | (e4m3x2(y[6] * s, y[7] * s) << 16));
+        } else {
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)r * p.ldo + c * 8) =
+              make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                         pack_bf16x2(y[6], y[7]));
+        }
+      }
+      norm_apply_step(r, c, dr, dc, cpr);
+    }
+    r0 = r;
+    c0 = c;
+    i0 += NF * stride;
+    if (i0 < total) norm_apply_load(p, ch, r0, c0, dr, dc, cpr);
+  }
 }
 
 // Bulk-copy variant: warp 4 (lane 0) streams whole rows into an NORM_RING-deep shared-memory ring
@@ -783,7 +900,8 @@ using namespace sa3;
 extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D, long long ldx,
                                     long long ldo, const float* gamma, float eps, const float* mod, long long ld_mod, int scale_off,
                                     int shift_off, int rows_per_batch, const int* row_batch, int mode, int out_dtype,
-                                    const float* quant_amax, float* scale_out, float* amax_out, void* stream) {
+                                    const float* quant_amax, float* scale_out, float* amax_out, float* row_r,
+                                    void* stream) {
   if (!x || rows <= 0 || D <= 0 || (D % 8) || ldx < D) return SA3_ERR_ARG;
   if (x_dtype != SA3_DT_BF16 && x_dtype != SA3_DT_F32 && x_dtype != SA3_DT_F16) return SA3_ERR_DTYPE;
   if (!aligned16(x) || (ldx % 8)) return SA3_ERR_ALIGN;
@@ -825,6 +943,7 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
   p.quant_amax = quant_amax;
   p.scale_out = scale_out;
   p.amax_out = amax_out;
+  p.row_r = nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int nchunk = D / 8;
   int grid = (rows + 3) / 4;  // 4 warps (rows) per 128-thread block
@@ -842,6 +961,23 @@ extern "C" int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int r
     const int smem = tab_batches * 2 * D * 4;
     int gridd = (rows + 7) / 8;
     int rc;
+    // row_r is stored and used only where the direct kernel runs both passes (D / 128 = 8, 12 or 16)
+    const bool direct = D / 128 == 8 || D / 128 == 12 || D / 128 == 16;
+    if (row_r && direct && mode == SA3_NORM_AMAX) p.row_r = row_r;  // the direct kernel stores 1/rms per row
+    if (row_r && direct && xh && mode == SA3_NORM_WRITE && (tab_batches >= 1 || !mod) && aligned16(x) &&
+        ldx % 8 == 0 && (out_dtype == SA3_DT_E4M3 || aligned16(out))) {
+      // 1/rms of every row is known: the WRITE pass is an elementwise stream
+      p.row_r = row_r;
+      const int tb = mod ? tab_batches : 1;
+      const long long chunks = (long long)rows * (D / 8);
+      const long long per_block = 256LL * NORM_APPLY_INFLIGHT;
+      long long ga = (chunks + per_block - 1) / per_block;
+      if (ga > 148 * 3) ga = 148 * 3;
+      const int smem_a = tb * 2 * D * 4;
+      if ((rc = ensure_smem(norm_apply_kernel, 2 * 2 * 4096 * 4))) return rc;
+      launch_ex(norm_apply_kernel, dim3((int)ga), dim3(256), smem_a, st, 1, p, tb);
+      return launch_status();
+    }
 #define SA3_NORM_DIRECT(V, DB)                                                                                 \
   case V:                                                                                                      \
     if (xh) {                                                                                                  \

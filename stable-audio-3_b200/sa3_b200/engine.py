@@ -170,6 +170,8 @@ class _Workspace:
         bf = torch.bfloat16
         self.h = torch.empty(M, D, device=dev, dtype=stream_dtype)  # residual stream (fp16 or fp32)
         self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
+        # 1/rms of each stream row, stored by a norm's max|y| pass and read by its write pass
+        self.row_r = torch.empty(M, device=dev, dtype=torch.float32) if fp8 else None
         self.qkv = torch.empty(M, nq * D, device=dev, dtype=bf)
         if split is not None:
             # per sequence [left halo | own rows | right halo] of the q|k|v|q'|k' projection
@@ -377,9 +379,10 @@ class DiTEngine:
         if self.fp8:
             am = ws.amax[slot:slot + 1]
             sc = ws.scale[slot:slot + 1]
-            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, **kw)
+            rr = ws.row_r[:rows]
+            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, row_r=rr, **kw)
             self._sync_amax(ws, slot)
-            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, quant_amax=am, scale_out=sc, **kw)
+            ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, quant_amax=am, scale_out=sc, row_r=rr, **kw)
             return a, sc
         ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, **kw)
         return a, None

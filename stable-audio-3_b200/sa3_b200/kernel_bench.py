@@ -199,13 +199,21 @@ def case(name: str, iters: int) -> dict:
         am = torch.zeros(1, device=dev)
         sc = torch.zeros(1, device=dev)
         out = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn)
+        rr = torch.empty(M, device=dev)  # per-row 1/rms from the max|y| pass, as in the block
 
         def fn():
-            ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, amax_only=am)
+            ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, amax_only=am,
+                                 row_r=rr)
             ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D, rows_per_batch=N, out=out,
-                                 quant_amax=am, scale_out=sc)
+                                 quant_amax=am, scale_out=sc, row_r=rr)
         ms = _time(fn, iters)
-        return {"case": name, "ms": ms, "GBps": (2 * M * D * x.element_size() + M * D) / ms / 1e6}
+        ms_amax = _time(lambda: ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D,  # noqa: E731
+                                                     rows_per_batch=N, amax_only=am, row_r=rr), iters)
+        ms_write = _time(lambda: ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D,  # noqa: E731
+                                                      rows_per_batch=N, out=out, quant_amax=am, scale_out=sc,
+                                                      row_r=rr), iters)
+        return {"case": name, "ms": ms, "GBps": (2 * M * D * x.element_size() + M * D) / ms / 1e6,
+                "ms_amax_pass": ms_amax, "ms_write_pass": ms_write}
     if name in ("quant_attn", "quant_ff"):
         # activation quantisation with the scale from a producer's max|x|: M x 1536 (attention output) and
         # M x 6144 (FF hidden)

@@ -141,9 +141,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
 # ---------------------------------------------------------------------- glue
 def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float, *, mod=None, scale_off: int = 0,
                      shift_off: int = 0, rows_per_batch: int = 0, row_batch=None, out=None,
-                     out_dtype=torch.bfloat16, quant_amax=None, scale_out=None, amax_only=None) -> Optional[torch.Tensor]:
-    """RMSNorm(x)*gamma*(1+scale)+shift per row; bf16 or e4m3 out, or only max|y| into `amax_only`."""
-    _need_cuda(x, gamma, mod, row_batch, out, quant_amax, scale_out, amax_only)
+                     out_dtype=torch.bfloat16, quant_amax=None, scale_out=None, amax_only=None,
+                     row_r=None) -> Optional[torch.Tensor]:
+    """RMSNorm(x)*gamma*(1+scale)+shift per row; bf16 or e4m3 out, or only max|y| into `amax_only`.
+
+    row_r (fp32 [rows], optional): the max|y| pass stores each row's 1/rms there, and a later write pass of
+    the same x given the same buffer reads it instead of recomputing it (same output, one elementwise pass)."""
+    _need_cuda(x, gamma, mod, row_batch, out, quant_amax, scale_out, amax_only, row_r)
+    if row_r is not None and (row_r.dtype != torch.float32 or row_r.numel() < x.shape[0] or not row_r.is_contiguous()):
+        raise RuntimeError("row_r must be a contiguous fp32 tensor of at least `rows` elements")
     rows, D = x.shape
     lib = _lib.load()
     if amax_only is not None:
@@ -151,7 +157,7 @@ def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float,
         rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), _dt(x), None, rows, D, _row_stride(x), 0, _ptr(gamma), eps, _ptr(mod),
                                       _row_stride(mod) if mod is not None else 0, scale_off, shift_off,
                                       rows_per_batch, _ptr(row_batch), _lib.NORM_AMAX, _lib.DT_BF16, None, None,
-                                      amax_only.data_ptr(), _stream())
+                                      amax_only.data_ptr(), _ptr(row_r), _stream())
         _lib.check(rc, "sa3_rmsnorm_modulate(amax)")
         return None
     if out is None:
@@ -160,7 +166,7 @@ def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float,
     rc = lib.sa3_rmsnorm_modulate(x.data_ptr(), _dt(x), out.data_ptr(), rows, D, _row_stride(x), _row_stride(out),
                                   _ptr(gamma), eps, _ptr(mod), _row_stride(mod) if mod is not None else 0, scale_off,
                                   shift_off, rows_per_batch, _ptr(row_batch), _lib.NORM_WRITE, _dt(out),
-                                  _ptr(quant_amax), _ptr(scale_out), None, _stream())
+                                  _ptr(quant_amax), _ptr(scale_out), None, _ptr(row_r), _stream())
     _lib.check(rc, "sa3_rmsnorm_modulate")
     return out
 

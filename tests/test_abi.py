@@ -40,7 +40,7 @@ def test_host_side_argument_errors_need_no_gpu():
                              64, -1, -1, 0.125, 0, None, None) == -1
     assert lib.sa3_diff_attn_swa(None, None, None, None, 0, 1, 1, 1, 64, 17, None) == -1
     assert lib.sa3_rmsnorm_modulate(None, 0, None, 0, 0, 0, 0, None, 1e-5, None, 0, 0, 0, 0, None, 0, 0, None,
-                                    None, None, None) == -1
+                                    None, None, None, None) == -1
     assert lib.sa3_convert(None, 0, None, 0, 0, 0, 0, 0, None, None) == -1
 
 

@@ -425,6 +425,19 @@ def test_rmsnorm_modulate_fp32_stream(cuda, layout, stream):
     s = torch.zeros(1, device=cuda)
     q = ops.rmsnorm_modulate(xd, gd, 1e-5, out_dtype=torch.float8_e4m3fn, quant_amax=amax, scale_out=s, **kw)
     assert rel_fro(q.float().cpu() * s.cpu(), oq.fake_quant_act(ref)) < 2e-2
+    # the two passes with a per-row 1/rms buffer (the block's FP8 norm): the max|y| pass stores it, the write
+    # pass reads it (an elementwise kernel where the batches allow); outputs are the same bits as without it
+    rr = torch.full((M,), float("nan"), device=cuda)
+    amax2, s2 = torch.zeros(1, device=cuda), torch.zeros(1, device=cuda)
+    ops.rmsnorm_modulate(xd, gd, 1e-5, amax_only=amax2, row_r=rr, **kw)
+    q2 = ops.rmsnorm_modulate(xd, gd, 1e-5, out_dtype=torch.float8_e4m3fn, quant_amax=amax2, scale_out=s2, row_r=rr,
+                              **kw)
+    out2 = ops.rmsnorm_modulate(xd, gd, 1e-5, row_r=rr, **kw)
+    torch.cuda.synchronize()
+    assert amax2.item() == amax.item() and s2.item() == s.item()
+    assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8))
+    assert torch.equal(out2, out)
+    assert bool(torch.isfinite(rr).all())
 
 
 def test_qk_norm_rope(cuda):
