@@ -209,6 +209,7 @@ __device__ __forceinline__ void decode_item(const AttnParams& p, int item, int p
   tile0 = 2 * pair;
 }
 
+template <bool NARROW>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQ2,
@@ -481,6 +482,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int j0 = un.j_lo + j * ATT_BN;
         const int clo = lo_j - j0, chi = hi_j - j0;  // visible columns [clo, chi) of this tile
         const bool full = __all_sync(0xffffffffu, clo <= 0 && chi >= ATT_BN);
+        // NARROW: bit c is set when 32-column chunk c holds a visible column for some row of this warp;
+        // the exponentials of the other chunks are skipped and their P is written as 0, which is what
+        // exp2(-inf) gives for their masked scores
+        uint32_t need = 0xfu;
+        if (NARROW) {
+          const int wlo = __reduce_min_sync(0xffffffffu, clo), whi = __reduce_max_sync(0xffffffffu, chi);
+          need = 0u;
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (wlo < 32 * (c + 1) && whi > 32 * c) need |= 1u << c;
+        }
         uint32_t sa[32], sb[32], sc[32], sd[32];
         tmem_ld32_async(t_s, sa);
         tmem_ld32_async(t_s + 32, sb);
@@ -520,7 +532,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const uint64_t scale2 = f2(p.scale_log2, p.scale_log2), negm2 = f2(-m_use, -m_use);
         uint64_t acc[4] = {0, 0, 0, 0};
         take_turn();
-        {
+        if (!NARROW) {
           uint32_t w[16];
           exp_chunk(sa, scale2, negm2, acc, w, p.f16);
           tmem_st16(t_p, w);
@@ -530,6 +542,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           tmem_st16(t_p + 32, w);
           exp_chunk(sd, scale2, negm2, acc, w, p.f16);
           tmem_st16(t_p + 48, w);
+        } else {
+          uint32_t w[16];
+          auto chunk = [&](const uint32_t(&sx)[32], uint32_t bit, uint32_t col) {
+            if (need & bit) {
+              exp_chunk(sx, scale2, negm2, acc, w, p.f16);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) w[e] = 0u;
+            }
+            tmem_st16(t_p + col, w);
+          };
+          chunk(sa, 1u, 0);
+          chunk(sb, 2u, 16);
+          chunk(sc, 4u, 32);
+          chunk(sd, 8u, 48);
         }
         pass_turn();
         const float2 r01 = f2_split(fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3])));
@@ -706,9 +733,19 @@ extern "C" int sa3_attention(const void* q, const void* k, const void* v, const 
     return SA3_ERR_LAUNCH;
   const int grid = num_items < sms ? (int)num_items : sms;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if ((rc = ensure_smem(attention_tc_kernel, ATT_SMEM))) return rc;
-  launch_ex(attention_tc_kernel, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, st, 1, mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
-                                                            pairs_per_head);
+  // Narrow windows (the SAME-L window 17) skip the exponentials of the chunks of a tile that no row of a
+  // softmax warp sees. SA3_ATT_NARROW=0 / 1 in the environment forces the general / narrow kernel (the
+  // two give identical outputs).
+  static const int narrow_env = [] {
+    const char* e = getenv("SA3_ATT_NARROW");
+    return e ? atoi(e) : -1;
+  }();
+  const bool narrow = narrow_env >= 0 ? narrow_env != 0
+                                      : (window_left >= 0 && window_right >= 0 && window_left + window_right + 1 <= 96);
+  auto kern = narrow ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+  if ((rc = ensure_smem(kern, ATT_SMEM))) return rc;
+  launch_ex(kern, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, st, 1, mq, mk, mv, mq2, mk2, mv2, p, (int)num_items,
+            pairs_per_head);
   return launch_status();
 }
 
