@@ -96,6 +96,26 @@ def test_diff_attn_swa_plugin(cuda, dtype):
     assert max_rel(_bhnd(out), ref) < 1e-2
 
 
+def test_diff_attn_swa_plugin_long(cuda):
+    """The plugin op at N = 5000 (20 pairs of query tiles x 24 heads = 480 work items, several per CTA; the
+    narrow-window kernel): row blocks spread over the sequence against the oracle, each computed on a slice of
+    rows that holds the block's whole window (17 keys either side), so the oracle stays small."""
+    from sa3_b200.plugin import diff_attn_swa
+
+    g = torch.Generator().manual_seed(12)
+    B, N, H, W = 1, 5000, 24, 17
+    qb, kb, vb = (torch.randn(B, N, 2 * H, 64, generator=g).bfloat16() for _ in range(3))
+    out = _bhnd(diff_attn_swa(qb.to(cuda), kb.to(cuda), vb.to(cuda), H))
+    x = lambda t: _bhnd(t)  # noqa: E731
+    for a in (0, 100, 1234, 2500, 3999, 4936):
+        lo, hi = max(a - W, 0), min(a + 64 + W, N)
+        sl = lambda t: x(t)[:, :, lo:hi]  # noqa: E731
+        ref = (orf.attention(sl(qb)[:, :H], sl(kb)[:, :H], sl(vb)[:, :H], W, W)
+               - orf.attention(sl(qb)[:, H:], sl(kb)[:, H:], sl(vb)[:, H:], W, W))
+        blk = slice(a - lo, a - lo + min(64, N - a))
+        assert max_rel(out[:, :, a:a + 64], ref[:, :, blk]) < 1e-2
+
+
 @pytest.mark.parametrize("where", ["default", "side"])
 def test_diff_attn_swa_plugin_stream_order(cuda, where):
     """The op runs on the stream it is given, after the work already queued there: a fill of the output
