@@ -287,6 +287,35 @@ int sa3_fp8_linear_noalloc(const void* x, const void* w, const float* w_scale, c
 int sa3_diff_attn_swa(const void* q_bat, const void* k_bat, const void* v_bat, void* out, int dtype, int batch,
                       int seqlen, int num_heads, int head_dim, int window, void* stream);
 
+/* ---------------------------------------------- sequence split: max over ranks through peer memory (e)
+ *
+ * Replaces the 4-byte NCCL all-reduce (MAX) of the per-tensor FP8 activation amax
+ * that the sequence-split step makes at every quantisation point (the reference
+ * has no sequence split; the split is this library's, see sa3_b200/seqsplit.py).
+ * Each rank allocates a mailbox (sa3_peer_box_alloc, sa3_peer_box_bytes() bytes,
+ * zeroed) and shares it with the other ranks of the node through a CUDA IPC
+ * handle (sa3_ipc_get_handle / sa3_ipc_open_handle, sa3_ipc_handle_bytes()
+ * bytes). sa3_peer_max(value, boxes, rank, world, stream) then replaces *value
+ * (fp32, device) with its maximum over the world ranks: boxes[r] is rank r's
+ * mailbox as this process addresses it (its own allocation for r == rank, the
+ * opened IPC pointer otherwise). One warp stores (epoch, value) into every
+ * rank's mailbox over NVLink and waits, bounded by about a second, for every
+ * rank's word of the same epoch; on timeout it records device error site 90 and
+ * keeps the local value. Every rank must make the same calls in the same order,
+ * each rank on its own GPU of one node with peer access (never two ranks on one
+ * GPU: their kernels wait on each other). world <= SA3_PEER_MAX_RANKS.
+ */
+#define SA3_PEER_MAX_RANKS 8
+#define SA3_PEER_SLOTS 4
+int sa3_peer_box_bytes(void);
+int sa3_peer_box_alloc(void** box);
+int sa3_peer_box_free(void* box);
+int sa3_ipc_handle_bytes(void);
+int sa3_ipc_get_handle(void* ptr, void* handle);
+int sa3_ipc_open_handle(const void* handle, void** ptr);
+int sa3_ipc_close_handle(void* ptr);
+int sa3_peer_max(float* value, void* const* boxes, int rank, int world, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

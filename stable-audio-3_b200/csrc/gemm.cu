@@ -20,6 +20,7 @@ namespace sa3 {
 SA3_DEFINE_ERROR_READER(read_error_gemm)
 int read_error_glue(int* out);
 int read_error_attention(int* out);
+int read_error_peer(int* out);
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
@@ -1747,9 +1748,11 @@ extern "C" int sa3_version(void) { return 100; }
 extern "C" int sa3_get_device_error(int* err) {
   if (!err) return SA3_ERR_ARG;
   if (cudaDeviceSynchronize() != cudaSuccess) return SA3_ERR_LAUNCH;
-  int a = 0, b = 0, c = 0, rc;
-  if ((rc = read_error_gemm(&a)) || (rc = read_error_glue(&b)) || (rc = read_error_attention(&c))) return rc;
-  *err = a ? a : (b ? b : c);
+  int a = 0, b = 0, c = 0, d = 0, rc;
+  if ((rc = read_error_gemm(&a)) || (rc = read_error_glue(&b)) || (rc = read_error_attention(&c)) ||
+      (rc = read_error_peer(&d)))
+    return rc;
+  *err = a ? a : (b ? b : (c ? c : d));
   return SA3_OK;
 }
 

@@ -82,6 +82,14 @@ SIGNATURES = {
                       c_int, c_int, c_ll, c_ll, c_ll, c_ll, c_int, c_int, c_float, c_int, c_vp, c_vp],
     "sa3_diff_attn_swa": [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp],
     "sa3_fp8_linear_noalloc": [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_ll, c_vp],
+    "sa3_peer_box_bytes": [],
+    "sa3_peer_box_alloc": [ctypes.POINTER(c_vp)],
+    "sa3_peer_box_free": [c_vp],
+    "sa3_ipc_handle_bytes": [],
+    "sa3_ipc_get_handle": [c_vp, c_vp],
+    "sa3_ipc_open_handle": [c_vp, ctypes.POINTER(c_vp)],
+    "sa3_ipc_close_handle": [c_vp],
+    "sa3_peer_max": [c_vp, ctypes.POINTER(c_vp), c_int, c_int, c_vp],
 }
 
 _lib = None

@@ -347,6 +347,9 @@ class DiTEngine:
                                       local_all=self.loc1_all is not None, split=split,
                                       kv_all=self.kv_all is not None, valid=valid, stream_dtype=self.stream_dtype)
             ws.valid_key = vkey
+            if split is not None and split.world > 1 and self.fp8:
+                # collective set-up of the peer-memory amax exchange (every rank builds its workspace here)
+                _seqsplit.prepare_peer_max(split.group)
         if self.rope is None or self.rope.shape[0] < ws.max_pos:
             self.rope = ops.rope_table(ws.max_pos, 32, device=self.dev)
         return ws

@@ -14,6 +14,7 @@ unsplit step's scales. Cross-attention keys (the context) and the conditioning a
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import List, Tuple
 
@@ -153,11 +154,86 @@ def exchange_halos(ext: torch.Tensor, batch: int, own: int, split: SeqSplit, wai
     return reqs
 
 
+class PeerMax:
+    """Max of one fp32 device value over the ranks of `group` through NVLink peer memory (sa3_peer_max): each
+    rank owns a mailbox in its GPU memory, opened by the other ranks through CUDA IPC handles. One kernel per
+    call, no NCCL. Construct it on every rank of the group at the same point (it gathers the handles)."""
+
+    def __init__(self, group=None):
+        from . import _lib
+
+        lib = _lib.load()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self._lib, self._opened = lib, []
+        box = ctypes.c_void_p()
+        _lib.check(lib.sa3_peer_box_alloc(ctypes.byref(box)), "sa3_peer_box_alloc")
+        self._box = box
+        h = (ctypes.c_char * lib.sa3_ipc_handle_bytes())()
+        _lib.check(lib.sa3_ipc_get_handle(box, h), "sa3_ipc_get_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        ptrs, ok = [], True
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(box.value)
+                continue
+            p = ctypes.c_void_p()
+            if lib.sa3_ipc_open_handle(hb, ctypes.byref(p)) != 0:
+                ok = False
+                break
+            self._opened.append(p)
+            ptrs.append(p.value)
+        oks = [None] * self.world
+        dist.all_gather_object(oks, ok, group=group)
+        self.ok = all(oks)
+        self._boxes = (ctypes.c_void_p * self.world)(*ptrs) if self.ok else None
+
+    def __call__(self, t: torch.Tensor) -> None:
+        from . import _lib
+
+        rc = self._lib.sa3_peer_max(t.data_ptr(), self._boxes, self.rank, self.world,
+                                    torch.cuda.current_stream().cuda_stream)
+        _lib.check(rc, "sa3_peer_max")
+
+
+_peer_max = {}  # process group key -> PeerMax, or None where the group keeps the NCCL all-reduce
+
+
+def _group_key(group):
+    return "default" if group is None else id(group)
+
+
+def prepare_peer_max(group=None) -> None:
+    """Collective (every rank of `group`, same point): set up the peer-memory max exchange when every rank runs on
+    its own GPU of one host (distinct device UUIDs) and has opened every other rank's mailbox; otherwise the
+    group keeps the NCCL all-reduce. SA3_PEER_MAX=0 in the environment keeps NCCL everywhere."""
+    key = _group_key(group)
+    if key in _peer_max or not dist.is_initialized():
+        return
+    import os
+    import socket
+
+    world = dist.get_world_size(group)
+    use = os.environ.get("SA3_PEER_MAX", "1") != "0" and torch.cuda.is_available() and 2 <= world <= 8
+    me = (socket.gethostname(), str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+          if torch.cuda.is_available() else "", use)
+    who = [None] * world
+    dist.all_gather_object(who, me, group=group)
+    eligible = all(w[2] for w in who) and len({w[0] for w in who}) == 1 and len({w[1] for w in who}) == world
+    pm = PeerMax(group) if eligible else None
+    _peer_max[key] = pm if pm is not None and pm.ok else None
+
+
 def all_reduce_max(t: torch.Tensor, group=None) -> None:
     """In-place max over the split's ranks (a per-tensor FP8 activation amax: the tensor is the whole
-    sequence, so every rank quantizes with the scale the unsplit step would use)."""
+    sequence, so every rank quantizes with the scale the unsplit step would use): through peer memory where
+    prepare_peer_max set that up for the group, else one NCCL all-reduce."""
     if dist.is_initialized():
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        pm = _peer_max.get(_group_key(group))
+        if pm is not None and t.is_cuda:
+            pm(t)
+        else:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
 
 
 def cfg_combine_split(x: torch.Tensor, t: torch.Tensor, out: torch.Tensor, cfg_scale: float, apg_scale: float,
