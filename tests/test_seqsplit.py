@@ -78,8 +78,13 @@ def _worker(rank, world, port, n_tok, window, outq):
         out2 = torch.randn(2, C, n_tok - 64, generator=g)
         t = torch.tensor([0.6])
         comb = ss.cfg_combine_split(x[..., sp.lat_start:sp.lat_end], t, out2[..., sp.lat_start:sp.lat_end], 5.0, 0.7)
+        # the FP8 amax max-reduction: without GPUs every rank agrees to keep the collective (no peer memory)
+        ss.prepare_peer_max(None)
+        amax = torch.tensor([float(3 * rank + 1)])
+        ss.all_reduce_max(amax)
         # numpy payloads travel by value (a shared-memory tensor could outlive its sender)
-        outq.put((rank, s0, s1, torch.stack(outs).numpy(), sp.lat_start, sp.lat_end, comb.numpy()))
+        outq.put((rank, s0, s1, torch.stack(outs).numpy(), sp.lat_start, sp.lat_end, comb.numpy(), amax.item(),
+                  ss._peer_max.get("default") is None))
     finally:
         dist.destroy_process_group()
 
@@ -110,6 +115,7 @@ def test_split_attention_and_cfg_match_unsplit(world, n_tok, window):
     ref = ss.cfg_combine_split(x, torch.tensor([0.6]), out2, 5.0, 0.7)
     comb = torch.cat([torch.from_numpy(r[6]) for r in res], dim=-1)
     assert torch.allclose(comb, ref, atol=1e-5, rtol=1e-4)
+    assert all(r[7] == 3 * (world - 1) + 1 and r[8] for r in res)
 
 
 def test_split_workspace_tables():
