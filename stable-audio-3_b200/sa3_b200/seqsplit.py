@@ -196,19 +196,33 @@ class PeerMax:
         _lib.check(rc, "sa3_peer_max")
 
 
-_peer_max = {}  # process group key -> PeerMax, or None where the group keeps the NCCL all-reduce
+# id(process group) -> (the group object, PeerMax or None where the group keeps the NCCL all-reduce). The entry
+# holds the group object and is used only while that very object is the group asked for, so a group destroyed
+# and created again (with other peers) never reaches mailboxes opened for the old one.
+_peer_max = {}
 
 
-def _group_key(group):
-    return "default" if group is None else id(group)
+def _resolve_group(group):
+    return group if group is not None else dist.distributed_c10d._get_default_group()
+
+
+def _peer_entry(group):
+    g = _resolve_group(group)
+    ent = _peer_max.get(id(g))
+    return ent if ent is not None and ent[0] is g else None
+
+
+def peer_max_active(group=None) -> bool:
+    """True when all_reduce_max of `group` goes through peer memory."""
+    ent = _peer_entry(group) if dist.is_initialized() else None
+    return ent is not None and ent[1] is not None
 
 
 def prepare_peer_max(group=None) -> None:
     """Collective (every rank of `group`, same point): set up the peer-memory max exchange when every rank runs on
     its own GPU of one host (distinct device UUIDs) and has opened every other rank's mailbox; otherwise the
     group keeps the NCCL all-reduce. SA3_PEER_MAX=0 in the environment keeps NCCL everywhere."""
-    key = _group_key(group)
-    if key in _peer_max or not dist.is_initialized():
+    if not dist.is_initialized() or _peer_entry(group) is not None:
         return
     import os
     import socket
@@ -221,7 +235,8 @@ def prepare_peer_max(group=None) -> None:
     dist.all_gather_object(who, me, group=group)
     eligible = all(w[2] for w in who) and len({w[0] for w in who}) == 1 and len({w[1] for w in who}) == world
     pm = PeerMax(group) if eligible else None
-    _peer_max[key] = pm if pm is not None and pm.ok else None
+    g = _resolve_group(group)
+    _peer_max[id(g)] = (g, pm if pm is not None and pm.ok else None)
 
 
 def all_reduce_max(t: torch.Tensor, group=None) -> None:
@@ -229,7 +244,8 @@ def all_reduce_max(t: torch.Tensor, group=None) -> None:
     sequence, so every rank quantizes with the scale the unsplit step would use): through peer memory where
     prepare_peer_max set that up for the group, else one NCCL all-reduce."""
     if dist.is_initialized():
-        pm = _peer_max.get(_group_key(group))
+        ent = _peer_entry(group)
+        pm = ent[1] if ent is not None else None
         if pm is not None and t.is_cuda:
             pm(t)
         else:

@@ -84,7 +84,7 @@ def _worker(rank, world, port, n_tok, window, outq):
         ss.all_reduce_max(amax)
         # numpy payloads travel by value (a shared-memory tensor could outlive its sender)
         outq.put((rank, s0, s1, torch.stack(outs).numpy(), sp.lat_start, sp.lat_end, comb.numpy(), amax.item(),
-                  ss._peer_max.get("default") is None))
+                  not ss.peer_max_active()))
     finally:
         dist.destroy_process_group()
 

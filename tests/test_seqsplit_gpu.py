@@ -72,7 +72,7 @@ def _worker(rank, world, port, mode, outq):
             net = eng.inner_split(torch.cat([xb, xb]), torch.cat([t, t]), sp, torch.cat([cond, torch.zeros_like(cond)]),
                                   torch.cat([gemb, gemb]), torch.cat([lb, lb]))
         torch.cuda.synchronize()
-        peer = ss._peer_max.get("default") is not None
+        peer = ss.peer_max_active()
         # by value: the sender exits right after
         outq.put((rank, a, b, v.cpu().numpy(), net.cpu().numpy(), peer))
     finally:
@@ -91,7 +91,7 @@ def _peer_worker(rank, world, port, outq):
                             timeout=datetime.timedelta(seconds=120))
     try:
         ss.prepare_peer_max(None)
-        pm = ss._peer_max.get("default")
+        used = ss.peer_max_active()
         vals = torch.rand(200, world, generator=torch.Generator().manual_seed(3)) * 100
         t = torch.zeros(1, device="cuda")
         bad = 0
@@ -130,7 +130,7 @@ def _peer_worker(rank, world, port, outq):
             e1.record()
             torch.cuda.synchronize()
             times[name] = e0.elapsed_time(e1) * 10.0  # us per exchange
-        outq.put((rank, pm is not None, bad, _lib.device_error(), times))
+        outq.put((rank, used, bad, _lib.device_error(), times))
     finally:
         dist.destroy_process_group()
 
