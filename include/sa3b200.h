@@ -188,6 +188,20 @@ int sa3_rmsnorm_modulate(const void* x, int x_dtype, void* out, int rows, int D,
                          const float* quant_amax, float* scale_out, float* amax_out, float* row_r,
                          void* stream);
 
+/* One launch for an FP8 (or bf16) norm of the fp16 stream: the AMAX pass and the WRITE pass of
+ * sa3_rmsnorm_modulate with row_r, joined by a grid-wide barrier. *amax accumulates max|y| as the AMAX
+ * pass does (start it at 0); out receives y (e4m3 scaled by 448 / max(*amax, 1e-12), or bf16) and
+ * *scale_out (if non-NULL) the dequantisation scale. row_r: fp32 [rows] scratch. barrier: two uint32
+ * (8-byte aligned), zero before the first call, left ready for the next; one stream at a time may use
+ * them. The single launch serves fp16 x with D = 1536 and at most two uniform modulation batches (or
+ * none); other calls issue the two passes. Either way the bytes equal the two passes'. Every block of
+ * the launch must be resident at once (the grid is capped at the kernel's occupancy); the barrier's
+ * wait gives up after about a second with device error site 95. */
+int sa3_rmsnorm_quant_fused(const void* x, int x_dtype, void* out, int rows, int D, long long ldx, long long ldo,
+                            const float* gamma, float eps, const float* mod, long long ld_mod, int scale_off,
+                            int shift_off, int rows_per_batch, const int* row_batch, int out_dtype, float* amax,
+                            float* scale_out, float* row_r, unsigned int* barrier, void* stream);
+
 /* Per-tensor dynamic FP8 quantisation: out = e4m3(x * r), r = 448/max(*amax,1e-12);
  * the dequantisation scale s = max(*amax,1e-12)/448 is stored to *scale_out when non-NULL. If amax_out is non-NULL, the
  * kernel only computes max|x| into it (no write). x is bf16. */

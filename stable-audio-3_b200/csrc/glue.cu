@@ -306,10 +306,8 @@ template <int NV, bool DB, bool XH>
 constexpr int norm_direct_blocks() { return (DB || NV > 12) ? 2 : 3; }
 
 template <int NV, bool DB, bool XH>
-__global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>()) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+__device__ __forceinline__ void norm_direct_body(const NormParams& p, int tab_batches, float* ntab) {
   using Raw = typename std::conditional<XH, uint2, float4>::type;  // the fp16 stream is kept packed until used
-  grid_dep_wait();
-  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = gridDim.x * (NORM_D_THREADS / 32);
   int li = blockIdx.x * (NORM_D_THREADS / 32) + warp;
@@ -422,6 +420,13 @@ __global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>
   if (p.mode == SA3_NORM_AMAX) block_amax_commit(amax, p.amax_out);
 }
 
+template <int NV, bool DB, bool XH>
+__global__ void __launch_bounds__(NORM_D_THREADS, norm_direct_blocks<NV, DB, XH>()) rmsnorm_direct_kernel(NormParams p, int tab_batches) {
+  grid_dep_wait();
+  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
+  norm_direct_body<NV, DB, XH>(p, tab_batches, ntab);
+}
+
 // WRITE pass from the per-row 1/rms that the AMAX pass stored (p.row_r): no row reductions are left, so
 // the pass is an elementwise stream over 8-element chunks with NORM_APPLY_INFLIGHT independent loads per
 // thread (the structure of quantize_e4m3_kernel), y = fmaf(x * r, a, shift) with the modulation
@@ -448,22 +453,25 @@ __device__ __forceinline__ void norm_apply_step(int& r, int& c, int dr, int dc, 
   }
 }
 
+// FUSED: row_r was written earlier in the same launch by other blocks, so it is read through L2 (__ldcg), not
+// through the read-only path.
+template <bool FUSED>
 __device__ __forceinline__ void norm_apply_load(const NormParams& p, NormApplyChunks& ch, int r, int c, int dr, int dc,
                                                 int cpr) {
 #pragma unroll
   for (int k = 0; k < NORM_APPLY_INFLIGHT; ++k) {
     if (r < p.rows) {
       ch.u[k] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + (long long)r * p.ldx + c * 8);
-      ch.rr[k] = __ldg(p.row_r + r);
+      ch.rr[k] = FUSED ? __ldcg(p.row_r + r) : __ldg(p.row_r + r);
     }
     norm_apply_step(r, c, dr, dc, cpr);
   }
 }
 
-__global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int tab_batches) {
+// FUSED: the table in ntab was built by the max|y| pass of the same launch, and the scale is read through L2.
+template <bool FUSED>
+__device__ __forceinline__ void norm_apply_body(const NormParams& p, int tab_batches, float* ntab) {
   constexpr int NF = NORM_APPLY_INFLIGHT;
-  grid_dep_wait();
-  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
   const int cpr = p.D / 8;  // 8-element chunks per row
   const long long total = (long long)p.rows * cpr;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -471,8 +479,8 @@ __global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int ta
   long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   int r0 = (int)(i0 / cpr), c0 = (int)(i0 % cpr);
   NormApplyChunks ch;
-  norm_apply_load(p, ch, r0, c0, dr, dc, cpr);
-  {
+  norm_apply_load<FUSED>(p, ch, r0, c0, dr, dc, cpr);
+  if (!FUSED) {
     const int D4 = p.D >> 2, n4 = tab_batches * D4;
     for (int idx = threadIdx.x; idx < n4; idx += blockDim.x) {
       const int b = idx / D4, e = 4 * (idx - b * D4);
@@ -490,11 +498,17 @@ __global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int ta
       *reinterpret_cast<float4*>(ntab + (2 * b + 1) * p.D + e) = ts;
     }
   }
-  __syncthreads();
+  if (!FUSED) __syncthreads();
   float s = 1.f;
   if (p.out_dtype == SA3_DT_E4M3) {
-    s = quant_inv_scale(p.quant_amax);
-    if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
+    if (FUSED) {
+      const float am = fmaxf(__ldcg(p.quant_amax), 1e-12f);  // quant_inv_scale / quant_scale on the L2 value
+      s = kE4M3Max / am;
+      if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = am / kE4M3Max;
+    } else {
+      s = quant_inv_scale(p.quant_amax);
+      if (p.scale_out && blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = quant_scale(p.quant_amax);
+    }
   }
   while (i0 < total) {
     int r = r0, c = c0;
@@ -533,8 +547,62 @@ __global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int ta
     r0 = r;
     c0 = c;
     i0 += NF * stride;
-    if (i0 < total) norm_apply_load(p, ch, r0, c0, dr, dc, cpr);
+    if (i0 < total) norm_apply_load<FUSED>(p, ch, r0, c0, dr, dc, cpr);
   }
+}
+
+__global__ void __launch_bounds__(256, 3) norm_apply_kernel(NormParams p, int tab_batches) {
+  grid_dep_wait();
+  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
+  norm_apply_body<false>(p, tab_batches, ntab);
+}
+
+// Grid-wide barrier with sense reversal: bar[0] counts arrivals, bar[1] is the generation. A block reads the
+// generation, then arrives; the last block to arrive resets the count and advances the generation, the others
+// wait (bounded by SA3_WAIT_BUDGET_CYCLES, then device error site 95) for it to change. Every block of the grid
+// must be resident at once (the host caps the grid at the kernel's occupancy).
+__device__ __forceinline__ void norm_grid_barrier(unsigned int* bar) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int gen;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
+    __threadfence();
+    if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+      bar[0] = 0u;
+      __threadfence();
+      atomicAdd(bar + 1, 1u);
+    } else {
+      const long long t0 = clock64();
+      while (true) {
+        unsigned int g;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+        if (g != gen) break;
+        if (clock64() - t0 > SA3_WAIT_BUDGET_CYCLES) {
+          record_error(SA3_DEVERR_TIMEOUT, 95);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+// One launch per norm of the fp16 stream: the max|y| pass (direct kernel body: 1/rms of every row into row_r,
+// max|y| into amax_out), a grid barrier, then the elementwise e4m3 / bf16 write pass from row_r with the scale of
+// the now complete max. Same operations as the two launches, so the same bytes.
+template <int NV>
+__global__ void __launch_bounds__(NORM_D_THREADS, 2) norm_fused_kernel(NormParams p, int tab_batches, unsigned int* bar) {
+  grid_dep_wait();
+  extern __shared__ __align__(16) float ntab[];  // [tab_batches][2][D]
+  NormParams pa = p;
+  pa.mode = SA3_NORM_AMAX;
+  norm_direct_body<NV, true, true>(pa, tab_batches, ntab);
+  norm_grid_barrier(bar);
+  NormParams pw = p;
+  pw.mode = SA3_NORM_WRITE;
+  norm_apply_body<true>(pw, tab_batches, ntab);
 }
 
 // Bulk-copy variant: warp 4 (lane 0) streams whole rows into an NORM_RING-deep shared-memory ring
@@ -1105,3 +1173,72 @@ extern "C" int sa3_convert(const void* x, int x_dtype, void* out, int out_dtype,
   launch_ex(convert_kernel, dim3(grid_for((long long)rows * (cols / 8), 256)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, p);
   return launch_status();
 }
+
+extern "C" int sa3_rmsnorm_quant_fused(const void* x, int x_dtype, void* out, int rows, int D, long long ldx,
+                                       long long ldo, const float* gamma, float eps, const float* mod, long long ld_mod,
+                                       int scale_off, int shift_off, int rows_per_batch, const int* row_batch,
+                                       int out_dtype, float* amax, float* scale_out, float* row_r, unsigned int* barrier,
+                                       void* stream) {
+  if (!x || !out || !amax || !row_r || !barrier || rows <= 0 || D <= 0) return SA3_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(barrier) & 7) return SA3_ERR_ALIGN;
+  const bool vec = aligned16(gamma) && (!mod || (aligned16(mod) && ld_mod % 4 == 0 && scale_off % 4 == 0 &&
+                                                  shift_off % 4 == 0));
+  int tab_batches = 1;
+  if (mod) tab_batches = (!row_batch && rows_per_batch > 0 && (rows + rows_per_batch - 1) / rows_per_batch <= 2)
+                             ? (rows + rows_per_batch - 1) / rows_per_batch
+                             : 0;
+  const bool out_ok = out_dtype == SA3_DT_E4M3 ? ((reinterpret_cast<uintptr_t>(out) & 7) == 0 && ldo % 8 == 0 && ldo >= D)
+                                               : (out_dtype == SA3_DT_BF16 && aligned16(out) && ldo % 8 == 0 && ldo >= D);
+  const bool fused = x_dtype == SA3_DT_F16 && D == 1536 && vec && tab_batches >= 1 && aligned16(x) && ldx % 8 == 0 &&
+                     ldx >= D && out_ok;
+  if (!fused) {
+    // the two launches: max|y| (storing 1/rms per row), then the write pass
+    int rc = sa3_rmsnorm_modulate(x, x_dtype, nullptr, rows, D, ldx, 0, gamma, eps, mod, ld_mod, scale_off, shift_off,
+                                  rows_per_batch, row_batch, SA3_NORM_AMAX, out_dtype, nullptr, nullptr, amax, row_r,
+                                  stream);
+    if (rc) return rc;
+    return sa3_rmsnorm_modulate(x, x_dtype, out, rows, D, ldx, ldo, gamma, eps, mod, ld_mod, scale_off, shift_off,
+                                rows_per_batch, row_batch, SA3_NORM_WRITE, out_dtype, amax, scale_out, nullptr, row_r,
+                                stream);
+  }
+  NormParams p;
+  p.x = x;
+  p.x_f32 = 0;
+  p.x_f16 = 1;
+  p.out = out;
+  p.rows = rows;
+  p.D = D;
+  p.ldx = ldx;
+  p.ldo = ldo;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.mod = mod;
+  p.ld_mod = ld_mod;
+  p.scale_off = scale_off;
+  p.shift_off = shift_off;
+  p.rows_per_batch = rows_per_batch;
+  p.row_batch = nullptr;
+  p.mode = SA3_NORM_WRITE;
+  p.out_dtype = out_dtype;
+  p.quant_amax = amax;
+  p.scale_out = scale_out;
+  p.amax_out = amax;
+  p.row_r = row_r;
+  const int smem = tab_batches * 2 * D * 4;
+  int rc;
+  if ((rc = ensure_smem(norm_fused_kernel<12>, 2 * 2 * 2048 * 4))) return rc;
+  // every block of the grid must be resident at once for the barrier: at most the kernel's occupancy
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, norm_fused_kernel<12>, NORM_D_THREADS, smem) !=
+          cudaSuccess ||
+      per_sm <= 0 || sms <= 0)
+    return SA3_ERR_LAUNCH;
+  int grid = (rows + 7) / 8;
+  if (grid > per_sm * sms) grid = per_sm * sms;
+  launch_ex(norm_fused_kernel<12>, dim3(grid), dim3(NORM_D_THREADS), smem, reinterpret_cast<cudaStream_t>(stream), 1, p,
+            tab_batches, barrier);
+  return launch_status();
+}
+

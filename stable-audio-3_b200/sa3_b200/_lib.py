@@ -74,6 +74,8 @@ SIGNATURES = {
     "sa3_permute_cols": [c_vp, c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp],
     "sa3_rmsnorm_modulate": [c_vp, c_int, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int,
                              c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "sa3_rmsnorm_quant_fused": [c_vp, c_int, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_float, c_vp, c_ll, c_int, c_int,
+                                c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp],
     "sa3_convert": [c_vp, c_int, c_vp, c_int, c_int, c_int, c_ll, c_ll, c_vp, c_vp],
     "sa3_quantize_e4m3": [c_vp, c_vp, c_int, c_int, c_ll, c_ll, c_vp, c_vp, c_vp, c_vp],
     "sa3_qk_norm_rope": [c_vp, c_int, c_ll, c_int, c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_vp),

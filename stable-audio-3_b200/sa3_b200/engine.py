@@ -28,6 +28,7 @@ reference's bf16 path rounds it first); the CFG / APG combine runs in fp32.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -47,6 +48,10 @@ QUANT_SUFFIXES = ("self_attn.to_qkv", "self_attn.to_out", "cross_attn.to_q", "cr
 # Byte budget of the batched first local-conditioning layer's output (every block's SiLU(W1 c + b1) for all
 # latent rows); larger packed batches compute it block by block.
 _LOCAL_ALL_MAX_BYTES = 4 << 30
+
+# FP8 norms outside a sequence split run both passes as one launch (grid barrier); SA3_NORM_FUSED=0 in the
+# environment selects the two launches (the same bytes)
+_NORM_ONE_LAUNCH = os.environ.get("SA3_NORM_FUSED", "1") != "0"
 
 # GPTQ linears with at least this many input rows dequantise their weight once per call (bf16, N x K, into one
 # buffer shared by all layers) and run the bf16 GEMM; fewer rows run the kernel that dequantises each weight
@@ -170,8 +175,10 @@ class _Workspace:
         bf = torch.bfloat16
         self.h = torch.empty(M, D, device=dev, dtype=stream_dtype)  # residual stream (fp16 or fp32)
         self.a = torch.empty(M, D, device=dev, dtype=torch.float8_e4m3fn if fp8 else bf)
-        # 1/rms of each stream row, stored by a norm's max|y| pass and read by its write pass
+        # 1/rms of each stream row, stored by a norm's max|y| pass and read by its write pass; the grid barrier of
+        # the one-launch norm (arrival count, generation)
         self.row_r = torch.empty(M, device=dev, dtype=torch.float32) if fp8 else None
+        self.norm_barrier = torch.zeros(2, device=dev, dtype=torch.int32) if fp8 else None
         self.qkv = torch.empty(M, nq * D, device=dev, dtype=bf)
         if split is not None:
             # per sequence [left halo | own rows | right halo] of the q|k|v|q'|k' projection
@@ -383,6 +390,11 @@ class DiTEngine:
             am = ws.amax[slot:slot + 1]
             sc = ws.scale[slot:slot + 1]
             rr = ws.row_r[:rows]
+            if _NORM_ONE_LAUNCH and (ws.split is None or ws.split.world == 1):
+                # both passes in one launch where the kernel serves the shape
+                ops.rmsnorm_quant_fused(x, gamma, cfg.norm_eps, out=a, amax=am, row_r=rr, barrier=ws.norm_barrier,
+                                        scale_out=sc, **kw)
+                return a, sc
             ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, amax_only=am, row_r=rr, **kw)
             self._sync_amax(ws, slot)
             ops.rmsnorm_modulate(x, gamma, cfg.norm_eps, out=a, quant_amax=am, scale_out=sc, row_r=rr, **kw)

@@ -212,8 +212,12 @@ def case(name: str, iters: int) -> dict:
         ms_write = _time(lambda: ops.rmsnorm_modulate(x, gam, 1e-5, mod=mod, scale_off=0, shift_off=D,  # noqa: E731
                                                       rows_per_batch=N, out=out, quant_amax=am, scale_out=sc,
                                                       row_r=rr), iters)
+        bar = torch.zeros(2, device=dev, dtype=torch.int32)
+        ms_fused = _time(lambda: ops.rmsnorm_quant_fused(x, gam, 1e-5, out=out, amax=am, row_r=rr,  # noqa: E731
+                                                         barrier=bar, scale_out=sc, mod=mod, scale_off=0,
+                                                         shift_off=D, rows_per_batch=N), iters)
         return {"case": name, "ms": ms, "GBps": (2 * M * D * x.element_size() + M * D) / ms / 1e6,
-                "ms_amax_pass": ms_amax, "ms_write_pass": ms_write}
+                "ms_amax_pass": ms_amax, "ms_write_pass": ms_write, "ms_one_launch": ms_fused}
     if name in ("quant_attn", "quant_ff"):
         # activation quantisation with the scale from a producer's max|x|: M x 1536 (attention output) and
         # M x 6144 (FF hidden)

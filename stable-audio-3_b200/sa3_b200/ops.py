@@ -171,6 +171,28 @@ def rmsnorm_modulate(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float,
     return out
 
 
+def rmsnorm_quant_fused(x: torch.Tensor, gamma: Optional[torch.Tensor], eps: float, *, out: torch.Tensor,
+                        amax: torch.Tensor, row_r: torch.Tensor, barrier: torch.Tensor, scale_out=None, mod=None,
+                        scale_off: int = 0, shift_off: int = 0, rows_per_batch: int = 0, row_batch=None) -> torch.Tensor:
+    """The two norm passes (max|y| into `amax`, then `out` quantised with it) as one launch where the kernel
+    serves the shape (fp16 stream, D = 1536, <= 2 uniform batches), else as the two passes; same bytes either
+    way. `barrier`: an int32 CUDA tensor of 2 zeros kept for the stream's later calls."""
+    _need_cuda(x, gamma, mod, row_batch, out, amax, row_r, barrier, scale_out)
+    rows, D = x.shape
+    if row_r.dtype != torch.float32 or row_r.numel() < rows or not row_r.is_contiguous():
+        raise RuntimeError("row_r must be a contiguous fp32 tensor of at least `rows` elements")
+    if barrier.dtype != torch.int32 or barrier.numel() < 2 or not barrier.is_contiguous():
+        raise RuntimeError("barrier must be a contiguous int32 tensor of 2 elements")
+    _count()
+    rc = _lib.load().sa3_rmsnorm_quant_fused(x.data_ptr(), _dt(x), out.data_ptr(), rows, D, _row_stride(x),
+                                             _row_stride(out), _ptr(gamma), eps, _ptr(mod),
+                                             _row_stride(mod) if mod is not None else 0, scale_off, shift_off,
+                                             rows_per_batch, _ptr(row_batch), _dt(out), amax.data_ptr(),
+                                             _ptr(scale_out), row_r.data_ptr(), barrier.data_ptr(), _stream())
+    _lib.check(rc, "sa3_rmsnorm_quant_fused")
+    return out
+
+
 def quantize_e4m3(x: torch.Tensor, amax: torch.Tensor, out=None, scale_out=None) -> torch.Tensor:
     _need_cuda(x, amax, out, scale_out)
     rows, cols = x.shape

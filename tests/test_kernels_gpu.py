@@ -438,6 +438,18 @@ def test_rmsnorm_modulate_fp32_stream(cuda, layout, stream):
     assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8))
     assert torch.equal(out2, out)
     assert bool(torch.isfinite(rr).all())
+    # both passes as one launch (grid barrier) where the kernel serves the shape, else the two passes: same
+    # bytes, twice in a row on the same barrier words
+    bar = torch.zeros(2, device=cuda, dtype=torch.int32)
+    for _ in range(2):
+        amax3, s3 = torch.zeros(1, device=cuda), torch.zeros(1, device=cuda)
+        q3 = torch.empty_like(q)
+        ops.rmsnorm_quant_fused(xd, gd, 1e-5, out=q3, amax=amax3, row_r=torch.empty(M, device=cuda), barrier=bar,
+                                scale_out=s3, **kw)
+        torch.cuda.synchronize()
+        assert amax3.item() == amax.item() and s3.item() == s.item()
+        assert torch.equal(q3.view(torch.uint8), q.view(torch.uint8))
+    assert bar[0].item() == 0
 
 
 def test_qk_norm_rope(cuda):
